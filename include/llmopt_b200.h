@@ -1,0 +1,209 @@
+/*
+ * llmopt_b200.h - C ABI of the B200-native paged-KV hot path.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * plus the CUDA stream to launch on.  Nothing here allocates device memory:
+ * split-K scratch ("workspace") is passed in by the caller, sized with
+ * llmopt_paged_attention_workspace_size().  Functions never throw; they return
+ * an llmopt_status and leave a human-readable message in llmopt_last_error()
+ * (thread-local).  Kernels that find a bad index at run time (a block id
+ * outside the pool, a context longer than its block-table row) skip the
+ * access and OR a LLMOPT_DEVERR_* bit into the optional device word `err`.
+ *
+ * Cache layout (identical to the reference's PagedKVCache storage,
+ * src/llmopt/cache/paged_cache.py:171-173): key_cache and value_cache are
+ * contiguous [num_layers, num_blocks, block_size, num_kv_heads, head_dim].
+ * Block tables are [batch, table_width] (int32 or int64, row stride
+ * table_stride elements, -1 padded); context_lens / token_offsets are [batch]
+ * (int32 or int64).
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   llmopt_paged_attention  <- PagedAttention.forward
+ *                              src/llmopt/attention/paged_attention.py:146-187
+ *   llmopt_merge_states     <- merge_states  paged_attention.py:30-55
+ *   llmopt_kv_write         <- PagedKVCache.write  src/llmopt/cache/paged_cache.py:175-232
+ *   llmopt_kv_write_decode  <- PagedKVCache.write_decode  paged_cache.py:234-261
+ *   llmopt_paged_gather     <- PagedKVCache.gather  paged_cache.py:263-312
+ */
+#ifndef LLMOPT_B200_H_
+#define LLMOPT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LLMOPT_API __attribute__((visibility("default")))
+#else
+#define LLMOPT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LLMOPT_B200_ABI_VERSION 1
+
+/* Element types (torch.float32 / float16 / bfloat16). */
+enum {
+  LLMOPT_DTYPE_F32 = 0,
+  LLMOPT_DTYPE_F16 = 1,
+  LLMOPT_DTYPE_BF16 = 2
+};
+
+/* Return codes. The Python layer maps them to the reference's exception types. */
+enum {
+  LLMOPT_OK = 0,
+  LLMOPT_ERR_INVALID_ARGUMENT = 1, /* ValueError */
+  LLMOPT_ERR_UNSUPPORTED = 2,      /* ValueError: dtype/shape not supported   */
+  LLMOPT_ERR_WORKSPACE = 3,        /* RuntimeError: workspace too small        */
+  LLMOPT_ERR_CUDA = 4,             /* RuntimeError: CUDA launch/driver error   */
+  LLMOPT_ERR_INDEX = 5             /* IndexError                               */
+};
+
+/* Bits a kernel ORs into the optional `err` word (uint32 in device memory). */
+#define LLMOPT_DEVERR_BLOCK_ID 1u      /* block id >= num_blocks (access skipped)     */
+#define LLMOPT_DEVERR_TABLE_WIDTH 2u   /* position beyond the block-table row         */
+#define LLMOPT_DEVERR_WAIT_TIMEOUT 4u  /* a bounded on-device wait gave up            */
+
+/* split_tokens argument of the attention entry points. */
+#define LLMOPT_SPLIT_AUTO 0LL  /* balanced split-K chosen from context and SM count */
+#define LLMOPT_SPLIT_NONE (-1LL) /* one split per sequence (split_kv=False)        */
+/* split_tokens > 0: each sequence cut into chunks of at most split_tokens
+ * tokens, rounded up to whole blocks (PagedAttentionConfig.split_size). */
+
+/* Library identification; callable without a GPU. */
+LLMOPT_API const char* llmopt_b200_version(void);
+LLMOPT_API int llmopt_b200_abi_version(void);
+LLMOPT_API const char* llmopt_status_string(int status);
+/* Message of the last failing call on this thread ("" if none). */
+LLMOPT_API const char* llmopt_last_error(void);
+
+/*
+ * Bytes of split-K workspace llmopt_paged_attention needs for these shapes on
+ * `device` (the CUDA ordinal).  Pass the same arguments as the call.
+ */
+LLMOPT_API int llmopt_paged_attention_workspace_size(int device, int64_t batch, int32_t num_heads,
+                                          int32_t num_kv_heads, int32_t head_dim, int32_t q_len,
+                                          int32_t block_size, int64_t table_width,
+                                          int32_t kv_dtype, int64_t split_tokens,
+                                          size_t* bytes);
+
+/*
+ * Paged attention over the block-addressed cache: decode (q_len == 1) and
+ * chunked prefill (q_len > 1, causal within the chunk, full over the prefix:
+ * query i of sequence s sits at position context_lens[s] - q_len + i).
+ * Replaces PagedAttention.forward (paged_attention.py:146-187).
+ *
+ *   query  [batch, num_heads, q_len, head_dim], element strides (q_s, q_h, q_t),
+ *          head_dim contiguous; rounded to the cache dtype before the dot
+ *          products, as the reference's q.to(k.dtype).
+ *   out    same shape, element strides (o_s, o_h, o_t), dtype out_dtype.
+ *   lse    optional fp32 [batch, num_heads, q_len] contiguous: natural-log
+ *          sum-exp of the masked, scaled (and soft-capped) scores; -inf for a
+ *          fully masked row (whose output is 0, as the reference's nan_to_num).
+ *   softcap > 0 applies tanh(s / softcap) * softcap after scaling.
+ *   Query head h reads KV head h / (num_heads / num_kv_heads).
+ */
+LLMOPT_API int llmopt_paged_attention(const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h,
+                           int64_t q_t,
+                           const void* key_cache, const void* value_cache, int32_t kv_dtype,
+                           int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                           int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                           const void* block_table, int32_t table_is_i64, int64_t table_width,
+                           int64_t table_stride,
+                           const void* context_lens, int32_t ctx_is_i64,
+                           void* out, int32_t out_dtype, int64_t o_s, int64_t o_h, int64_t o_t,
+                           float* lse,
+                           int64_t batch, int32_t num_heads, int32_t q_len, float scale,
+                           float softcap, int64_t split_tokens,
+                           void* workspace, size_t workspace_bytes, uint32_t* err,
+                           void* stream);
+
+/*
+ * The two halves of llmopt_paged_attention, for callers that time or schedule
+ * them separately: LLMOPT_PHASE_SPLIT runs the split-K attention kernel (its
+ * partial states go to the workspace), LLMOPT_PHASE_COMBINE merges them into
+ * out / lse.  Issue SPLIT then COMBINE on one stream with identical arguments
+ * and workspace; LLMOPT_PHASE_ALL is llmopt_paged_attention itself.
+ */
+#define LLMOPT_PHASE_SPLIT 1
+#define LLMOPT_PHASE_COMBINE 2
+#define LLMOPT_PHASE_ALL 3
+LLMOPT_API int llmopt_paged_attention_phase(const void* query, int32_t q_dtype, int64_t q_s,
+                           int64_t q_h, int64_t q_t,
+                           const void* key_cache, const void* value_cache, int32_t kv_dtype,
+                           int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                           int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                           const void* block_table, int32_t table_is_i64, int64_t table_width,
+                           int64_t table_stride,
+                           const void* context_lens, int32_t ctx_is_i64,
+                           void* out, int32_t out_dtype, int64_t o_s, int64_t o_h, int64_t o_t,
+                           float* lse,
+                           int64_t batch, int32_t num_heads, int32_t q_len, float scale,
+                           float softcap, int64_t split_tokens,
+                           void* workspace, size_t workspace_bytes, uint32_t* err,
+                           void* stream, int32_t phases);
+
+/*
+ * Exact log-sum-exp merge of two partial attention states.  Replaces
+ * merge_states (paged_attention.py:30-55).  o1/o2/out are contiguous
+ * [rows, head_dim] of o_dtype; l1/l2/lse_out contiguous [rows] of lse_dtype.
+ * Same IEEE behaviour as torch.logaddexp (two -inf inputs give NaN outputs).
+ */
+LLMOPT_API int llmopt_merge_states(const void* o1, const void* o2, const void* l1, const void* l2,
+                        void* out, void* lse_out, int64_t rows, int32_t head_dim,
+                        int32_t o_dtype, int32_t lse_dtype, void* stream);
+
+/*
+ * Chunked-prefill KV append.  Replaces PagedKVCache.write + _write_one
+ * (paged_cache.py:175-232): for each sequence, rows keys[s, i] land at
+ * position token_offsets[s] + i; the walk stops at the first -1 table entry or
+ * the end of the row.  keys/values [batch, q_len, num_kv_heads, head_dim]
+ * with element strides (seq, token, head), head_dim contiguous, cast to the
+ * cache dtype with round-to-nearest-even.
+ */
+LLMOPT_API int llmopt_kv_write(const void* keys, const void* values, int32_t in_dtype,
+                    int64_t k_s, int64_t k_t, int64_t k_h, int64_t v_s, int64_t v_t, int64_t v_h,
+                    void* key_cache, void* value_cache, int32_t kv_dtype,
+                    int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                    const void* block_table, int32_t table_is_i64, int64_t table_width,
+                    int64_t table_stride, const void* token_offsets, int32_t off_is_i64,
+                    int64_t batch, int32_t q_len, uint32_t* err, void* stream);
+
+/*
+ * Single-token decode append.  Replaces PagedKVCache.write_decode
+ * (paged_cache.py:234-261): row s lands in table column floor(off/bs) (a
+ * negative column wraps, as torch indexing does) at slot off mod bs; a block
+ * id < 0 or >= num_blocks is written to block 0, which is the reference's
+ * behaviour.  keys/values [batch, num_kv_heads, head_dim], strides (seq, head).
+ */
+LLMOPT_API int llmopt_kv_write_decode(const void* keys, const void* values, int32_t in_dtype,
+                           int64_t k_s, int64_t k_h, int64_t v_s, int64_t v_h,
+                           void* key_cache, void* value_cache, int32_t kv_dtype,
+                           int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                           int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                           const void* block_table, int32_t table_is_i64, int64_t table_width,
+                           int64_t table_stride, const void* token_offsets, int32_t off_is_i64,
+                           int64_t batch, uint32_t* err, void* stream);
+
+/*
+ * Padded gather of a batch's KV.  Replaces PagedKVCache.gather
+ * (paged_cache.py:263-312).  out_keys/out_values contiguous
+ * [batch, max_len, num_kv_heads, head_dim] in the cache dtype (zero where
+ * invalid); valid contiguous [batch, max_len] uint8.  max_len must not exceed
+ * table_width * block_size (the reference raises IndexError there).
+ */
+LLMOPT_API int llmopt_paged_gather(const void* key_cache, const void* value_cache, int32_t kv_dtype,
+                        int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                        int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                        const void* block_table, int32_t table_is_i64, int64_t table_width,
+                        int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
+                        int64_t batch, int64_t max_len, void* out_keys, void* out_values,
+                        uint8_t* valid, uint32_t* err, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* LLMOPT_B200_H_ */

@@ -1,0 +1,400 @@
+"""CPU oracle for llmopt's paged-KV hot path.  TEST INFRASTRUCTURE ONLY.
+
+This module is the checker, never the product.  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference leg may
+import it.  The product path (the CUDA library behind
+``quantized-llm-inference-engine-_b200``) never calls into it and has no CPU
+fallback.
+
+It restates, in numpy, the algorithm of the reference's pure-PyTorch path so
+that the CUDA kernels can be compared against it on identical inputs:
+
+* ``PagedKVCache.gather``      src/llmopt/cache/paged_cache.py:263-312
+* ``PagedKVCache.write``       src/llmopt/cache/paged_cache.py:175-232
+* ``PagedKVCache.write_decode`` src/llmopt/cache/paged_cache.py:234-261
+* ``PagedAttention.forward``   src/llmopt/attention/paged_attention.py:146-187
+  (``_expand_kv`` :189-210, ``_build_mask`` :212-229, ``_forward_dense``
+  :231-250, ``_forward_split`` :252-293)
+* ``merge_states``             src/llmopt/attention/paged_attention.py:30-55
+
+Parity of this restatement is pinned against golden vectors produced by the
+reference implementation itself (``tests/golden/make_golden.py`` imports the
+reference, runs it on seeded inputs and commits the outputs); the CPU test
+``tests/test_oracle_golden.py`` checks every function here against them.
+
+Storage conventions.  A cache or activation tensor is a numpy array plus a
+"kind": ``"f32"`` (float32 array), ``"f16"`` (float16 array) or ``"bf16"``
+(uint16 array holding bfloat16 bit patterns, since numpy has no bfloat16).
+Attention arithmetic runs in ``acc`` precision (float64 by default, the
+checker's "truth"; float32 when timing the baseline) on values upcast from
+the stored kind, which is the recipe "reference path with the cache upcast to
+fp32" - the reference itself does its matmuls in the cache dtype
+(paged_attention.py:242), which for bf16 only adds rounding noise.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+__all__ = [
+    "KINDS",
+    "OracleConfig",
+    "bf16_bits_to_f32",
+    "f32_to_bf16_bits",
+    "to_f32",
+    "from_f32",
+    "convert",
+    "gather",
+    "write",
+    "write_decode",
+    "merge_states",
+    "paged_attention",
+    "attention_lse",
+    "decode_bytes",
+    "prefill_flops",
+]
+
+KINDS = ("f32", "f16", "bf16")
+
+
+# ---------------------------------------------------------------------------
+# dtype helpers: torch-CPU-compatible rounding for the ``.to(dtype)`` casts in
+# paged_cache.py:223-228 and :260-261.
+# ---------------------------------------------------------------------------
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    """Widen bfloat16 bit patterns (uint16) to float32 exactly."""
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round float32 to bfloat16 with round-to-nearest-even.
+
+    Finite values and infinities round exactly as torch's CPU ``.to(bfloat16)``
+    does (add ``0x7FFF`` plus the kept LSB, truncate).  NaN maps to a quiet NaN
+    (0x7FC0); torch's CPU kernels do not agree among themselves on the NaN
+    payload, so tests compare NaNs as "is NaN" only.
+    """
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    lsb = (u >> np.uint64(16)) & np.uint64(1)
+    rounded = ((u + np.uint64(0x7FFF) + lsb) >> np.uint64(16)) & np.uint64(0xFFFF)
+    out = rounded.astype(np.uint16)
+    out[np.isnan(x)] = np.uint16(0x7FC0)
+    return out
+
+
+def to_f32(arr: np.ndarray, kind: str) -> np.ndarray:
+    """Exact widening of a stored tensor to float32."""
+    if kind == "bf16":
+        return bf16_bits_to_f32(arr)
+    if kind == "f16":
+        return np.asarray(arr, dtype=np.float16).astype(np.float32)
+    if kind == "f32":
+        return np.asarray(arr, dtype=np.float32)
+    raise ValueError(f"unknown kind {kind!r}")
+
+
+def from_f32(x: np.ndarray, kind: str) -> np.ndarray:
+    """Round float32 values to ``kind`` storage (RNE, as torch's CPU cast)."""
+    if kind == "bf16":
+        return f32_to_bf16_bits(x)
+    if kind == "f16":
+        with np.errstate(over="ignore"):
+            return np.asarray(x, dtype=np.float32).astype(np.float16)
+    if kind == "f32":
+        return np.asarray(x, dtype=np.float32).copy()
+    raise ValueError(f"unknown kind {kind!r}")
+
+
+def convert(arr: np.ndarray, src: str, dst: str) -> np.ndarray:
+    """``tensor.to(dst)`` for a ``src``-kind tensor (through float32, as torch)."""
+    if src == dst:
+        return np.array(arr, copy=True)
+    return from_f32(to_f32(arr, src), dst)
+
+
+# ---------------------------------------------------------------------------
+# KV cache: gather / write / write_decode
+# ---------------------------------------------------------------------------
+
+def gather(key_cache: np.ndarray, value_cache: np.ndarray, layer: int,
+           block_ids: np.ndarray, context_lens: np.ndarray):
+    """Restates ``PagedKVCache.gather`` (paged_cache.py:263-312).
+
+    ``key_cache``/``value_cache`` are ``[L, num_blocks, block_size, kv_heads,
+    head_dim]`` stored arrays (any kind).  Returns padded ``keys``, ``values``
+    (same storage kind, ``[B, max_len, kv_heads, head_dim]``) and the bool
+    ``valid`` mask ``[B, max_len]``.  Out-of-range table columns or block ids
+    raise ``IndexError`` exactly where the reference's indexing would.
+    """
+    block_ids = np.asarray(block_ids).astype(np.int64)
+    context_lens = np.asarray(context_lens).astype(np.int64)
+    B = block_ids.shape[0]
+    _, num_blocks, block_size, kvh, d = key_cache.shape
+    max_len = int(context_lens.max()) if B else 0
+    if max_len <= 0:
+        empty = np.zeros((B, 0, kvh, d), dtype=key_cache.dtype)
+        return empty, empty.copy(), np.zeros((B, 0), dtype=bool)
+    pos = np.arange(max_len)
+    col = pos // block_size                      # paged_cache.py:289
+    slot = pos % block_size                      # paged_cache.py:290
+    if col.max() >= block_ids.shape[1]:
+        raise IndexError("context exceeds the block table width")
+    ids = block_ids[:, col]                      # paged_cache.py:292
+    valid = ids >= 0                             # paged_cache.py:293
+    safe = np.where(valid, ids, 0)               # paged_cache.py:294
+    valid &= pos[None, :] < context_lens[:, None]  # paged_cache.py:295
+    if safe.max(initial=0) >= num_blocks:
+        raise IndexError("block id out of range")
+    k = key_cache[layer][safe, slot[None, :]]     # [B, max_len, kvh, d]
+    v = value_cache[layer][safe, slot[None, :]]
+    zero = np.zeros((), dtype=key_cache.dtype)
+    m = valid[:, :, None, None]
+    return np.where(m, k, zero), np.where(m, v, zero), valid
+
+
+def _block_at(blocks: np.ndarray, index: int) -> int:
+    """``int(blocks[index].item())`` with torch's negative-index wrap."""
+    n = blocks.shape[0]
+    if index < -n or index >= n:
+        raise IndexError(f"block table index {index} out of range")
+    return int(blocks[index])
+
+
+def write(key_cache: np.ndarray, value_cache: np.ndarray, kind: str, layer: int,
+          block_ids: np.ndarray, token_offsets: np.ndarray,
+          keys: np.ndarray, values: np.ndarray, in_kind: str) -> None:
+    """Restates ``PagedKVCache.write`` + ``_write_one`` (paged_cache.py:175-232).
+
+    Per sequence, rows are written block by block starting at
+    ``token_offsets[s]``; the walk stops at the end of the table row or at the
+    first ``-1`` entry (:216-219).  Values are cast to the cache kind (:223-228).
+    Mutates the caches in place.
+    """
+    B, q_len = keys.shape[0], keys.shape[1]
+    if q_len == 0 or B == 0:                      # paged_cache.py:197-198
+        return
+    block_ids = np.asarray(block_ids).astype(np.int64)
+    bs = key_cache.shape[2]
+    num_blocks = key_cache.shape[1]
+    for s in range(B):                            # paged_cache.py:199-201
+        start = int(token_offsets[s])
+        blocks = block_ids[s]
+        written = 0
+        cursor = start
+        block_index = start // bs                 # paged_cache.py:215
+        while written < q_len and block_index < blocks.shape[0]:
+            block = _block_at(blocks, block_index)
+            if block < 0:                         # paged_cache.py:218-219
+                break
+            if block >= num_blocks:
+                raise IndexError(f"block id {block} out of range")
+            lo = cursor % bs
+            take = min(bs - lo, q_len - written)  # paged_cache.py:220-221
+            key_cache[layer, block, lo:lo + take] = convert(keys[s, written:written + take], in_kind, kind)
+            value_cache[layer, block, lo:lo + take] = convert(values[s, written:written + take], in_kind, kind)
+            written += take
+            cursor += take
+            if cursor % bs == 0:                  # paged_cache.py:231-232
+                block_index += 1
+
+
+def write_decode(key_cache: np.ndarray, value_cache: np.ndarray, kind: str, layer: int,
+                 block_ids: np.ndarray, token_offsets: np.ndarray,
+                 keys: np.ndarray, values: np.ndarray, in_kind: str) -> None:
+    """Restates ``PagedKVCache.write_decode`` (paged_cache.py:234-261).
+
+    ``keys``/``values`` are ``[B, kv_heads, head_dim]``.  Block index is the
+    floor division of the offset, slot the (non-negative) remainder; a block id
+    that is ``< 0`` or ``>= num_blocks`` is redirected to block 0 (:257-259),
+    which is the reference's behaviour and is reproduced bit-exactly.
+    """
+    B = keys.shape[0]
+    if B == 0:
+        return
+    block_ids = np.asarray(block_ids).astype(np.int64)
+    bs = key_cache.shape[2]
+    num_blocks = key_cache.shape[1]
+    offsets = np.asarray(token_offsets).astype(np.int64)
+    col = np.floor_divide(offsets, bs)            # paged_cache.py:252
+    slot = np.mod(offsets, bs)                    # paged_cache.py:253
+    width = block_ids.shape[1]
+    if np.any(col < -width) or np.any(col >= width):
+        raise IndexError("decode offset outside the block table")
+    blocks = block_ids[np.arange(B), col]         # paged_cache.py:256 (negative wraps)
+    valid = (blocks >= 0) & (blocks < num_blocks)  # paged_cache.py:257
+    blocks = np.where(valid, blocks, 0)           # paged_cache.py:259
+    # Advanced-index assignment: with duplicate (block, slot) targets the last
+    # writer wins, as in torch's CPU index_put.
+    for s in range(B):
+        key_cache[layer, blocks[s], slot[s]] = convert(keys[s], in_kind, kind)
+        value_cache[layer, blocks[s], slot[s]] = convert(values[s], in_kind, kind)
+
+
+# ---------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------
+
+@dataclass
+class OracleConfig:
+    """Mirror of ``PagedAttentionConfig`` (paged_attention.py:58-72)."""
+
+    split_kv: bool = True
+    split_size: int = 512
+    softcap: float = 0.0
+
+
+def merge_states(output, partial, prefix_lse, suffix_lse):
+    """Restates ``merge_states`` (paged_attention.py:30-55)."""
+    with np.errstate(invalid="ignore", over="ignore"):
+        merged_lse = np.logaddexp(prefix_lse, suffix_lse)
+        s1 = np.exp(prefix_lse - merged_lse)[..., None]
+        s2 = np.exp(suffix_lse - merged_lse)[..., None]
+        return output * s1 + partial * s2, merged_lse
+
+
+def _expand_kv(k: np.ndarray, group: int) -> np.ndarray:
+    """``_expand_kv`` (paged_attention.py:189-210): query head h reads KV head h // group."""
+    if group == 1:
+        return k
+    return np.repeat(k, group, axis=1)
+
+
+def _build_mask(valid: np.ndarray, context_lens: np.ndarray, q_len: int) -> np.ndarray:
+    """``_build_mask`` (paged_attention.py:212-229): padding, plus causal for q_len > 1."""
+    mask = np.broadcast_to(valid[:, None, None, :], (valid.shape[0], 1, q_len, valid.shape[1]))
+    if q_len > 1:
+        q_pos = context_lens[:, None] - q_len + np.arange(q_len)[None, :]
+        k_pos = np.arange(valid.shape[1])
+        causal = k_pos[None, None, :] <= q_pos[:, :, None]
+        mask = mask & causal[:, None, :, :]
+    return mask
+
+
+def _scores(q, k, scale, softcap):
+    s = np.matmul(q, np.swapaxes(k, -1, -2)) * scale
+    if softcap > 0:                               # paged_attention.py:243-244
+        s = np.tanh(s / softcap) * softcap
+    return s
+
+
+def _softmax_rows(scores):
+    with np.errstate(invalid="ignore"):
+        m = scores.max(axis=-1, keepdims=True)
+        e = np.exp(scores - m)
+        p = e / e.sum(axis=-1, keepdims=True)
+    return np.nan_to_num(p, nan=0.0)              # paged_attention.py:249
+
+
+def _logsumexp(scores):
+    with np.errstate(invalid="ignore", divide="ignore"):
+        m = scores.max(axis=-1, keepdims=True)
+        m_safe = np.where(np.isfinite(m), m, 0.0)
+        out = np.log(np.exp(scores - m_safe).sum(axis=-1)) + m_safe[..., 0]
+    return out
+
+
+def _forward_dense(q, k, v, valid, ctx, q_len, scale, softcap, group):
+    """``_forward_dense`` (paged_attention.py:231-250); also returns the row LSE."""
+    k, v = _expand_kv(k, group), _expand_kv(v, group)
+    scores = _scores(q, k, scale, softcap)
+    mask = _build_mask(valid, ctx, q_len)
+    scores = np.where(mask, scores, -np.inf)
+    out = np.matmul(_softmax_rows(scores), v)
+    return out, _logsumexp(scores)
+
+
+def _forward_split(q, k, v, valid, ctx, q_len, scale, softcap, group, chunk):
+    """``_forward_split`` (paged_attention.py:252-293): chunks merged by LSE."""
+    k, v = _expand_kv(k, group), _expand_kv(v, group)
+    total = k.shape[2]
+    outs, lses = [], []
+    for start in range(0, total, chunk):          # paged_attention.py:269
+        end = min(start + chunk, total)
+        scores = _scores(q, k[:, :, start:end], scale, softcap)
+        mask = _build_mask(valid[:, start:end], ctx - start, q_len)  # :277-279
+        scores = np.where(mask, scores, -np.inf)
+        lses.append(_logsumexp(scores))           # :281
+        outs.append(np.matmul(_softmax_rows(scores), v[:, :, start:end]))
+    acc, acc_lse = outs[0], lses[0]
+    for part, part_lse in zip(outs[1:], lses[1:]):  # :287-290
+        acc, acc_lse = merge_states(acc, part, acc_lse, part_lse)
+    return np.nan_to_num(acc, nan=0.0), acc_lse   # :293
+
+
+def paged_attention(query: np.ndarray, q_kind: str,
+                    key_cache: np.ndarray, value_cache: np.ndarray, kv_kind: str,
+                    layer: int, block_ids: np.ndarray, context_lens: np.ndarray,
+                    num_heads: int, num_kv_heads: int, q_len: int | None = None,
+                    scale: float | None = None, config: OracleConfig | None = None,
+                    acc=np.float64):
+    """Restates ``PagedAttention.forward`` (paged_attention.py:146-187).
+
+    ``query`` is ``[B, H, q_len, D]`` stored as ``q_kind``.  Returns ``(out,
+    lse)`` in ``acc`` precision: ``out`` ``[B, H, q_len, D]`` and the natural-log
+    LSE of the masked, scaled (and soft-capped) scores ``[B, H, q_len]``
+    (``-inf`` for fully masked rows).  The query is first rounded to the cache
+    kind, as ``q.to(k.dtype)`` does (:242, :265).
+    """
+    cfg = config or OracleConfig()
+    if num_heads % num_kv_heads:
+        raise ValueError("num_heads must be divisible by num_kv_heads")
+    group = num_heads // num_kv_heads
+    B, H, ql, D = query.shape
+    q_len = ql if q_len is None else q_len
+    scale = D ** -0.5 if scale is None else scale
+    if q_len == 0:                                # :172-177
+        return np.zeros((B, H, 0, D), dtype=acc), np.zeros((B, H, 0), dtype=acc)
+    context_lens = np.asarray(context_lens).astype(np.int64)
+    keys, values, valid = gather(key_cache, value_cache, layer, block_ids, context_lens)
+    k = np.ascontiguousarray(to_f32(keys, kv_kind).transpose(0, 2, 1, 3), dtype=acc)
+    v = np.ascontiguousarray(to_f32(values, kv_kind).transpose(0, 2, 1, 3), dtype=acc)
+    q = to_f32(convert(query, q_kind, kv_kind), kv_kind).astype(acc)
+    if cfg.split_kv and cfg.split_size < k.shape[2]:  # :185
+        return _forward_split(q, k, v, valid, context_lens, q_len, scale, cfg.softcap,
+                              group, cfg.split_size)
+    return _forward_dense(q, k, v, valid, context_lens, q_len, scale, cfg.softcap, group)
+
+
+def attention_lse(*args, **kwargs):
+    """Only the LSE of :func:`paged_attention` (dense form)."""
+    kwargs = dict(kwargs)
+    kwargs["config"] = OracleConfig(split_kv=False,
+                                    softcap=(kwargs.get("config") or OracleConfig()).softcap)
+    return paged_attention(*args, **kwargs)[1]
+
+
+# ---------------------------------------------------------------------------
+# algorithmic work (the units the roofline is computed in)
+# ---------------------------------------------------------------------------
+
+def decode_bytes(context_lens, num_kv_heads: int, head_dim: int, kv_bytes: int,
+                 batch: int, num_heads: int, q_bytes: int, out_bytes: int,
+                 block_size: int) -> int:
+    """Algorithmic HBM bytes of one paged-decode launch.
+
+    Each distinct KV byte once per KV head, plus q, out and the block-table
+    entries read: ``sum_s ctx_s*KVH*D*2*sizeof(kv) + B*H*D*(sizeof q + sizeof
+    out) + sum_s ceil(ctx_s/bs)*4``.
+    """
+    ctx = np.asarray(context_lens, dtype=np.int64)
+    kv = int(ctx.sum()) * num_kv_heads * head_dim * 2 * kv_bytes
+    qo = batch * num_heads * head_dim * (q_bytes + out_bytes)
+    table = int(((ctx + block_size - 1) // block_size).sum()) * 4
+    return kv + qo + table
+
+
+def prefill_flops(prefix_lens, q_len: int, num_heads: int, head_dim: int) -> int:
+    """Causal FLOPs of one chunked-prefill launch: ``sum_s 4*H*D*(q*p_s + q(q+1)/2)``."""
+    p = np.asarray(prefix_lens, dtype=np.int64)
+    return int(sum(4 * num_heads * head_dim * (q_len * int(x) + q_len * (q_len + 1) // 2) for x in p))
+
+
+def _self_check() -> None:  # pragma: no cover - manual sanity hook
+    x = np.array([1.0, 1.00390625, 1.005859375, -2.0, np.inf, 3.3895314e38], dtype=np.float32)
+    assert f32_to_bf16_bits(x).tolist() == [0x3F80, 0x3F80, 0x3F81, 0xC000, 0x7F80, 0x7F80]
+    assert math.isclose(float(bf16_bits_to_f32(np.array([0x3F80], np.uint16))[0]), 1.0)

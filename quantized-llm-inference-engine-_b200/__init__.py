@@ -1,0 +1,39 @@
+"""llmopt_b200: B200-native (sm_100a) paged-KV hot path for the llmopt engine.
+
+Drop-in replacements for the reference's ``llmopt.attention.PagedAttention``
+(+ ``PagedAttentionConfig``, ``merge_states``) and ``llmopt.cache.PagedKVCache``,
+backed by the C-ABI library ``libllmopt_b200.so`` (``include/llmopt_b200.h``):
+
+* paged decode attention with an exact log-sum-exp split-K combine;
+* chunked-prefill causal attention over block-table-addressed KV;
+* the KV append into the block pool, fused with the dtype cast.
+
+``install()`` rebinds the reference engine's names; ``dist`` shards the path by
+KV head over several GPUs.  The package directory name is not a Python
+identifier; it is importable with ``importlib.import_module`` and registers
+itself as ``llmopt_b200`` on import.
+"""
+
+from __future__ import annotations
+
+import sys as _sys
+
+from ._lib import check, lib, version
+from .attention import AttentionBackend, PagedAttention, PagedAttentionConfig, merge_states
+from .cache import PagedKVCache
+from .install import install, uninstall
+
+__all__ = [
+    "AttentionBackend",
+    "PagedAttention",
+    "PagedAttentionConfig",
+    "PagedKVCache",
+    "merge_states",
+    "install",
+    "uninstall",
+    "lib",
+    "check",
+    "version",
+]
+
+_sys.modules.setdefault("llmopt_b200", _sys.modules[__name__])

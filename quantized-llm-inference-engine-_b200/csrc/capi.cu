@@ -1,0 +1,637 @@
+// extern "C" entry points declared in include/llmopt_b200.h: argument checks,
+// split planning, TMA descriptor cache and kernel dispatch.  No entry point
+// allocates device memory or synchronises the stream.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+
+#include "../../include/llmopt_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+using namespace llmopt;
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int ok() {
+  g_last_error.clear();
+  return LLMOPT_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(LLMOPT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool valid_dtype(int dt) { return dt == kF32 || dt == kF16 || dt == kBF16; }
+
+// ---- device properties ---------------------------------------------------------
+std::mutex g_dev_mu;
+std::map<int, int> g_sm_count;
+
+int sm_count_of(int device) {
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  auto it = g_sm_count.find(device);
+  if (it != g_sm_count.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) {
+    n = 148;
+  }
+  g_sm_count[device] = n;
+  return n;
+}
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) d = 0;
+  return d;
+}
+
+// ---- TMA descriptors -------------------------------------------------------------
+// One 5-D descriptor per cache tensor: (head_dim, kv_heads, block_size,
+// num_blocks, layers), box (64, 1, block_size, 1, 1), 128-byte swizzle.
+using TmaKey = std::tuple<uintptr_t, int, int, int, int, int, int, int>;
+std::mutex g_tma_mu;
+std::map<TmaKey, CUtensorMap> g_tma_cache;
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  return fn;
+}
+
+bool kv_tensor_map(const void* base, int dtype, int layers, int num_blocks, int block_size,
+                   int kv_heads, int head_dim, CUtensorMap* out, std::string* why) {
+  const TmaKey key{reinterpret_cast<uintptr_t>(base), dtype, layers, num_blocks, block_size,
+                   kv_heads, head_dim, 0};
+  {
+    std::lock_guard<std::mutex> lock(g_tma_mu);
+    auto it = g_tma_cache.find(key);
+    if (it != g_tma_cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) {
+    *why = "cuTensorMapEncodeTiled unavailable";
+    return false;
+  }
+  const cuuint64_t es = 2;
+  cuuint64_t dims[5] = {(cuuint64_t)head_dim, (cuuint64_t)kv_heads, (cuuint64_t)block_size,
+                        (cuuint64_t)num_blocks, (cuuint64_t)layers};
+  cuuint64_t strides[4] = {es * head_dim, es * head_dim * kv_heads,
+                           es * head_dim * kv_heads * block_size,
+                           es * head_dim * kv_heads * block_size * (cuuint64_t)num_blocks};
+  cuuint32_t box[5] = {64, 1, (cuuint32_t)block_size, 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  CUresult r = encode(&map,
+                      dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                      5, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    *why = buf;
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(g_tma_mu);
+  if (g_tma_cache.size() > 512) g_tma_cache.clear();
+  g_tma_cache[key] = map;
+  *out = map;
+  return true;
+}
+
+// ---- split planning and workspace layout ------------------------------------------
+constexpr long long kAlign = 256;
+constexpr int kMaxBalancedCtasPerSm = 8;
+constexpr long long kMaxBalancedBatch = 4096;
+
+long long round_up(long long x, long long a) { return (x + a - 1) / a * a; }
+
+struct WsLayout {
+  long long prefix_off, lse_off, o_off, total;
+};
+
+WsLayout layout_for(long long batch, long long slots, int num_heads, int q_len, int head_dim) {
+  WsLayout w;
+  w.prefix_off = 0;
+  w.lse_off = round_up(4 * (batch + 1), kAlign);
+  w.o_off = w.lse_off + round_up(4 * slots * num_heads * (long long)q_len, kAlign);
+  w.total = w.o_off + round_up(4 * slots * num_heads * (long long)q_len * head_dim, kAlign);
+  return w;
+}
+
+SplitPlan fixed_plan(long long batch, long long width, long long split_blocks) {
+  SplitPlan p{};
+  p.mode = kModeFixed;
+  const long long w = width > 0 ? width : 1;
+  if (split_blocks < 1) split_blocks = 1;
+  if (split_blocks > w) split_blocks = w;
+  p.split_blocks = (int)split_blocks;
+  p.splits = (int)((w + split_blocks - 1) / split_blocks);
+  p.ctas = 0;
+  p.slots = batch * p.splits;
+  return p;
+}
+
+// Fixed plan for an explicit split_tokens (> 0: chunk size; < 0: one chunk).
+SplitPlan explicit_plan(long long batch, long long width, int block_size, long long split_tokens) {
+  if (split_tokens < 0) return fixed_plan(batch, width, width);
+  return fixed_plan(batch, width, (split_tokens + block_size - 1) / block_size);
+}
+
+// Automatic fixed plan for the CUDA-core path: about two waves of CTAs.
+SplitPlan generic_auto_plan(long long batch, long long width, int kv_heads, int rows, int sms) {
+  const long long row_tiles = (rows + kGenericRowTile - 1) / kGenericRowTile;
+  const long long per_split = batch * kv_heads * row_tiles;
+  long long splits = per_split > 0 ? (2LL * sms + per_split - 1) / per_split : 1;
+  const long long w = width > 0 ? width : 1;
+  if (splits > w) splits = w;
+  if (splits < 1) splits = 1;
+  return fixed_plan(batch, width, (w + splits - 1) / splits);
+}
+
+struct Choice {
+  bool tma = false;
+  DecodeLaunch launch{};
+  SplitPlan plan{};
+  CUtensorMap tmk, tmv;
+};
+
+// Pick the kernel and split plan.  Returns LLMOPT_OK or an error code.
+int choose(AttnArgs& a, long long split_tokens, int device, bool encode_maps, Choice* c) {
+  const int sms = sm_count_of(device);
+  // Fast path first: it supports the balanced plan (auto) and fixed plans.
+  AttnArgs probe = a;
+  if (split_tokens == LLMOPT_SPLIT_AUTO && a.batch <= kMaxBalancedBatch) {
+    probe.plan.mode = kModeBalanced;
+  } else if (split_tokens == LLMOPT_SPLIT_AUTO) {
+    probe.plan = generic_auto_plan(a.batch, a.table_width, a.kv_heads, a.rows, sms);
+  } else {
+    probe.plan = explicit_plan(a.batch, a.table_width, a.block_size, split_tokens);
+  }
+  if (decode_tma_supported(probe) && decode_tma_configure(probe, sms, &c->launch)) {
+    bool maps = true;
+    if (encode_maps) {
+      std::string why;
+      maps = kv_tensor_map(a.k_cache, a.kv_dtype, a.num_layers, a.num_blocks, a.block_size,
+                           a.kv_heads, a.head_dim, &c->tmk, &why) &&
+             kv_tensor_map(a.v_cache, a.kv_dtype, a.num_layers, a.num_blocks, a.block_size,
+                           a.kv_heads, a.head_dim, &c->tmv, &why);
+    }
+    if (maps) {
+      c->tma = true;
+      c->plan = probe.plan;
+      if (c->plan.mode == kModeBalanced) {
+        const int head_groups = a.kv_heads / c->launch.heads_per_cta;
+        int occ = c->launch.ctas_per_sm;
+        if (occ > kMaxBalancedCtasPerSm) occ = kMaxBalancedCtasPerSm;
+        long long ctas = (long long)sms * occ / head_groups;
+        if (ctas < 1) ctas = 1;
+        c->plan.ctas = (int)ctas;
+        c->plan.split_blocks = 0;
+        c->plan.splits = 0;
+        c->plan.slots = a.batch + ctas;
+      }
+      return LLMOPT_OK;
+    }
+  }
+  c->tma = false;
+  c->plan = split_tokens == LLMOPT_SPLIT_AUTO
+                ? generic_auto_plan(a.batch, a.table_width, a.kv_heads, a.rows, sms)
+                : explicit_plan(a.batch, a.table_width, a.block_size, split_tokens);
+  AttnArgs g = a;
+  g.plan = c->plan;
+  if (!generic_supported(g)) {
+    return fail(LLMOPT_ERR_UNSUPPORTED, "no kernel for head_dim=%d q_dtype=%d kv_dtype=%d",
+                a.head_dim, a.q_dtype, a.kv_dtype);
+  }
+  return LLMOPT_OK;
+}
+
+// Upper bound of the workspace over every plan `choose` can return.
+long long workspace_bound(long long batch, int num_heads, int kv_heads, int head_dim, int q_len,
+                          int block_size, long long width, long long split_tokens, int sms) {
+  const int rows = q_len * (num_heads / (kv_heads > 0 ? kv_heads : 1));
+  long long slots = 0;
+  if (split_tokens == LLMOPT_SPLIT_AUTO) {
+    slots = generic_auto_plan(batch, width, kv_heads, rows, sms).slots;
+    if (batch <= kMaxBalancedBatch) {
+      const long long bal = batch + (long long)sms * kMaxBalancedCtasPerSm;
+      if (bal > slots) slots = bal;
+    }
+  } else {
+    slots = explicit_plan(batch, width, block_size, split_tokens).slots;
+  }
+  return layout_for(batch, slots, num_heads, q_len, head_dim).total;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* llmopt_b200_version(void) { return "llmopt-b200 0.1.0 (sm_100a)"; }
+
+int llmopt_b200_abi_version(void) { return LLMOPT_B200_ABI_VERSION; }
+
+const char* llmopt_status_string(int status) {
+  switch (status) {
+    case LLMOPT_OK: return "ok";
+    case LLMOPT_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case LLMOPT_ERR_UNSUPPORTED: return "unsupported dtype or shape";
+    case LLMOPT_ERR_WORKSPACE: return "workspace too small";
+    case LLMOPT_ERR_CUDA: return "CUDA error";
+    case LLMOPT_ERR_INDEX: return "index out of range";
+    default: return "unknown status";
+  }
+}
+
+const char* llmopt_last_error(void) { return g_last_error.c_str(); }
+
+int llmopt_paged_attention_workspace_size(int device, int64_t batch, int32_t num_heads,
+                                          int32_t num_kv_heads, int32_t head_dim, int32_t q_len,
+                                          int32_t block_size, int64_t table_width,
+                                          int32_t kv_dtype, int64_t split_tokens,
+                                          size_t* bytes) {
+  (void)kv_dtype;
+  if (bytes == nullptr) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "bytes is null");
+  if (batch < 0 || num_heads < 1 || num_kv_heads < 1 || head_dim < 1 || q_len < 0 ||
+      block_size < 1 || table_width < 0) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
+  }
+  if (num_heads % num_kv_heads != 0) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "num_heads must be divisible by num_kv_heads");
+  }
+  if (batch == 0 || q_len == 0) {
+    *bytes = 0;
+    return ok();
+  }
+  *bytes = (size_t)workspace_bound(batch, num_heads, num_kv_heads, head_dim, q_len, block_size,
+                                   table_width, split_tokens, sm_count_of(device));
+  return ok();
+}
+
+int llmopt_paged_attention(const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h,
+                           int64_t q_t, const void* key_cache, const void* value_cache,
+                           int32_t kv_dtype, int32_t num_layers, int32_t num_blocks,
+                           int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                           int32_t layer_idx, const void* block_table, int32_t table_is_i64,
+                           int64_t table_width, int64_t table_stride, const void* context_lens,
+                           int32_t ctx_is_i64, void* out, int32_t out_dtype, int64_t o_s,
+                           int64_t o_h, int64_t o_t, float* lse, int64_t batch, int32_t num_heads,
+                           int32_t q_len, float scale, float softcap, int64_t split_tokens,
+                           void* workspace, size_t workspace_bytes, uint32_t* err,
+                           void* stream) {
+  return llmopt_paged_attention_phase(
+      query, q_dtype, q_s, q_h, q_t, key_cache, value_cache, kv_dtype, num_layers, num_blocks,
+      block_size, num_kv_heads, head_dim, layer_idx, block_table, table_is_i64, table_width,
+      table_stride, context_lens, ctx_is_i64, out, out_dtype, o_s, o_h, o_t, lse, batch,
+      num_heads, q_len, scale, softcap, split_tokens, workspace, workspace_bytes, err, stream,
+      LLMOPT_PHASE_ALL);
+}
+
+int llmopt_paged_attention_phase(const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h,
+                                 int64_t q_t, const void* key_cache, const void* value_cache,
+                                 int32_t kv_dtype, int32_t num_layers, int32_t num_blocks,
+                                 int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                                 int32_t layer_idx, const void* block_table,
+                                 int32_t table_is_i64, int64_t table_width,
+                                 int64_t table_stride, const void* context_lens,
+                                 int32_t ctx_is_i64, void* out, int32_t out_dtype, int64_t o_s,
+                                 int64_t o_h, int64_t o_t, float* lse, int64_t batch,
+                                 int32_t num_heads, int32_t q_len, float scale, float softcap,
+                                 int64_t split_tokens, void* workspace, size_t workspace_bytes,
+                                 uint32_t* err, void* stream, int32_t phases) {
+  if (phases < 1 || phases > LLMOPT_PHASE_ALL) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "phases must be 1, 2 or 3");
+  }
+  if (!valid_dtype(q_dtype) || !valid_dtype(kv_dtype) || !valid_dtype(out_dtype)) {
+    return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype (q=%d kv=%d out=%d)", q_dtype,
+                kv_dtype, out_dtype);
+  }
+  if (num_heads < 1 || num_kv_heads < 1 || num_heads % num_kv_heads != 0) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "num_heads must be divisible by num_kv_heads");
+  }
+  if (batch < 0 || q_len < 0 || num_layers < 1 || num_blocks < 1 || block_size < 1 ||
+      head_dim < 1 || table_width < 0) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
+  }
+  if (layer_idx < 0 || layer_idx >= num_layers) {
+    return fail(LLMOPT_ERR_INDEX, "layer_idx %d out of range [0, %d)", layer_idx, num_layers);
+  }
+  if (head_dim > 256) {
+    return fail(LLMOPT_ERR_UNSUPPORTED, "head_dim %d > 256", head_dim);
+  }
+  if (batch == 0 || q_len == 0) return ok();
+  if (!query || !key_cache || !value_cache || !out || !context_lens ||
+      (!block_table && table_width > 0)) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null pointer argument");
+  }
+  if (table_width > 0 && table_stride < table_width) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "table_stride < table_width");
+  }
+  AttnArgs a{};
+  a.q = query;
+  a.q_s = q_s;
+  a.q_h = q_h;
+  a.q_t = q_t;
+  a.q_dtype = q_dtype;
+  a.k_cache = key_cache;
+  a.v_cache = value_cache;
+  a.kv_dtype = kv_dtype;
+  a.num_layers = num_layers;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.layer = layer_idx;
+  a.table = block_table;
+  a.table_i64 = table_is_i64 ? 1 : 0;
+  a.table_width = table_width;
+  a.table_stride = table_stride;
+  a.ctx = context_lens;
+  a.ctx_i64 = ctx_is_i64 ? 1 : 0;
+  a.batch = batch;
+  a.num_heads = num_heads;
+  a.q_len = q_len;
+  a.group = num_heads / num_kv_heads;
+  a.rows = q_len * a.group;
+  a.scale = scale;
+  a.softcap = softcap;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.o_s = o_s;
+  a.o_h = o_h;
+  a.o_t = o_t;
+  a.lse = lse;
+  a.err = err;
+
+  const int device = current_device();
+  Choice c;
+  int st = choose(a, split_tokens, device, true, &c);
+  if (st != LLMOPT_OK) return st;
+  a.plan = c.plan;
+  const WsLayout w = layout_for(batch, a.plan.slots, num_heads, q_len, head_dim);
+  if (workspace == nullptr || (long long)workspace_bytes < w.total) {
+    return fail(LLMOPT_ERR_WORKSPACE, "workspace of %zu bytes < %lld needed", workspace_bytes,
+                w.total);
+  }
+  if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+  }
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  a.prefix = reinterpret_cast<int*>(ws + w.prefix_off);
+  a.part_lse = reinterpret_cast<float*>(ws + w.lse_off);
+  a.part_o = reinterpret_cast<float*>(ws + w.o_off);
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (phases & LLMOPT_PHASE_SPLIT) {
+    cudaError_t e =
+        c.tma ? decode_tma_launch(a, c.launch, c.tmk, c.tmv, s) : generic_launch(a, s);
+    if (e != cudaSuccess) return cuda_fail(e, c.tma ? "decode_tma launch" : "generic launch");
+  }
+  if (phases & LLMOPT_PHASE_COMBINE) {
+    cudaError_t e = combine_launch(a, s);
+    if (e != cudaSuccess) return cuda_fail(e, "combine launch");
+  }
+  return ok();
+}
+
+int llmopt_merge_states(const void* o1, const void* o2, const void* l1, const void* l2,
+                        void* out, void* lse_out, int64_t rows, int32_t head_dim,
+                        int32_t o_dtype, int32_t lse_dtype, void* stream) {
+  if (!valid_dtype(o_dtype) || !valid_dtype(lse_dtype)) {
+    return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype");
+  }
+  if (rows < 0 || head_dim < 0) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
+  if (rows == 0 || head_dim == 0) return ok();
+  if (!o1 || !o2 || !l1 || !l2 || !out) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null pointer argument");
+  }
+  cudaError_t e = merge_states_launch(o1, o2, l1, l2, out, lse_out, rows, head_dim, o_dtype,
+                                      lse_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    return e == cudaErrorInvalidValue
+               ? fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype pair (o=%d lse=%d)", o_dtype,
+                      lse_dtype)
+               : cuda_fail(e, "merge_states launch");
+  }
+  return ok();
+}
+
+static int check_cache_args(int kv_dtype, int num_layers, int num_blocks, int block_size,
+                            int num_kv_heads, int head_dim, int layer_idx, int64_t table_width,
+                            int64_t table_stride) {
+  if (!valid_dtype(kv_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported cache dtype");
+  if (num_layers < 1 || num_blocks < 1 || block_size < 1 || num_kv_heads < 1 || head_dim < 1 ||
+      table_width < 0) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid cache shape");
+  }
+  if (layer_idx < 0 || layer_idx >= num_layers) {
+    return fail(LLMOPT_ERR_INDEX, "layer_idx %d out of range [0, %d)", layer_idx, num_layers);
+  }
+  if (table_width > 0 && table_stride < table_width) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "table_stride < table_width");
+  }
+  return LLMOPT_OK;
+}
+
+static int vector_width(const void* src_k, const void* src_v, int in_dtype, const void* k_cache,
+                        const void* v_cache, int head_dim, std::initializer_list<int64_t> strides) {
+  (void)in_dtype;
+  if (head_dim % 8 != 0) return 1;
+  for (const void* p : {src_k, src_v, k_cache, v_cache}) {
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return 1;
+  }
+  for (int64_t s : strides) {
+    if (s % 8 != 0) return 1;
+  }
+  return 8;
+}
+
+int llmopt_kv_write(const void* keys, const void* values, int32_t in_dtype, int64_t k_s,
+                    int64_t k_t, int64_t k_h, int64_t v_s, int64_t v_t, int64_t v_h,
+                    void* key_cache, void* value_cache, int32_t kv_dtype, int32_t num_layers,
+                    int32_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                    int32_t head_dim, int32_t layer_idx, const void* block_table,
+                    int32_t table_is_i64, int64_t table_width, int64_t table_stride,
+                    const void* token_offsets, int32_t off_is_i64, int64_t batch, int32_t q_len,
+                    uint32_t* err, void* stream) {
+  if (!valid_dtype(in_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported input dtype");
+  int st = check_cache_args(kv_dtype, num_layers, num_blocks, block_size, num_kv_heads, head_dim,
+                            layer_idx, table_width, table_stride);
+  if (st != LLMOPT_OK) return st;
+  if (batch < 0 || q_len < 0) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
+  if (batch == 0 || q_len == 0) return ok();
+  if (!keys || !values || !key_cache || !value_cache || !token_offsets ||
+      (!block_table && table_width > 0)) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null pointer argument");
+  }
+  KvWriteArgs a{};
+  a.keys = keys;
+  a.values = values;
+  a.in_dtype = in_dtype;
+  a.k_s = k_s;
+  a.k_t = k_t;
+  a.k_h = k_h;
+  a.v_s = v_s;
+  a.v_t = v_t;
+  a.v_h = v_h;
+  a.k_cache = key_cache;
+  a.v_cache = value_cache;
+  a.kv_dtype = kv_dtype;
+  a.num_layers = num_layers;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.layer = layer_idx;
+  a.table = block_table;
+  a.table_i64 = table_is_i64 ? 1 : 0;
+  a.table_width = table_width;
+  a.table_stride = table_stride;
+  a.offsets = token_offsets;
+  a.off_i64 = off_is_i64 ? 1 : 0;
+  a.batch = batch;
+  a.q_len = q_len;
+  a.err = err;
+  a.vec = vector_width(keys, values, in_dtype, key_cache, value_cache, head_dim,
+                       {k_s, k_t, k_h, v_s, v_t, v_h});
+  if (table_width == 0) return ok();  // every walk ends before its first column
+  cudaError_t e = kv_write_launch(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "kv_write launch");
+  return ok();
+}
+
+int llmopt_kv_write_decode(const void* keys, const void* values, int32_t in_dtype, int64_t k_s,
+                           int64_t k_h, int64_t v_s, int64_t v_h, void* key_cache,
+                           void* value_cache, int32_t kv_dtype, int32_t num_layers,
+                           int32_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                           int32_t head_dim, int32_t layer_idx, const void* block_table,
+                           int32_t table_is_i64, int64_t table_width, int64_t table_stride,
+                           const void* token_offsets, int32_t off_is_i64, int64_t batch,
+                           uint32_t* err, void* stream) {
+  if (!valid_dtype(in_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported input dtype");
+  int st = check_cache_args(kv_dtype, num_layers, num_blocks, block_size, num_kv_heads, head_dim,
+                            layer_idx, table_width, table_stride);
+  if (st != LLMOPT_OK) return st;
+  if (batch < 0) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
+  if (batch == 0) return ok();
+  if (table_width == 0) return fail(LLMOPT_ERR_INDEX, "empty block table");
+  if (!keys || !values || !key_cache || !value_cache || !token_offsets || !block_table) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null pointer argument");
+  }
+  KvWriteArgs a{};
+  a.keys = keys;
+  a.values = values;
+  a.in_dtype = in_dtype;
+  a.k_s = k_s;
+  a.k_t = 0;
+  a.k_h = k_h;
+  a.v_s = v_s;
+  a.v_t = 0;
+  a.v_h = v_h;
+  a.k_cache = key_cache;
+  a.v_cache = value_cache;
+  a.kv_dtype = kv_dtype;
+  a.num_layers = num_layers;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.layer = layer_idx;
+  a.table = block_table;
+  a.table_i64 = table_is_i64 ? 1 : 0;
+  a.table_width = table_width;
+  a.table_stride = table_stride;
+  a.offsets = token_offsets;
+  a.off_i64 = off_is_i64 ? 1 : 0;
+  a.batch = batch;
+  a.q_len = 1;
+  a.err = err;
+  a.vec = vector_width(keys, values, in_dtype, key_cache, value_cache, head_dim,
+                       {k_s, k_h, v_s, v_h});
+  cudaError_t e = kv_write_decode_launch(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "kv_write_decode launch");
+  return ok();
+}
+
+int llmopt_paged_gather(const void* key_cache, const void* value_cache, int32_t kv_dtype,
+                        int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                        int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                        const void* block_table, int32_t table_is_i64, int64_t table_width,
+                        int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
+                        int64_t batch, int64_t max_len, void* out_keys, void* out_values,
+                        uint8_t* valid, uint32_t* err, void* stream) {
+  int st = check_cache_args(kv_dtype, num_layers, num_blocks, block_size, num_kv_heads, head_dim,
+                            layer_idx, table_width, table_stride);
+  if (st != LLMOPT_OK) return st;
+  if (batch < 0 || max_len < 0) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
+  if (batch == 0 || max_len == 0) return ok();
+  if (max_len > table_width * (int64_t)block_size) {
+    return fail(LLMOPT_ERR_INDEX, "max_len %lld exceeds table width %lld x block_size %d",
+                (long long)max_len, (long long)table_width, block_size);
+  }
+  if (!key_cache || !value_cache || !block_table || !context_lens || !out_keys || !out_values ||
+      !valid) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null pointer argument");
+  }
+  GatherArgs a{};
+  a.k_cache = key_cache;
+  a.v_cache = value_cache;
+  a.kv_dtype = kv_dtype;
+  a.num_layers = num_layers;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.layer = layer_idx;
+  a.table = block_table;
+  a.table_i64 = table_is_i64 ? 1 : 0;
+  a.table_width = table_width;
+  a.table_stride = table_stride;
+  a.ctx = context_lens;
+  a.ctx_i64 = ctx_is_i64 ? 1 : 0;
+  a.batch = batch;
+  a.max_len = max_len;
+  a.out_k = out_keys;
+  a.out_v = out_values;
+  a.valid = valid;
+  a.err = err;
+  cudaError_t e = gather_launch(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gather launch");
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,191 @@
+// Split-K combine and merge_states.
+//
+// combine_kernel folds the split partials of each (sequence, head, query row)
+// with the exact log-sum-exp rule of merge_states
+// (src/llmopt/attention/paged_attention.py:30-55), done in one pass over all
+// partials instead of the reference's sequential pairwise chain (:287-290):
+//   lse = M + log(sum_p exp(lse_p - M)),  out = sum_p exp(lse_p - lse) * out_p
+// with M = max_p lse_p.  A row whose partials are all -inf (every key masked)
+// gets out = 0 and lse = -inf, which is what the reference's nan_to_num
+// produces (:291-293).  One warp per output row; lanes own head_dim slices.
+#include <float.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace llmopt {
+namespace {
+
+constexpr int kWarpsPerCta = 4;
+constexpr int kMaxDimPerLane = 8;  // head_dim <= 256
+
+struct SlotRange {
+  long long first;   // fixed: first slot; balanced: first CTA
+  long long count;   // fixed: number of slots; balanced: CTAs to scan
+  long long p_lo, p_hi, total;  // balanced: the sequence's block range and T
+};
+
+__device__ __forceinline__ bool balanced_touch(long long c, const SlotRange& r, long long ctas) {
+  const long long a0 = range_start(c, r.total, ctas);
+  const long long a1 = range_start(c + 1, r.total, ctas);
+  const long long lo = a0 > r.p_lo ? a0 : r.p_lo;
+  const long long hi = a1 < r.p_hi ? a1 : r.p_hi;
+  return lo < hi;
+}
+
+template <int O_DT>
+__global__ void __launch_bounds__(kWarpsPerCta * 32) combine_kernel(const AttnArgs a) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * kWarpsPerCta + warp;
+  const long long nrows = a.batch * a.num_heads * (long long)a.q_len;
+  if (row >= nrows) return;
+  const int qi = (int)(row % a.q_len);
+  const long long sh = row / a.q_len;
+  const int h = (int)(sh % a.num_heads);
+  const long long s = sh / a.num_heads;
+  const int D = a.head_dim;
+
+  SlotRange r{0, 0, 0, 0, 0};
+  const bool balanced = a.plan.mode == kModeBalanced;
+  if (balanced) {
+    r.p_lo = a.prefix[s];
+    r.p_hi = a.prefix[s + 1];
+    r.total = a.prefix[a.batch];
+    if (r.p_hi > r.p_lo) {
+      r.first = range_owner(r.p_lo, r.total, a.plan.ctas);
+      r.count = range_owner(r.p_hi - 1, r.total, a.plan.ctas) - r.first + 1;
+    }
+  } else {
+    const long long ctx_s = load_index(a.ctx, a.ctx_i64, s);
+    const long long nb = blocks_of(ctx_s, a.block_size, a.table_width);
+    long long cnt = (nb + a.plan.split_blocks - 1) / a.plan.split_blocks;
+    if (cnt > a.plan.splits) cnt = a.plan.splits;
+    r.first = s * a.plan.splits;
+    r.count = cnt;
+  }
+
+  auto slot_of = [&](long long i) -> long long {
+    return balanced ? s + (r.first + i) : r.first + i;
+  };
+  auto valid_of = [&](long long i) -> bool {
+    return balanced ? balanced_touch(r.first + i, r, a.plan.ctas) : true;
+  };
+
+  // pass 1: max LSE
+  float mx = -INFINITY;
+  for (long long i = lane; i < r.count; i += 32) {
+    if (!valid_of(i)) continue;
+    const float l = a.part_lse[(slot_of(i) * a.num_heads + h) * a.q_len + qi];
+    mx = fmaxf(mx, l);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+
+  float acc[kMaxDimPerLane];
+#pragma unroll
+  for (int k = 0; k < kMaxDimPerLane; ++k) acc[k] = 0.f;
+  float wsum = 0.f;
+  if (mx != -INFINITY) {
+    for (long long i = 0; i < r.count; ++i) {
+      if (!valid_of(i)) continue;
+      const long long prow = (slot_of(i) * a.num_heads + h) * a.q_len + qi;
+      const float l = a.part_lse[prow];
+      if (l == -INFINITY) continue;
+      const float w = expf(l - mx);
+      wsum += w;
+      const float* src = a.part_o + prow * D;
+#pragma unroll
+      for (int k = 0; k < kMaxDimPerLane; ++k) {
+        const int d = lane + 32 * k;
+        if (d < D) acc[k] = fmaf(w, src[d], acc[k]);
+      }
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  const long long obase = s * a.o_s + (long long)h * a.o_h + (long long)qi * a.o_t;
+#pragma unroll
+  for (int k = 0; k < kMaxDimPerLane; ++k) {
+    const int d = lane + 32 * k;
+    if (d < D) store_f32<O_DT>(a.out, obase + d, acc[k] * inv);
+  }
+  if (a.lse != nullptr && lane == 0) {
+    a.lse[row] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+  }
+}
+
+// torch.logaddexp semantics: equal infinities return themselves, otherwise
+// max + log1p(exp(-|a - b|)) (NaN propagates).
+__device__ __forceinline__ float logaddexp_f(float x, float y) {
+  const float m = fmaxf(x, y);
+  if (isinf(m) && x == y) return m;
+  if (isnan(x) || isnan(y)) return x + y;
+  return m + log1pf(expf(-fabsf(x - y)));
+}
+
+template <int O_DT, int L_DT>
+__global__ void merge_states_kernel(const void* o1, const void* o2, const void* l1,
+                                    const void* l2, void* out, void* lse_out, long long rows,
+                                    int head_dim) {
+  const long long n = rows * head_dim;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / head_dim;
+    const float a1 = load_f32<L_DT>(l1, r);
+    const float a2 = load_f32<L_DT>(l2, r);
+    const float m = logaddexp_f(a1, a2);
+    const float w1 = expf(a1 - m);
+    const float w2 = expf(a2 - m);
+    store_f32<O_DT>(out, i, load_f32<O_DT>(o1, i) * w1 + load_f32<O_DT>(o2, i) * w2);
+    if (i - r * head_dim == 0 && lse_out != nullptr) store_f32<L_DT>(lse_out, r, m);
+  }
+}
+
+template <int O_DT, int L_DT>
+const void* merge_ptr() {
+  return reinterpret_cast<const void*>(&merge_states_kernel<O_DT, L_DT>);
+}
+
+}  // namespace
+
+cudaError_t combine_launch(const AttnArgs& a, cudaStream_t stream) {
+  const long long nrows = a.batch * a.num_heads * (long long)a.q_len;
+  if (nrows <= 0) return cudaSuccess;
+  const long long grid = (nrows + kWarpsPerCta - 1) / kWarpsPerCta;
+  if (grid > 0x7fffffffLL || a.head_dim > 32 * kMaxDimPerLane) return cudaErrorInvalidValue;
+  const void* fn = nullptr;
+  switch (a.out_dtype) {
+    case kF32: fn = reinterpret_cast<const void*>(&combine_kernel<kF32>); break;
+    case kF16: fn = reinterpret_cast<const void*>(&combine_kernel<kF16>); break;
+    case kBF16: fn = reinterpret_cast<const void*>(&combine_kernel<kBF16>); break;
+    default: return cudaErrorInvalidValue;
+  }
+  void* args[] = {const_cast<AttnArgs*>(&a)};
+  return cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kWarpsPerCta * 32), args, 0, stream);
+}
+
+cudaError_t merge_states_launch(const void* o1, const void* o2, const void* l1, const void* l2,
+                                void* out, void* lse_out, long long rows, int head_dim,
+                                int o_dtype, int lse_dtype, cudaStream_t stream) {
+  const long long n = rows * head_dim;
+  if (n <= 0) return cudaSuccess;
+  const void* fn = nullptr;
+#define LLMOPT_MERGE_CASE(OT, LT) \
+  if (o_dtype == OT && lse_dtype == LT) fn = merge_ptr<OT, LT>();
+  LLMOPT_MERGE_CASE(kF32, kF32)
+  LLMOPT_MERGE_CASE(kF16, kF32)
+  LLMOPT_MERGE_CASE(kBF16, kF32)
+  LLMOPT_MERGE_CASE(kF16, kF16)
+  LLMOPT_MERGE_CASE(kBF16, kBF16)
+  LLMOPT_MERGE_CASE(kF32, kF16)
+  LLMOPT_MERGE_CASE(kF32, kBF16)
+#undef LLMOPT_MERGE_CASE
+  if (fn == nullptr) return cudaErrorInvalidValue;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  void* args[] = {const_cast<void**>(&o1), const_cast<void**>(&o2), const_cast<void**>(&l1),
+                  const_cast<void**>(&l2), &out, &lse_out, &rows, &head_dim};
+  return cudaLaunchKernel(fn, dim3((unsigned)blocks), dim3(256), args, 0, stream);
+}
+
+}  // namespace llmopt

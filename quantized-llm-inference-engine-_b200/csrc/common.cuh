@@ -1,0 +1,218 @@
+// Shared device helpers for the paged-KV kernels (sm_100a).
+//
+// * element conversions with torch's rounding (round-to-nearest-even casts);
+// * thin inline-PTX wrappers for mbarriers, TMA tile loads, ldmatrix and the
+//   m16n8k16 tensor-core MMA used by the decode kernel;
+// * bounded waits: every spin on an mbarrier gives up after kWaitLimitCycles,
+//   records LLMOPT_DEVERR_WAIT_TIMEOUT and lets the kernel finish.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace llmopt {
+
+enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
+
+constexpr unsigned kErrBlockId = 1u;
+constexpr unsigned kErrTableWidth = 2u;
+constexpr unsigned kErrWaitTimeout = 4u;
+
+// About one second at B200 clocks: a wait that long means a lost producer.
+constexpr long long kWaitLimitCycles = 2000000000LL;
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ void record_error(unsigned* err, unsigned bits) {
+  if (err != nullptr) atomicOr(err, bits);
+}
+
+// ---------------------------------------------------------------------------
+// element types
+// ---------------------------------------------------------------------------
+template <int DT> struct ElemT;
+template <> struct ElemT<kF32> { using T = float; };
+template <> struct ElemT<kF16> { using T = __half; };
+template <> struct ElemT<kBF16> { using T = __nv_bfloat16; };
+
+template <int DT>
+__device__ __forceinline__ float load_f32(const void* base, long long idx) {
+  if constexpr (DT == kF32) {
+    return static_cast<const float*>(base)[idx];
+  } else if constexpr (DT == kF16) {
+    return __half2float(static_cast<const __half*>(base)[idx]);
+  } else {
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[idx]);
+  }
+}
+
+// float -> storage type, round-to-nearest-even (torch's .to(dtype) for finite
+// values and infinities; subnormals are kept, not flushed).
+template <int DT>
+__device__ __forceinline__ typename ElemT<DT>::T from_f32(float x) {
+  if constexpr (DT == kF32) {
+    return x;
+  } else if constexpr (DT == kF16) {
+    return __float2half_rn(x);
+  } else {
+    return __float2bfloat16_rn(x);
+  }
+}
+
+// Round a float to storage type DT and widen it back (q.to(k.dtype) in fp32 math).
+template <int DT>
+__device__ __forceinline__ float round_through(float x) {
+  if constexpr (DT == kF32) {
+    return x;
+  } else if constexpr (DT == kF16) {
+    return __half2float(__float2half_rn(x));
+  } else {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void store_f32(void* base, long long idx, float x) {
+  static_cast<typename ElemT<DT>::T*>(base)[idx] = from_f32<DT>(x);
+}
+
+// Two floats packed into one 32-bit register of 16-bit elements (low = first).
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (DT == kF16) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+__device__ __forceinline__ long long load_index(const void* p, int is64, long long i) {
+  return is64 ? static_cast<const long long*>(p)[i]
+              : static_cast<long long>(static_cast<const int*>(p)[i]);
+}
+
+// Python floor division / modulo (the reference's torch.div(..., "floor") and %).
+__device__ __forceinline__ long long floordiv(long long a, long long b) {
+  long long q = a / b;
+  return (a % b != 0 && ((a < 0) != (b < 0))) ? q - 1 : q;
+}
+__device__ __forceinline__ long long floormod(long long a, long long b) {
+  long long r = a % b;
+  return (r != 0 && ((r < 0) != (b < 0))) ? r + b : r;
+}
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity; false after the limit.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitLimitCycles) return false;
+  }
+  return true;
+}
+
+// 5-D TMA tile load (no multicast) into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3), "r"(c4)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                              uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D = A * B + D for one m16n8k16 tile with fp32 accumulators.
+template <int DT>
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  if constexpr (DT == kF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// 2^x on the special-function unit (MUFU.EX2); exact 0 for -inf.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float warp_max_xor(float v, int mask) {
+  return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, mask));
+}
+
+}  // namespace llmopt

@@ -1,0 +1,117 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "plan.cuh"
+
+namespace llmopt {
+
+// Everything the attention kernels read, in one POD passed by value.
+struct AttnArgs {
+  // query [batch, num_heads, q_len, head_dim]
+  const void* q;
+  long long q_s, q_h, q_t;
+  int q_dtype;
+  // cache [layers, num_blocks, block_size, kv_heads, head_dim]
+  const void* k_cache;
+  const void* v_cache;
+  int kv_dtype;
+  int num_layers, num_blocks, block_size, kv_heads, head_dim, layer;
+  // block table / context
+  const void* table;
+  int table_i64;
+  long long table_width, table_stride;
+  const void* ctx;
+  int ctx_i64;
+  // shape
+  long long batch;
+  int num_heads, q_len, group, rows;  // rows = q_len * group (query rows per KV head)
+  float scale, softcap;
+  // partition + workspace
+  SplitPlan plan;
+  int* prefix;        // [batch + 1] block prefix sums (balanced mode)
+  float* part_lse;    // [slots, num_heads, q_len]
+  float* part_o;      // [slots, num_heads, q_len, head_dim]
+  // output
+  void* out;
+  int out_dtype;
+  long long o_s, o_h, o_t;
+  float* lse;         // optional [batch, num_heads, q_len]
+  unsigned* err;
+};
+
+// Fast decode path: TMA-staged blocks + m16n8k16 tensor-core tiles.
+struct DecodeLaunch {
+  int heads_per_cta;  // KV heads one CTA stages per block (box height)
+  int stages;         // shared-memory ring depth
+  int ctas_per_sm;
+  size_t smem_bytes;
+};
+
+bool decode_tma_supported(const AttnArgs& a);
+// Fills `launch` (occupancy, smem) for this shape; false if it cannot run here.
+bool decode_tma_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch);
+cudaError_t decode_tma_launch(const AttnArgs& a, const DecodeLaunch& launch,
+                              const CUtensorMap& tmk, const CUtensorMap& tmv,
+                              cudaStream_t stream);
+
+// Generic path: any dtype / head_dim <= 256 / block size / q_len (CUDA cores).
+constexpr int kGenericRowTile = 16;
+constexpr int kGenericKeyTile = 32;
+bool generic_supported(const AttnArgs& a);
+cudaError_t generic_launch(const AttnArgs& a, cudaStream_t stream);
+
+// Merge of split partials into the output (+ optional LSE).
+cudaError_t combine_launch(const AttnArgs& a, cudaStream_t stream);
+
+// merge_states
+cudaError_t merge_states_launch(const void* o1, const void* o2, const void* l1, const void* l2,
+                                void* out, void* lse_out, long long rows, int head_dim,
+                                int o_dtype, int lse_dtype, cudaStream_t stream);
+
+// KV cache writes and gather.
+struct KvWriteArgs {
+  const void* keys;
+  const void* values;
+  int in_dtype;
+  long long k_s, k_t, k_h, v_s, v_t, v_h;
+  void* k_cache;
+  void* v_cache;
+  int kv_dtype;
+  int num_layers, num_blocks, block_size, kv_heads, head_dim, layer;
+  const void* table;
+  int table_i64;
+  long long table_width, table_stride;
+  const void* offsets;
+  int off_i64;
+  long long batch;
+  int q_len;
+  unsigned* err;
+  int vec;  // elements per vector access (8 when every address allows 16-byte stores, else 1)
+};
+
+cudaError_t kv_write_launch(const KvWriteArgs& a, cudaStream_t stream);
+cudaError_t kv_write_decode_launch(const KvWriteArgs& a, cudaStream_t stream);
+
+struct GatherArgs {
+  const void* k_cache;
+  const void* v_cache;
+  int kv_dtype;
+  int num_layers, num_blocks, block_size, kv_heads, head_dim, layer;
+  const void* table;
+  int table_i64;
+  long long table_width, table_stride;
+  const void* ctx;
+  int ctx_i64;
+  long long batch, max_len;
+  void* out_k;
+  void* out_v;
+  unsigned char* valid;
+  unsigned* err;
+};
+cudaError_t gather_launch(const GatherArgs& a, cudaStream_t stream);
+
+}  // namespace llmopt

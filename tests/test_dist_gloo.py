@@ -1,0 +1,79 @@
+"""Head-sharding plumbing on CPU: shard ranges and the output all-gather (gloo, 2 ranks).
+
+The kernels themselves need a GPU; what is tested here is the host logic that
+surrounds them on several ranks: which heads each rank owns, and that the
+head-major all-gather reassembles ``[seq, H, q_len, D]`` exactly.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import load_package
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_shard_heads_partition():
+    from importlib import import_module
+
+    d = import_module("quantized-llm-inference-engine-_b200.dist")
+    for world in (1, 2, 4, 8):
+        shards = [d.shard_heads(64, 8, world, r) for r in range(world)]
+        assert [s.kv_lo for s in shards] == [r * 8 // world for r in range(world)]
+        assert shards[-1].kv_hi == 8 and shards[-1].q_hi == 64
+        for s in shards:
+            # query head h reads KV head h // group: the query range maps into the KV range
+            group = 64 // 8
+            assert s.q_lo // group == s.kv_lo and (s.q_hi - 1) // group == s.kv_hi - 1
+    with pytest.raises(ValueError):
+        d.shard_heads(32, 8, 3, 0)
+    with pytest.raises(ValueError):
+        d.shard_heads(32, 8, 2, 2)
+
+
+def _worker(rank: int, world: int, port: int, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    from importlib import import_module
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        d = import_module("quantized-llm-inference-engine-_b200.dist")
+        seq, H, q_len, D = 3, 8, 2, 4
+        g = torch.Generator().manual_seed(0)
+        full = torch.randn(seq, H, q_len, D, generator=g)      # what every rank should end with
+        shard = d.shard_heads(H, 4, world, rank)
+        local = full[:, shard.q_lo:shard.q_hi].permute(1, 0, 2, 3).contiguous()  # head-major
+        got = d.gather_heads(local)
+        result_q.put((rank, bool(torch.equal(got, full)), tuple(got.shape)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_head_major_all_gather_world2():
+    load_package()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(ok for _, ok, _ in results)
+    assert all(shape == (3, 8, 2, 4) for _, _, shape in results)

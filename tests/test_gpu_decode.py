@@ -1,0 +1,264 @@
+"""GPU parity of the paged decode / short-chunk attention against the oracle.
+
+Covers the tensor-core decode path's shape space (head_dim 64/128/256, group
+1..16, KV heads 1..8, q_len * group <= 16, bf16/fp16 caches, fp32/16-bit
+queries), ragged and edge context lengths, -1 holes, soft-capping, and the
+split planner's corner cases (empty sequences, fewer blocks than CTAs, one
+very long sequence, batches past the balanced-plan limit).  At BASELINE
+config-2 size it checks size-independent properties: every split mode gives
+the same answer, relocating physical blocks changes nothing bit-for-bit, and
+sequences that share prefix blocks with equal queries get identical outputs.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from _gpu import device_case, device_errors, make_cache, run_attention, subset_case, to_dev
+from _parity import assert_fp32_close, assert_lowp_close, assert_lse_close
+from cases import build_paged_case
+from conftest import load_package
+from oracle import paged_oracle as po
+
+pytestmark = pytest.mark.gpu
+
+
+def oracle(case, softcap=0.0):
+    # fp64 arithmetic for the 1e-5 fp32 bar; fp32 is ample for the 2e-2 16-bit bar
+    # and halves the memory of the oracle's padded, group-expanded copies.
+    acc = np.float64 if case["kv_kind"] == "f32" else np.float32
+    return po.paged_attention(case["query"], case["q_kind"], case["key_cache"], case["value_cache"],
+                              case["kv_kind"], case["layer"], case["block_ids"],
+                              case["context_lens"], case["heads"], case["kv_heads"],
+                              q_len=case["q_len"],
+                              config=po.OracleConfig(split_kv=False, softcap=softcap), acc=acc)
+
+
+def check_case(cuda, case, softcap=0.0, modes=("auto", "fixed", "none"), split_size=48):
+    want, want_lse = oracle(case, softcap)
+    for mode in modes:
+        out, lse = run_attention(case, cuda, split_kv=mode != "none", split_size=split_size,
+                                 softcap=softcap, split_mode="fixed" if mode == "fixed" else "auto")
+        if case["kv_kind"] == "f32":
+            assert_fp32_close(out, want, f"mode={mode}")
+        else:
+            assert_lowp_close(out, want, f"mode={mode}")
+        assert_lse_close(lse, want_lse, f"mode={mode} lse")
+    assert device_errors(cuda) == 0
+
+
+EDGE_CTX = [1, 15, 16, 17, 31, 33, 100, 600]
+
+
+@pytest.mark.parametrize("head_dim", [64, 128, 256])
+@pytest.mark.parametrize("heads,kv_heads", [(32, 8), (8, 8), (16, 2), (16, 1), (8, 4)])
+def test_decode_shapes(cuda, head_dim, heads, kv_heads):
+    case = build_paged_case(100 + head_dim + heads + kv_heads, batch=len(EDGE_CTX), heads=heads,
+                            kv_heads=kv_heads, head_dim=head_dim, block_size=16, ctx=EDGE_CTX,
+                            kv_kind="bf16", q_kind="bf16", value_scale=0.5)
+    check_case(cuda, case)
+
+
+@pytest.mark.parametrize("q_len,heads", [(2, 32), (4, 32), (16, 8), (3, 16)])
+def test_short_chunks_on_tensor_core_path(cuda, q_len, heads):
+    """q_len * group <= 16: speculative-decode sized chunks, causal inside the chunk."""
+    case = build_paged_case(7 + q_len, batch=5, heads=heads, kv_heads=8, head_dim=128,
+                            block_size=16, ctx=[3, 16, 17, 64, 301], kv_kind="bf16",
+                            q_kind="bf16", q_len=q_len)
+    check_case(cuda, case)
+
+
+@pytest.mark.parametrize("q_kind,kv_kind", [("f32", "bf16"), ("f32", "f16"), ("f16", "f16"),
+                                            ("bf16", "f16"), ("f16", "bf16")])
+def test_decode_dtypes(cuda, q_kind, kv_kind):
+    case = build_paged_case(11, batch=4, heads=32, kv_heads=8, head_dim=128, block_size=16,
+                            ctx=[5, 40, 257, 700], kv_kind=kv_kind, q_kind=q_kind)
+    check_case(cuda, case)
+
+
+def test_decode_softcap_and_holes(cuda):
+    case = build_paged_case(12, batch=4, heads=32, kv_heads=8, head_dim=128, block_size=16,
+                            ctx=[40, 200, 513, 64], kv_kind="bf16", q_kind="bf16",
+                            holes=[(1, 0), (1, 5), (2, 31), (3, 3)], value_scale=2.0)
+    check_case(cuda, case, softcap=10.0)
+
+
+def test_empty_and_tiny_sequences(cuda):
+    """ctx 0 rows give out 0 / lse -inf; fewer blocks in the batch than CTAs."""
+    ctx = [0, 1, 0, 0, 2, 0, 17, 0]
+    case = build_paged_case(13, batch=len(ctx), heads=32, kv_heads=8, head_dim=128,
+                            block_size=16, ctx=ctx, kv_kind="bf16", q_kind="bf16", width=3)
+    check_case(cuda, case)
+    out, lse = run_attention(case, cuda)
+    assert np.all(out[np.array(ctx) == 0] == 0)
+    assert np.all(np.isneginf(lse[np.array(ctx) == 0]))
+
+
+def test_one_long_sequence_spans_many_ctas(cuda):
+    case, cache = device_case(14, cuda, ctx=[12000, 3], heads=16, kv_heads=2, head_dim=128)
+    out, lse = run_attention(case, cuda, cache=cache)
+    want, want_lse = oracle(subset_case(case, cache, [0, 1]))
+    assert_lowp_close(out, want, "long sequence")
+    assert_lse_close(lse, want_lse, "long sequence lse")
+    assert device_errors(cuda) == 0
+
+
+def test_large_batch_uses_fixed_plan(cuda):
+    rng = np.random.default_rng(15)
+    ctx = rng.integers(1, 40, size=4200)
+    case = build_paged_case(15, batch=len(ctx), heads=4, kv_heads=2, head_dim=64, block_size=16,
+                            ctx=ctx, kv_kind="bf16", q_kind="bf16")
+    check_case(cuda, case, modes=("auto",))
+
+
+def test_fp32_generic_path_config1(cuda):
+    """BASELINE config 1 (fp32): CUDA-core path, 1e-5 relative."""
+    rng = np.random.default_rng(1000)
+    ctx = rng.integers(16, 513, size=8)
+    case = build_paged_case(0, batch=8, heads=8, kv_heads=2, head_dim=64, block_size=16,
+                            ctx=ctx, kv_kind="f32", q_kind="f32", num_blocks=512)
+    check_case(cuda, case, split_size=int(np.ceil(ctx.max() / 4)))
+
+
+def test_generic_prefill_fp32(cuda):
+    case = build_paged_case(16, batch=3, heads=8, kv_heads=2, head_dim=32, block_size=8,
+                            ctx=[70, 5, 130], kv_kind="f32", q_kind="f32", q_len=20)
+    check_case(cuda, case)
+
+
+def test_bad_block_ids_are_flagged_not_read(cuda):
+    case = build_paged_case(17, batch=3, heads=32, kv_heads=8, head_dim=128, block_size=16,
+                            ctx=[64, 64, 64], kv_kind="bf16", q_kind="bf16")
+    nb = case["key_cache"].shape[1]
+    case["block_ids"][1, 2] = nb + 100          # outside the pool
+    out, _ = run_attention(case, cuda)
+    assert np.isfinite(out).all()
+    from importlib import import_module
+
+    assert device_errors(cuda) & import_module("quantized-llm-inference-engine-_b200._lib").DEVERR_BLOCK_ID
+
+
+def test_context_beyond_table_is_flagged(cuda):
+    case = build_paged_case(18, batch=2, heads=8, kv_heads=2, head_dim=128, block_size=16,
+                            ctx=[64, 64], kv_kind="bf16", q_kind="bf16")
+    case["context_lens"] = np.array([64, 200])   # table has 4 columns = 64 tokens
+    run_attention(case, cuda)
+    from importlib import import_module
+
+    assert device_errors(cuda) & import_module("quantized-llm-inference-engine-_b200._lib").DEVERR_TABLE_WIDTH
+
+
+# ---------------------------------------------------------------------------
+# BASELINE config 2 (full size): size-independent properties
+# ---------------------------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def config2(cuda):
+    rng = np.random.default_rng(2)
+    ctx = rng.integers(1024, 8193, size=64)
+    return device_case(2, cuda, ctx=ctx, heads=32, kv_heads=8, head_dim=128, value_scale=0.5)
+
+
+def test_config2_split_modes_agree_and_match_oracle(cuda, config2):
+    case, cache = config2
+    outs = {}
+    for mode in ("auto", "fixed", "none"):
+        outs[mode] = run_attention(case, cuda, split_kv=mode != "none", split_size=512,
+                                   split_mode="fixed" if mode == "fixed" else "auto", cache=cache)
+    for mode in ("fixed", "none"):
+        assert_lowp_close(outs[mode][0], outs["auto"][0], f"{mode} vs auto")
+        assert_lse_close(outs[mode][1], outs["auto"][1], f"{mode} vs auto lse")
+    pick = [0, 17, 63]
+    want, want_lse = oracle(subset_case(case, cache, pick))
+    assert_lowp_close(outs["auto"][0][pick], want, "oracle subset")
+    assert_lse_close(outs["auto"][1][pick], want_lse, "oracle subset lse")
+    assert device_errors(cuda) == 0
+
+
+def test_config2_block_relocation_is_bit_identical(cuda, config2):
+    case, cache = config2
+    out_a, lse_a = run_attention(case, cuda, cache=cache)
+    nb = cache.num_blocks
+    perm = np.random.default_rng(3).permutation(nb)      # new physical home of block b
+    pkg = load_package()
+    moved = pkg.PagedKVCache(1, nb, 16, 8, 128, dtype=torch.bfloat16, device=cuda)
+    p = torch.from_numpy(perm).to(cuda)
+    moved.key_cache[:, p] = cache.key_cache
+    moved.value_cache[:, p] = cache.value_cache
+    mcase = dict(case)
+    t = case["block_ids"].copy()
+    t[t >= 0] = perm[t[t >= 0]]
+    mcase["block_ids"] = t
+    out_b, lse_b = run_attention(mcase, cuda, cache=moved)
+    assert np.array_equal(out_a, out_b)
+    assert np.array_equal(lse_a, lse_b)
+
+
+def test_shared_prefix_blocks_give_identical_outputs(cuda):
+    """Config-5 style sharing: a 2048-token prefix mapped to the same 128 blocks.
+
+    Sequences 0 and 1 share the prefix blocks, have suffix blocks with equal
+    bytes and equal queries: their outputs must be bit-identical.
+    """
+    rng = np.random.default_rng(5)
+    B, bs, prefix_blocks = 8, 16, 128
+    suffix = rng.integers(64, 1025, size=B)
+    suffix[1] = suffix[0]
+    ctx = prefix_blocks * bs + suffix
+    nsuf = [-(-int(x) // bs) for x in suffix]
+    nb = prefix_blocks + sum(nsuf)
+    perm = rng.permutation(nb)
+    width = prefix_blocks + max(nsuf)
+    table = np.full((B, width), -1, dtype=np.int64)
+    o = prefix_blocks
+    for s in range(B):
+        table[s, :prefix_blocks] = perm[:prefix_blocks]
+        table[s, prefix_blocks:prefix_blocks + nsuf[s]] = perm[o:o + nsuf[s]]
+        o += nsuf[s]
+    case = build_paged_case(5, batch=B, heads=8, kv_heads=2, head_dim=128, block_size=bs,
+                            ctx=ctx, kv_kind="bf16", q_kind="bf16", num_blocks=nb)
+    case["block_ids"] = table
+    for j in range(nsuf[0]):
+        src, dst = table[0, prefix_blocks + j], table[1, prefix_blocks + j]
+        case["key_cache"][:, dst] = case["key_cache"][:, src]
+        case["value_cache"][:, dst] = case["value_cache"][:, src]
+    case["query"][1] = case["query"][0]
+    for mode in ("auto", "none"):
+        out, lse = run_attention(case, cuda, split_kv=mode != "none")
+        if mode == "none":
+            assert np.array_equal(out[0], out[1]) and np.array_equal(lse[0], lse[1])
+        want, want_lse = oracle(case)
+        assert_lowp_close(out, want, f"shared prefix {mode}")
+        assert_lse_close(lse, want_lse, f"shared prefix lse {mode}")
+
+
+def test_q_len_zero_and_empty_batch(cuda):
+    pkg = load_package()
+    cache = pkg.PagedKVCache(1, 4, 16, 2, 64, dtype=torch.bfloat16, device=cuda)
+    attn = pkg.PagedAttention(4, 2, 64)
+    q = torch.zeros(3, 4, 0, 64, dtype=torch.bfloat16, device=cuda)
+    table = torch.zeros(3, 1, dtype=torch.int32, device=cuda)
+    ctx = torch.ones(3, dtype=torch.long, device=cuda)
+    assert attn.forward(q, cache, 0, table, ctx).shape == (3, 4, 0, 64)
+    q = torch.zeros(0, 4, 1, 64, dtype=torch.bfloat16, device=cuda)
+    out = attn.forward(q, cache, 0, table[:0], ctx[:0], 1)
+    assert out.shape == (0, 4, 1, 64)
+
+
+def test_output_into_strided_view(cuda):
+    """Head-major output buffer (the multi-GPU all-gather layout)."""
+    case = build_paged_case(19, batch=3, heads=16, kv_heads=4, head_dim=128, block_size=16,
+                            ctx=[30, 300, 17], kv_kind="bf16", q_kind="bf16")
+    pkg = load_package()
+    cache = make_cache(case, cuda)
+    attn = pkg.PagedAttention(16, 4, 128)
+    q = to_dev(case["query"], "bf16", cuda)
+    table = torch.from_numpy(case["block_ids"]).to(cuda)
+    ctx = torch.from_numpy(case["context_lens"]).to(cuda)
+    head_major = torch.full((16, 3, 1, 128), float("nan"), dtype=torch.bfloat16, device=cuda)
+    attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False,
+                          out=head_major.permute(1, 0, 2, 3))
+    ref = attn.forward(q, cache, 0, table, ctx, 1)
+    assert torch.equal(head_major.permute(1, 0, 2, 3), ref)
