@@ -217,8 +217,10 @@ def test_shared_prefix_blocks_give_identical_outputs(cuda):
         table[s, :prefix_blocks] = perm[:prefix_blocks]
         table[s, prefix_blocks:prefix_blocks + nsuf[s]] = perm[o:o + nsuf[s]]
         o += nsuf[s]
+    # Build caches/query with a placeholder table, then install the sharing table.
     case = build_paged_case(5, batch=B, heads=8, kv_heads=2, head_dim=128, block_size=bs,
-                            ctx=ctx, kv_kind="bf16", q_kind="bf16", num_blocks=nb)
+                            ctx=[bs] * B, kv_kind="bf16", q_kind="bf16", num_blocks=nb)
+    case["context_lens"] = ctx
     case["block_ids"] = table
     for j in range(nsuf[0]):
         src, dst = table[0, prefix_blocks + j], table[1, prefix_blocks + j]
