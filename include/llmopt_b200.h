@@ -145,6 +145,38 @@ LLMOPT_API int llmopt_paged_attention_phase(const void* query, int32_t q_dtype, 
                            void* stream, int32_t phases);
 
 /*
+ * llmopt_paged_attention without a workspace argument.  No counterpart in the
+ * reference: it is an addition of this library for callers that cannot
+ * allocate device memory where they run attention - serving processes that
+ * give nearly all HBM to the KV block pool at start-up and may not allocate
+ * afterwards, and hosts calling this C ABI from other languages with no device
+ * allocator of their own.  Inputs and outputs are still the caller's.
+ *
+ * The split-K scratch is a fixed array of LLMOPT_NOALLOC_SCRATCH_BYTES compiled
+ * into the library, held in device memory by every GPU that loads it until the
+ * process exits.  The first call on a device looks up the array's address on
+ * that device (make that first call before any stream capture).  All calls on
+ * a device share the array and it keeps the last call's contents, so calls
+ * that may overlap on the GPU (other streams, other threads) race and must be
+ * serialised by the caller.  A shape needing more scratch than the array holds
+ * returns LLMOPT_ERR_WORKSPACE without launching anything.  The function never
+ * calls cudaMalloc, cudaFree or any other allocating routine.
+ */
+#define LLMOPT_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+LLMOPT_API int llmopt_paged_attention_noalloc(const void* query, int32_t q_dtype, int64_t q_s,
+                           int64_t q_h, int64_t q_t,
+                           const void* key_cache, const void* value_cache, int32_t kv_dtype,
+                           int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                           int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                           const void* block_table, int32_t table_is_i64, int64_t table_width,
+                           int64_t table_stride,
+                           const void* context_lens, int32_t ctx_is_i64,
+                           void* out, int32_t out_dtype, int64_t o_s, int64_t o_h, int64_t o_t,
+                           float* lse,
+                           int64_t batch, int32_t num_heads, int32_t q_len, float scale,
+                           float softcap, int64_t split_tokens, uint32_t* err, void* stream);
+
+/*
  * Exact log-sum-exp merge of two partial attention states.  Replaces
  * merge_states (paged_attention.py:30-55).  o1/o2/out are contiguous
  * [rows, head_dim] of o_dtype; l1/l2/lse_out contiguous [rows] of lse_dtype.

@@ -70,6 +70,10 @@ SIGNATURES = {
         _p, _i32, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
         _p, _i32, _i64, _i64, _p, _i32, _p, _i32, _i64, _i64, _i64, _p,
         _i64, _i32, _i32, _f32, _f32, _i64, _p, ctypes.c_size_t, _p, _p, _i32],
+    "llmopt_paged_attention_noalloc": [
+        _p, _i32, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+        _p, _i32, _i64, _i64, _p, _i32, _p, _i32, _i64, _i64, _i64, _p,
+        _i64, _i32, _i32, _f32, _f32, _i64, _p, _p],
     "llmopt_merge_states": [_p, _p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _p],
     "llmopt_kv_write": [
         _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -635,3 +635,123 @@ int llmopt_paged_gather(const void* key_cache, const void* value_cache, int32_t 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// llmopt_paged_attention_noalloc: paged attention whose split-K scratch is a
+// fixed array compiled into this library instead of caller-provided memory.
+//
+// It exists for callers that cannot allocate device memory at the point where
+// they run attention: serving processes that hand nearly all HBM to the KV
+// block pool at start-up (llmopt sizes the pool from gpu_memory_utilization)
+// and forbid allocations afterwards, and foreign-language hosts (C, Go, Java
+// through this C ABI) that have no device allocator of their own to carve a
+// workspace from.  The caller still passes every input and output.
+//
+// The scratch lives in device global memory: LLMOPT_NOALLOC_SCRATCH_BYTES per
+// GPU, held by every GPU that loads this code until the process exits.  Host
+// code must not use the array's name as a device address (in host code it is
+// only a stand-in); the address is looked up once per device with
+// cudaGetSymbolAddress, with that device current, by the first call on that
+// device - so make the first call on each device before any stream capture.
+// Every call on a device shares the one array and it keeps whatever the last
+// call left there: calls that can overlap on the GPU (different streams, or
+// several host threads) race on it and must be serialised by the caller.
+// Nothing in it has to start at zero: each call writes every scratch byte it
+// later reads.  Shapes whose scratch would exceed the array are rejected with
+// LLMOPT_ERR_WORKSPACE before anything is launched.  No cudaMalloc, cudaFree
+// or other allocating routine is called.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LLMOPT_NOALLOC_SCRATCH_BYTES];
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up once).
+int noalloc_scratch(int device, void** addr) {
+  if (device < 0 || device >= kNoAllocMaxDevices) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "device ordinal %d not supported", device);
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[device] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      return cuda_fail(e == cudaSuccess ? cudaErrorInvalidSymbol : e,
+                       "cudaGetSymbolAddress(scratch)");
+    }
+    g_noalloc_addr[device] = p;
+  }
+  *addr = g_noalloc_addr[device];
+  return LLMOPT_OK;
+}
+
+}  // namespace
+
+extern "C" int llmopt_paged_attention_noalloc(
+    const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h, int64_t q_t,
+    const void* key_cache, const void* value_cache, int32_t kv_dtype, int32_t num_layers,
+    int32_t num_blocks, int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+    int32_t layer_idx, const void* block_table, int32_t table_is_i64, int64_t table_width,
+    int64_t table_stride, const void* context_lens, int32_t ctx_is_i64, void* out,
+    int32_t out_dtype, int64_t o_s, int64_t o_h, int64_t o_t, float* lse, int64_t batch,
+    int32_t num_heads, int32_t q_len, float scale, float softcap, int64_t split_tokens,
+    uint32_t* err, void* stream) {
+  if (batch <= 0 || q_len <= 0) {
+    // Nothing to launch; the regular entry validates the remaining arguments.
+    return llmopt_paged_attention(query, q_dtype, q_s, q_h, q_t, key_cache, value_cache,
+                                  kv_dtype, num_layers, num_blocks, block_size, num_kv_heads,
+                                  head_dim, layer_idx, block_table, table_is_i64, table_width,
+                                  table_stride, context_lens, ctx_is_i64, out, out_dtype, o_s,
+                                  o_h, o_t, lse, batch, num_heads, q_len, scale, softcap,
+                                  split_tokens, nullptr, 0, err, stream);
+  }
+  if (num_heads < 1 || num_kv_heads < 1 || num_heads % num_kv_heads != 0 || head_dim < 1 ||
+      block_size < 1 || table_width < 0) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
+  }
+  if (!valid_dtype(q_dtype) || !valid_dtype(kv_dtype) || !valid_dtype(out_dtype)) {
+    return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype (q=%d kv=%d out=%d)", q_dtype,
+                kv_dtype, out_dtype);
+  }
+  // Size the scratch for the plan the regular entry will pick, and refuse
+  // shapes that do not fit before anything is launched.
+  AttnArgs a{};
+  a.q_dtype = q_dtype;
+  a.k_cache = key_cache;
+  a.v_cache = value_cache;
+  a.kv_dtype = kv_dtype;
+  a.num_layers = num_layers;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.table_width = table_width;
+  a.batch = batch;
+  a.num_heads = num_heads;
+  a.q_len = q_len;
+  a.group = num_heads / num_kv_heads;
+  a.rows = q_len * a.group;
+  const int device = current_device();
+  Choice c;
+  int st = choose(a, split_tokens, device, false, &c);
+  if (st != LLMOPT_OK) return st;
+  const long long need = layout_for(batch, c.plan.slots, num_heads, q_len, head_dim).total;
+  if (need > (long long)LLMOPT_NOALLOC_SCRATCH_BYTES) {
+    return fail(LLMOPT_ERR_WORKSPACE,
+                "llmopt_paged_attention_noalloc: this shape needs %lld bytes of split-K scratch "
+                "but the built-in scratch holds %lld; use llmopt_paged_attention with a "
+                "caller-provided workspace, or fewer sequences/splits per call",
+                need, (long long)LLMOPT_NOALLOC_SCRATCH_BYTES);
+  }
+  void* scratch = nullptr;
+  st = noalloc_scratch(device, &scratch);
+  if (st != LLMOPT_OK) return st;
+  return llmopt_paged_attention(query, q_dtype, q_s, q_h, q_t, key_cache, value_cache, kv_dtype,
+                                num_layers, num_blocks, block_size, num_kv_heads, head_dim,
+                                layer_idx, block_table, table_is_i64, table_width, table_stride,
+                                context_lens, ctx_is_i64, out, out_dtype, o_s, o_h, o_t, lse,
+                                batch, num_heads, q_len, scale, softcap, split_tokens, scratch,
+                                (size_t)LLMOPT_NOALLOC_SCRATCH_BYTES, err, stream);
+}
