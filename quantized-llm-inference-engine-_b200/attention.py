@@ -181,8 +181,15 @@ class PagedAttention:
             cache._check_storage()
         else:
             layer = layer_idx % cache.num_layers
+        out_dtype = query.dtype if query.dtype in rt.DTYPE_CODE else torch.float32
         if query.device != device:
             query = query.to(device)
+        if q_len * self.group_size > 16 and cache.key_cache.dtype in (torch.bfloat16, torch.float16):
+            # Chunked prefill runs on tensor-core tiles whose operands share one
+            # 16-bit type: round the query to the cache dtype first, which is what
+            # the reference does (q.to(k.dtype), paged_attention.py:242), and hand
+            # the tile loader a dense query.
+            query = query.to(cache.key_cache.dtype).contiguous()
         if query.dtype not in rt.DTYPE_CODE:
             query = query.to(torch.float32)
         if query.stride(-1) != 1:
@@ -192,7 +199,7 @@ class PagedAttention:
         if table.dim() != 2 or table.shape[0] < seq_len or ctx.shape[0] < seq_len:
             raise ValueError("block_ids must be [seq, max_blocks] and context_lens [seq]")
         if out is None:
-            out = torch.empty((seq_len, self.num_heads, q_len, self.head_dim), dtype=query.dtype,
+            out = torch.empty((seq_len, self.num_heads, q_len, self.head_dim), dtype=out_dtype,
                               device=device)
         elif out.shape != (seq_len, self.num_heads, q_len, self.head_dim) or out.stride(-1) != 1:
             raise ValueError("out must be [seq, num_heads, q_len, head_dim] with unit inner stride")

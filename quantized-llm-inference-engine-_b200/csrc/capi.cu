@@ -132,6 +132,37 @@ bool kv_tensor_map(const void* base, int dtype, int layers, int num_blocks, int 
   return true;
 }
 
+// Per-call descriptor of the query for the prefill kernel: (head_dim, q_len,
+// num_heads, batch), box (64, 128 / group tokens, group heads, 1).
+bool query_tensor_map(const AttnArgs& a, CUtensorMap* out, std::string* why) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) {
+    *why = "cuTensorMapEncodeTiled unavailable";
+    return false;
+  }
+  const cuuint64_t es = 2;
+  cuuint64_t dims[4] = {(cuuint64_t)a.head_dim, (cuuint64_t)a.q_len, (cuuint64_t)a.num_heads,
+                        (cuuint64_t)a.batch};
+  cuuint64_t strides[3] = {es * (cuuint64_t)a.q_t, es * (cuuint64_t)a.q_h,
+                           es * (cuuint64_t)a.q_s};
+  cuuint32_t box[4] = {64, (cuuint32_t)(kPrefillRows / a.group), (cuuint32_t)a.group, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  std::memset(out, 0, sizeof(*out));
+  CUresult r = encode(out,
+                      a.q_dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                      4, const_cast<void*>(a.q), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[96];
+    snprintf(buf, sizeof(buf), "query cuTensorMapEncodeTiled failed (%d)", (int)r);
+    *why = buf;
+    return false;
+  }
+  return true;
+}
+
 // ---- split planning and workspace layout ------------------------------------------
 constexpr long long kAlign = 256;
 constexpr int kMaxBalancedCtasPerSm = 8;
@@ -183,15 +214,35 @@ SplitPlan generic_auto_plan(long long batch, long long width, int kv_heads, int 
 }
 
 struct Choice {
-  bool tma = false;
+  bool tma = false;      // decode_tma_kernel + combine
+  bool prefill = false;  // prefill_tc_kernel (no combine)
   DecodeLaunch launch{};
   SplitPlan plan{};
-  CUtensorMap tmk, tmv;
+  CUtensorMap tmk, tmv, tmq;
 };
 
 // Pick the kernel and split plan.  Returns LLMOPT_OK or an error code.
 int choose(AttnArgs& a, long long split_tokens, int device, bool encode_maps, Choice* c) {
   const int sms = sm_count_of(device);
+  // Dense chunked prefill: tensor-core tiles over whole sequences, no split-K.
+  if (prefill_tc_supported(a)) {
+    bool maps = true;
+    if (encode_maps) {
+      std::string why;
+      maps = query_tensor_map(a, &c->tmq, &why) &&
+             kv_tensor_map(a.k_cache, a.kv_dtype, a.num_layers, a.num_blocks, a.block_size,
+                           a.kv_heads, a.head_dim, &c->tmk, &why) &&
+             kv_tensor_map(a.v_cache, a.kv_dtype, a.num_layers, a.num_blocks, a.block_size,
+                           a.kv_heads, a.head_dim, &c->tmv, &why);
+    }
+    if (maps) {
+      c->prefill = true;
+      c->tma = false;
+      c->plan = fixed_plan(a.batch, a.table_width, a.table_width);
+      c->plan.slots = 0;
+      return LLMOPT_OK;
+    }
+  }
   // Fast path first: it supports the balanced plan (auto) and fixed plans.
   AttnArgs probe = a;
   if (split_tokens == LLMOPT_SPLIT_AUTO && a.batch <= kMaxBalancedBatch) {
@@ -417,11 +468,16 @@ int llmopt_paged_attention_phase(const void* query, int32_t q_dtype, int64_t q_s
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (phases & LLMOPT_PHASE_SPLIT) {
-    cudaError_t e =
-        c.tma ? decode_tma_launch(a, c.launch, c.tmk, c.tmv, s) : generic_launch(a, s);
-    if (e != cudaSuccess) return cuda_fail(e, c.tma ? "decode_tma launch" : "generic launch");
+    cudaError_t e = c.prefill ? prefill_tc_launch(a, c.tmq, c.tmk, c.tmv, s)
+                    : c.tma   ? decode_tma_launch(a, c.launch, c.tmk, c.tmv, s)
+                              : generic_launch(a, s);
+    if (e != cudaSuccess) {
+      return cuda_fail(e, c.prefill ? "prefill_tc launch"
+                          : c.tma   ? "decode_tma launch"
+                                    : "generic launch");
+    }
   }
-  if (phases & LLMOPT_PHASE_COMBINE) {
+  if ((phases & LLMOPT_PHASE_COMBINE) && !c.prefill) {
     cudaError_t e = combine_launch(a, s);
     if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   }
@@ -718,6 +774,10 @@ extern "C" int llmopt_paged_attention_noalloc(
   // Size the scratch for the plan the regular entry will pick, and refuse
   // shapes that do not fit before anything is launched.
   AttnArgs a{};
+  a.q = query;
+  a.q_s = q_s;
+  a.q_h = q_h;
+  a.q_t = q_t;
   a.q_dtype = q_dtype;
   a.k_cache = key_cache;
   a.v_cache = value_cache;

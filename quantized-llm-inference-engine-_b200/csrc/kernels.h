@@ -58,6 +58,14 @@ cudaError_t decode_tma_launch(const AttnArgs& a, const DecodeLaunch& launch,
                               const CUtensorMap& tmk, const CUtensorMap& tmv,
                               cudaStream_t stream);
 
+// Chunked prefill on tcgen05 tensor cores (q_len * group > 16, 16-bit cache and
+// query of the same dtype, head_dim 64/128, block_size 16).  Writes the final
+// output and LSE itself: no split partials, no combine.
+bool prefill_tc_supported(const AttnArgs& a);
+cudaError_t prefill_tc_launch(const AttnArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
+                              const CUtensorMap& tmv, cudaStream_t stream);
+constexpr int kPrefillRows = 128;  // query rows per prefill CTA
+
 // Generic path: any dtype / head_dim <= 256 / block size / q_len (CUDA cores).
 constexpr int kGenericRowTile = 16;
 constexpr int kGenericKeyTile = 32;

@@ -1,0 +1,486 @@
+// Chunked-prefill paged attention on the 5th-generation tensor cores (sm_100a).
+//
+// Replaces PagedAttention.forward for q_len > 1 (src/llmopt/attention/
+// paged_attention.py:146-250: gather, h // group expansion, causal mask
+// k_pos <= ctx - q_len + i, softmax, P V) when the query rows of one KV head
+// form a real dense contraction (q_len * group > 16) on a 16-bit cache.
+//
+// One CTA owns 128 query rows of one (sequence, KV head): kTQ = 128 / group
+// consecutive chunk tokens x the group's query heads, rows ordered
+// [head][token].  It walks that sequence's keys in tiles of 128 (8 KV blocks
+// of 16 tokens) up to the causal limit of its last row:
+//
+//   TMA warp   Q once (4-D tensor map over the query), then per key tile the
+//              8 blocks' K and V rows through the block table (5-D map over the
+//              cache, one 16-token box per block and 64-dim slice), into a
+//              2-stage ring.  -1 table entries are not loaded.
+//   MMA warp   one thread issues tcgen05.mma kind::f16: S = Q K^T (M=128,
+//              N=128, K=head_dim) into tensor memory, then O += P V (N=head_dim,
+//              K=128 keys) with P from shared memory and V as an MN-major
+//              operand.  Commits signal the softmax warps and free the stage.
+//   softmax    4 warps, one thread per row (= TMEM lane): tcgen05.ld of the S
+//              row, mask (block validity, context, causal), online softmax in
+//              fp32 with a lazy running max (O in TMEM is rescaled only when the
+//              row max grows by more than 2^8, which keeps every exp <= 256),
+//              P written as bf16/fp16 into a 128B-swizzled K-major tile.
+//   epilogue   O / l from TMEM to the output, plus the natural-log LSE.
+//
+// Stale rows (unloaded blocks, slots past the context) are zeroed in V before
+// P V so that a zero probability never meets an Inf/NaN.  Every wait is
+// bounded; tensor memory is released before the CTA exits.
+#include <float.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc_common.cuh"
+
+namespace llmopt {
+namespace {
+
+constexpr int kBS = 16;
+constexpr int kM = 128;                  // query rows per CTA = TMEM lanes
+constexpr int kN = 128;                  // keys per tile
+constexpr int kBlocksPerTile = kN / kBS;
+constexpr int kStages = 2;
+constexpr int kSoftmaxWarps = 4;
+constexpr int kTmaWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kThreads = 6 * 32;
+constexpr int kTile = kM * 128;          // one [128 rows x 128 B] swizzled sub-tile (16 KB)
+constexpr int kBlockBytes = kBS * 128;   // one 16-row box (2 KB)
+constexpr float kRescaleLog2 = 8.0f;
+constexpr uint32_t kTmemCols = 256;      // S: 128 columns, O: head_dim (<= 128) columns
+
+template <int D>
+struct Layout {
+  static constexpr int kSubs = D / 64;
+  static constexpr int kQ = 0;
+  static constexpr int kK = kQ + kSubs * kTile;
+  static constexpr int kV = kK + kStages * kSubs * kTile;
+  static constexpr int kP = kV + kStages * kSubs * kTile;
+  static constexpr int kBar = kP + 2 * kTile;
+  static constexpr int kBytes = kBar + 128;
+};
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t kv_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t s_full;
+  uint64_t p_full;
+  uint64_t o_done;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void wait_or_flag(uint64_t* bar, unsigned parity, unsigned* err) {
+  if (!mbar_wait(bar, parity)) record_error(err, kErrWaitTimeout);
+}
+
+// Valid-block bits of key tile j (bit i: block j*8+i is loaded) for one sequence.
+__device__ __forceinline__ unsigned tile_blocks(const AttnArgs& a, long long s, int j,
+                                                long long n_keys, unsigned* err, bool flag) {
+  unsigned bits = 0;
+#pragma unroll
+  for (int i = 0; i < kBlocksPerTile; ++i) {
+    const long long b = (long long)j * kBlocksPerTile + i;
+    if (b * kBS >= n_keys) break;
+    const long long id = load_index(a.table, a.table_i64, s * a.table_stride + b);
+    if (id >= 0 && id < a.num_blocks) {
+      bits |= 1u << i;
+    } else if (id >= a.num_blocks && flag) {
+      record_error(err, kErrBlockId);
+    }
+  }
+  return bits;
+}
+
+template <int D, int KV_DT>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq,
+                      const __grid_constant__ CUtensorMap tmk,
+                      const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
+  using L = Layout<D>;
+  constexpr int kSubs = L::kSubs;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int group = a.group;
+  const int tq = kM / group;                          // chunk tokens per CTA
+  const int qtiles = (a.q_len + tq - 1) / tq;
+  const long long x = blockIdx.x;
+  const long long s = x / ((long long)a.kv_heads * qtiles);
+  const int rem = (int)(x - s * (long long)a.kv_heads * qtiles);
+  const int kh = rem / qtiles;
+  const int t0 = (rem - kh * qtiles) * tq;
+
+  const long long ctx_s = load_index(a.ctx, a.ctx_i64, s);
+  const int t_end = t0 + tq < a.q_len ? t0 + tq : a.q_len;
+  const long long max_qpos = ctx_s - a.q_len + t_end - 1;
+  long long n_keys = max_qpos + 1 < ctx_s ? max_qpos + 1 : ctx_s;
+  if (n_keys > a.table_width * kBS) n_keys = a.table_width * kBS;
+  if (n_keys < 0) n_keys = 0;
+  const int n_tiles = (int)((n_keys + kN - 1) / kN);
+  if (rem == 0 && threadIdx.x == 0 && ctx_s > a.table_width * kBS) {
+    record_error(a.err, kErrTableWidth);
+  }
+
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(sm + L::kBar);
+  unsigned char* sQ = sm + L::kQ;
+  unsigned char* sK = sm + L::kK;
+  unsigned char* sV = sm + L::kV;
+  unsigned char* sP = sm + L::kP;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&bars->kv_full[i], 1);
+      mbar_init(&bars->kv_empty[i], 1);
+    }
+    mbar_init(&bars->s_full, 1);
+    mbar_init(&bars->p_full, kSoftmaxWarps * 32);
+    mbar_init(&bars->o_done, 1);
+    mbar_init_fence();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(&bars->tmem_base, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = bars->tmem_base;
+  const uint32_t tmem_s = tmem;
+  const uint32_t tmem_o = tmem + kN;
+
+  if (warp == kTmaWarp) {
+    // ------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      prefetch_tensormap(&tmq);
+      prefetch_tensormap(&tmk);
+      prefetch_tensormap(&tmv);
+      mbar_arrive_expect_tx(&bars->q_full, (unsigned)(kSubs * kTile));
+#pragma unroll
+      for (int sub = 0; sub < kSubs; ++sub) {
+        tc::tma_load_4d(sQ + sub * kTile, &tmq, &bars->q_full, sub * 64, t0, kh * group,
+                        (int)s);
+      }
+    }
+    for (int j = 0; j < n_tiles; ++j) {
+      const int st = j % kStages;
+      if (j >= kStages && lane == 0) {
+        wait_or_flag(&bars->kv_empty[st], (unsigned)((j / kStages - 1) & 1), a.err);
+      }
+      __syncwarp();
+      int id = 0;
+      bool valid = false;
+      if (lane < kBlocksPerTile) {
+        const long long b = (long long)j * kBlocksPerTile + lane;
+        if (b * kBS < n_keys) {
+          const long long raw = load_index(a.table, a.table_i64, s * a.table_stride + b);
+          if (raw >= 0 && raw < a.num_blocks) {
+            valid = true;
+            id = (int)raw;
+          } else if (raw >= a.num_blocks) {
+            record_error(a.err, kErrBlockId);
+          }
+        }
+      }
+      const unsigned mask = __ballot_sync(0xffffffffu, valid);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars->kv_full[st],
+                              (unsigned)(__popc(mask) * kSubs * 2 * kBlockBytes));
+      }
+      __syncwarp();
+      if (valid) {
+        unsigned char* kdst = sK + st * kSubs * kTile + lane * kBlockBytes;
+        unsigned char* vdst = sV + st * kSubs * kTile + lane * kBlockBytes;
+#pragma unroll
+        for (int sub = 0; sub < kSubs; ++sub) {
+          tma_load_5d(kdst + sub * kTile, &tmk, &bars->kv_full[st], sub * 64, kh, 0, id,
+                      a.layer);
+          tma_load_5d(vdst + sub * kTile, &tmv, &bars->kv_full[st], sub * 64, kh, 0, id,
+                      a.layer);
+        }
+      }
+    }
+    if (lane == 0) {
+      // Drain: no copy may still target this CTA's shared memory at exit.
+      wait_or_flag(&bars->q_full, 0, a.err);
+      const int first = n_tiles > kStages ? n_tiles - kStages : 0;
+      for (int j = first; j < n_tiles; ++j) {
+        wait_or_flag(&bars->kv_full[j % kStages], (unsigned)((j / kStages) & 1), a.err);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------- MMA issuer
+    const bool bf16 = KV_DT == kBF16;
+    const uint32_t idesc_qk = tc::instr_desc_f16(bf16, kM, kN, false, false);
+    const uint32_t idesc_pv = tc::instr_desc_f16(bf16, kM, D, false, true);
+    const uint32_t q_addr = smem_addr(sQ);
+    const uint32_t p_addr = smem_addr(sP);
+
+    // Zero V rows of tile j that hold no valid key (unloaded block / past ctx).
+    auto prepare_v = [&](int j) {
+      const int st = j % kStages;
+      const unsigned bits = tile_blocks(a, s, j, n_keys, a.err, false);
+      unsigned char* v = sV + st * kSubs * kTile;
+      for (int i = 0; i < kBlocksPerTile; ++i) {
+        const long long b = (long long)j * kBlocksPerTile + i;
+        int first_bad = 0;                       // rows [first_bad, 16) are zeroed
+        if ((bits >> i) & 1u) {
+          const long long left = ctx_s - b * kBS;
+          first_bad = left >= kBS ? kBS : (int)(left > 0 ? left : 0);
+        }
+        const int nbad = kBS - first_bad;
+        if (nbad == 0) continue;
+        for (int e = lane; e < nbad * kSubs * 8; e += 32) {
+          const int r = first_bad + e / (kSubs * 8);
+          const int rest = e % (kSubs * 8);
+          const int sub = rest >> 3;
+          const int ch = rest & 7;
+          *reinterpret_cast<uint4*>(v + sub * kTile + (i * kBS + r) * 128 + ch * 16) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+    };
+    auto issue_qk = [&](int j) {
+      const int st = j % kStages;
+      const uint32_t k_addr = smem_addr(sK + st * kSubs * kTile);
+      if (lane == 0) {
+        tc::fence_after_sync();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kTile + (kk & 3) * 32;
+          tc::mma_f16(tmem_s, tc::smem_desc_sw128(q_addr + off, 16, 1024),
+                      tc::smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc::commit(&bars->s_full);
+      }
+      __syncwarp();
+    };
+    auto issue_pv = [&](int j) {
+      const int st = j % kStages;
+      const uint32_t v_addr = smem_addr(sV + st * kSubs * kTile);
+      if (lane == 0) {
+        tc::fence_after_sync();
+#pragma unroll
+        for (int kk = 0; kk < kN / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * kTile + (kk & 3) * 32;
+          tc::mma_f16(tmem_o, tc::smem_desc_sw128(p_addr + a_off, 16, 1024),
+                      tc::smem_desc_sw128(v_addr + kk * 16 * 128, kTile, 1024), idesc_pv,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::commit(&bars->o_done);
+        tc::commit(&bars->kv_empty[st]);
+      }
+      __syncwarp();
+    };
+
+    if (n_tiles > 0) {
+      wait_or_flag(&bars->q_full, 0, a.err);
+      wait_or_flag(&bars->kv_full[0], 0, a.err);
+      prepare_v(0);
+      issue_qk(0);
+      for (int j = 0; j < n_tiles; ++j) {
+        wait_or_flag(&bars->p_full, (unsigned)(j & 1), a.err);
+        if (j + 1 < n_tiles) {
+          wait_or_flag(&bars->kv_full[(j + 1) % kStages], (unsigned)(((j + 1) / kStages) & 1),
+                       a.err);
+          prepare_v(j + 1);
+          issue_qk(j + 1);
+        }
+        issue_pv(j);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- softmax + epilogue
+    const int r = threadIdx.x;                 // row = TMEM lane
+    const int g = r / tq;
+    const int t = r - g * tq;
+    const int tok = t0 + t;
+    const bool row_valid = tok < a.q_len;
+    const long long qpos = ctx_s - a.q_len + tok;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float scale_log2 = a.scale * kLog2e;
+    const bool capped = a.softcap > 0.f;
+    float m_used = -INFINITY;
+    float l = 0.f;
+
+    for (int j = 0; j < n_tiles; ++j) {
+      const unsigned bits = tile_blocks(a, s, j, n_keys, a.err, false);
+      wait_or_flag(&bars->s_full, (unsigned)(j & 1), a.err);
+      tc::fence_after_sync();
+      float sv[kN];
+#pragma unroll
+      for (int c = 0; c < kN / 32; ++c) {
+        float tmp[32];
+        tc::tmem_ld32(tmem_s + lane_off + c * 32, tmp);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = tmp[i];
+      }
+      tc::tmem_wait_ld();
+      const long long kbase = (long long)j * kN;
+      float rowmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kN; ++c) {
+        const long long kpos = kbase + c;
+        const bool ok = ((bits >> (c / kBS)) & 1u) && kpos < ctx_s && kpos <= qpos;
+        float xv = sv[c];
+        xv = capped ? tanhf(xv * a.scale / a.softcap) * (a.softcap * kLog2e) : xv * scale_log2;
+        sv[c] = ok ? xv : -INFINITY;
+        rowmax = fmaxf(rowmax, sv[c]);
+      }
+      const float m_new = rowmax > m_used + kRescaleLog2 ? rowmax : m_used;
+      const float m_sub = m_new == -INFINITY ? 0.f : m_new;
+      float rowsum = 0.f;
+      uint32_t pk[kN / 2];
+#pragma unroll
+      for (int c = 0; c < kN; c += 2) {
+        const float p0 = fast_exp2(sv[c] - m_sub);
+        const float p1 = fast_exp2(sv[c + 1] - m_sub);
+        rowsum += p0 + p1;
+        pk[c / 2] = pack2<KV_DT>(p0, p1);
+      }
+      if (j > 0) {
+        wait_or_flag(&bars->o_done, (unsigned)((j - 1) & 1), a.err);
+        tc::fence_after_sync();
+        if (m_new != m_used && m_used != -INFINITY) {
+          const float alpha = fast_exp2(m_used - m_new);
+          l *= alpha;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float o[32];
+            tc::tmem_ld32(tmem_o + lane_off + c * 32, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tc::tmem_st32(tmem_o + lane_off + c * 32, o);
+          }
+          tc::tmem_wait_st();
+        }
+      }
+      m_used = m_new;
+      l += rowsum;
+      // P row r into the 128B-swizzled K-major tile (keys 0-63 | 64-127).
+      unsigned char* prow = sP + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < kN / 8; ++c) {
+        const int sub = c >> 3;
+        const int ch = c & 7;
+        *reinterpret_cast<uint4*>(prow + sub * kTile + ((ch ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc::fence_before_sync();
+      mbar_arrive(&bars->p_full);
+    }
+
+    if (n_tiles > 0) {
+      wait_or_flag(&bars->o_done, (unsigned)((n_tiles - 1) & 1), a.err);
+      tc::fence_after_sync();
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const int qh = kh * group + g;
+    const long long obase = s * a.o_s + (long long)qh * a.o_h + (long long)tok * a.o_t;
+    const bool vec_out = a.out_dtype == KV_DT &&
+                         (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && a.o_s % 8 == 0 &&
+                         a.o_h % 8 == 0 && a.o_t % 8 == 0;
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      float o[32];
+      tc::tmem_ld32(tmem_o + lane_off + c * 32, o);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = l > 0.f ? o[i] * inv : 0.f;
+      if (row_valid) {
+        if (vec_out) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            const uint4 w = make_uint4(pack2<KV_DT>(o[i], o[i + 1]), pack2<KV_DT>(o[i + 2], o[i + 3]),
+                                       pack2<KV_DT>(o[i + 4], o[i + 5]), pack2<KV_DT>(o[i + 6], o[i + 7]));
+            *reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.out) +
+                                      (obase + c * 32 + i) * 2) = w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (a.out_dtype == kF32) store_f32<kF32>(a.out, obase + c * 32 + i, o[i]);
+            else if (a.out_dtype == kF16) store_f32<kF16>(a.out, obase + c * 32 + i, o[i]);
+            else store_f32<kBF16>(a.out, obase + c * 32 + i, o[i]);
+          }
+        }
+      }
+    }
+    if (row_valid && a.lse != nullptr) {
+      a.lse[(s * a.num_heads + qh) * a.q_len + tok] =
+          l > 0.f ? (m_used + log2f(l)) * kLn2 : -INFINITY;
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int D, int KV_DT>
+const void* prefill_ptr() {
+  return reinterpret_cast<const void*>(&prefill_tc_kernel<D, KV_DT>);
+}
+
+const void* select_prefill(const AttnArgs& a) {
+  if (a.head_dim == 128 && a.kv_dtype == kBF16) return prefill_ptr<128, kBF16>();
+  if (a.head_dim == 128 && a.kv_dtype == kF16) return prefill_ptr<128, kF16>();
+  if (a.head_dim == 64 && a.kv_dtype == kBF16) return prefill_ptr<64, kBF16>();
+  if (a.head_dim == 64 && a.kv_dtype == kF16) return prefill_ptr<64, kF16>();
+  return nullptr;
+}
+
+size_t prefill_smem(int head_dim) {
+  return (head_dim == 128 ? Layout<128>::kBytes : Layout<64>::kBytes) + 1024;
+}
+
+}  // namespace
+
+bool prefill_tc_supported(const AttnArgs& a) {
+  if (a.kv_dtype != kBF16 && a.kv_dtype != kF16) return false;
+  if (a.q_dtype != a.kv_dtype) return false;           // both MMA operands share a type
+  if (a.block_size != kBS) return false;
+  if (a.head_dim != 64 && a.head_dim != 128) return false;
+  if (a.rows <= 16) return false;                       // the decode kernel covers these
+  if (a.group < 1 || a.group > kM || kM % a.group != 0) return false;
+  // Query tensor map: 16-byte aligned base and strides, unit innermost stride.
+  const uintptr_t qp = reinterpret_cast<uintptr_t>(a.q);
+  if ((qp & 15) || (a.q_t * 2) % 16 || (a.q_h * 2) % 16 || (a.q_s * 2) % 16) return false;
+  if (a.q_t < a.head_dim || a.q_h < 1 || a.q_s < 1) return false;
+  if ((reinterpret_cast<uintptr_t>(a.k_cache) & 15) || (reinterpret_cast<uintptr_t>(a.v_cache) & 15))
+    return false;
+  if ((long long)a.num_blocks * kBS > 0x7fffffffLL) return false;
+  if (a.batch > 0x7fffffffLL) return false;
+  return select_prefill(a) != nullptr;
+}
+
+cudaError_t prefill_tc_launch(const AttnArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
+                              const CUtensorMap& tmv, cudaStream_t stream) {
+  const void* fn = select_prefill(a);
+  if (fn == nullptr) return cudaErrorInvalidValue;
+  const size_t smem = prefill_smem(a.head_dim);
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int tq = kM / a.group;
+  const long long qtiles = (a.q_len + tq - 1) / tq;
+  const long long grid = a.batch * a.kv_heads * qtiles;
+  if (grid <= 0) return cudaSuccess;
+  if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  void* args[] = {const_cast<CUtensorMap*>(&tmq), const_cast<CUtensorMap*>(&tmk),
+                  const_cast<CUtensorMap*>(&tmv), const_cast<AttnArgs*>(&a)};
+  return cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kThreads), args, smem, stream);
+}
+
+}  // namespace llmopt
