@@ -60,6 +60,10 @@ def parse_args(argv=None):
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--config", choices=("c2", "c3", "c4", "c5"), default="c2",
+                   help="c2 (default, the headline line): Llama-3-8B decode; c3: chunked "
+                        "prefill; c4: 128k-context decode sharded by KV head (strong "
+                        "scaling); c5: shared-prefix decode (strong scaling)")
     return p.parse_args(argv)
 
 
@@ -486,10 +490,183 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# secondary configs (c3 prefill, c4 long context, c5 shared prefix)
+# ---------------------------------------------------------------------------
+
+def _tables_from_counts(rng, nblk, num_blocks, shared=None):
+    """Tables over a permuted pool; ``shared`` = ids every row starts with."""
+    perm = rng.permutation(num_blocks)
+    o = 0
+    lead = [] if shared is None else list(shared)
+    if shared is not None:
+        perm = np.setdiff1d(perm, np.asarray(shared), assume_unique=True)
+        perm = rng.permutation(perm)
+    width = int(max(nblk)) + len(lead)
+    table = np.full((len(nblk), width), -1, dtype=np.int32)
+    for s, n in enumerate(nblk):
+        table[s, :len(lead)] = lead
+        table[s, len(lead):len(lead) + n] = perm[o:o + n]
+        o += int(n)
+    return table
+
+
+def extra_workload(args, world: int) -> dict:
+    rng = np.random.default_rng(args.seed + {"c3": 3, "c4": 4, "c5": 5}[args.config])
+    if args.config == "c3":
+        B, q_len, H, KVH = 16, 256, 32, 8
+        prefix = (rng.integers(0, 4097, size=B) // BLOCK) * BLOCK
+        ctx = prefix + q_len
+        nblk = (ctx + BLOCK - 1) // BLOCK
+        nb = int(nblk.sum() * 1.10) + 1
+        return dict(kind="prefill", batch=B, q_len=q_len, heads=H, kv_heads=KVH, ctx=ctx,
+                    offsets=prefix, table=_tables_from_counts(rng, nblk, nb), num_blocks=nb,
+                    scaling="weak", note="B16 x 256-token chunks, prefix U[0,4096] block-aligned")
+    if args.config == "c4":
+        B, H, KVH = 4, 64, 8
+        ctx = np.full(B, 131072, dtype=np.int64)
+        nblk = ctx // BLOCK
+        nb = int(nblk.sum() * 1.10) + 1
+        return dict(kind="decode", batch=B, q_len=1, heads=H, kv_heads=KVH, ctx=ctx,
+                    offsets=ctx - 1, table=_tables_from_counts(rng, nblk, nb), num_blocks=nb,
+                    scaling="strong", note="B4 x 131072 context, 64 q / 8 KV heads")
+    B, H, KVH, shared_blocks = 256, 32, 8, 128
+    suffix = rng.integers(64, 1025, size=B)
+    ctx = shared_blocks * BLOCK + suffix
+    nsuf = (suffix + BLOCK - 1) // BLOCK
+    nb = int((shared_blocks + nsuf.sum()) * 1.10) + 1
+    shared = rng.choice(nb, size=shared_blocks, replace=False)
+    table = _tables_from_counts(rng, nsuf, nb, shared=shared)
+    return dict(kind="decode", batch=B, q_len=1, heads=H, kv_heads=KVH, ctx=ctx,
+                offsets=ctx - 1, table=table, num_blocks=nb, scaling="strong",
+                unique_tokens=int(shared_blocks * BLOCK + suffix.sum()),
+                note="B256, 2048-token prefix on 128 shared blocks + private U[64,1024]")
+
+
+def run_extra(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    pkg = importlib.import_module(PACKAGE)
+    pdist = importlib.import_module(f"{PACKAGE}.dist")
+    from oracle.paged_oracle import decode_bytes, prefill_flops
+
+    wl = extra_workload(args, world)
+    B, H, KVH, q_len = wl["batch"], wl["heads"], wl["kv_heads"], wl["q_len"]
+    shard = pdist.shard_heads(H, KVH, world, rank)
+    kvh, qh = shard.kv_heads, shard.q_heads
+    cache = pkg.PagedKVCache(1, wl["num_blocks"], BLOCK, kvh, HEAD_DIM, dtype=torch.bfloat16,
+                             device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000 + rank)
+    for t in (cache.key_cache, cache.value_cache):
+        for i in range(0, t.shape[1], 4096):
+            sl = t[:, i:i + 4096]
+            sl.copy_(torch.randn(sl.shape, generator=g, device=dev))
+    table = torch.from_numpy(wl["table"]).to(dev)
+    ctx = torch.from_numpy(wl["ctx"]).to(dev)
+    offs = torch.from_numpy(np.asarray(wl["offsets"], dtype=np.int64)).to(dev)
+    q = torch.randn((B, qh, q_len, HEAD_DIM), generator=g, device=dev).to(torch.bfloat16)
+    shape_new = (B, q_len, kvh, HEAD_DIM) if wl["kind"] == "prefill" else (B, kvh, HEAD_DIM)
+    knew = torch.randn(shape_new, generator=g, device=dev).to(torch.bfloat16)
+    vnew = torch.randn(shape_new, generator=g, device=dev).to(torch.bfloat16)
+    attn = pkg.PagedAttention(qh, kvh, HEAD_DIM)
+    head_major = torch.empty((qh, B, q_len, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    out_view = head_major.permute(1, 0, 2, 3)
+    gathered = (torch.empty((H, B, q_len, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+                if world > 1 else None)
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record()
+        if wl["kind"] == "prefill":
+            cache.write(0, table, offs, knew, vnew)
+        else:
+            cache.write_decode(0, table, offs, knew, vnew)
+        if ev is not None:
+            ev[1].record()
+        attn.forward_with_lse(q, cache, 0, table, ctx, q_len, want_lse=False, out=out_view)
+        if ev is not None:
+            ev[2].record()
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, head_major)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    start.record()
+    for i in range(args.steps):
+        step(evs[i])
+    end.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    append_ms = statistics.fmean(e[0].elapsed_time(e[1]) for e in evs)
+    attn_ms = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
+    if rank == 0:
+        line = {"config": args.config, "workload": wl["note"], "n_gpus": world,
+                "scaling": wl["scaling"], "steps": args.steps, "ms_per_step": round(ms_step, 5),
+                "append_ms": round(append_ms, 5), "attention_ms": round(attn_ms, 5),
+                "clocks": clocks}
+        if wl["kind"] == "prefill":
+            flops = prefill_flops(wl["ctx"] - q_len, q_len, H, HEAD_DIM)
+            app = B * q_len * KVH * HEAD_DIM * 2 * 4
+            peak = 1705.1
+            try:
+                with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+                    peak = float(json.load(f)["bf16_tflops"])
+            except Exception:
+                pass
+            tf = flops / (attn_ms * 1e-3) / 1e12
+            line.update({"metric": "chunked-prefill causal attention TFLOP/s", "unit": "TFLOP/s",
+                         "value": round(tf, 1), "algorithmic_flops": int(flops),
+                         "append_GBps": round(app / (append_ms * 1e-3) / 1e9, 1),
+                         "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak,
+                                      "unit": "TFLOP/s", "frac": round(tf / peak, 4),
+                                      "kernel": "prefill_tc_kernel"}})
+        else:
+            dec = decode_bytes(wl["ctx"], KVH, HEAD_DIM, 2, B, H, 2, 2, BLOCK)
+            value = dec / (ms_step * 1e-3) / 1e9
+            line.update({"metric": "paged-decode attn HBM GB/s (whole job)", "unit": "GB/s",
+                         "value": round(value, 1), "decode_tok_s": round(B / (ms_step * 1e-3), 1),
+                         "per_gpu_attention_GBps": round(
+                             decode_bytes(wl["ctx"], kvh, HEAD_DIM, 2, B, qh, 2, 2, BLOCK)
+                             / (attn_ms * 1e-3) / 1e9, 1)})
+            if "unique_tokens" in wl:
+                uniq = wl["unique_tokens"] * KVH * HEAD_DIM * 2 * 2
+                line["unique_GBps"] = round(uniq / (ms_step * 1e-3) / 1e9, 1)
+                line["l2_reuse_logical_over_unique"] = round(
+                    int(wl["ctx"].sum()) / wl["unique_tokens"], 2)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.config != "c2":
+        run_extra(args)
     else:
         run_ours(args)
 
