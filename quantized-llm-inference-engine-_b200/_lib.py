@@ -14,7 +14,8 @@ import os
 import threading
 
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG_DIR, "libllmopt_b200.so")
+#: LLMOPT_B200_LIBRARY may point at another build of the same ABI (experiments).
+LIB_PATH = os.environ.get("LLMOPT_B200_LIBRARY") or os.path.join(PKG_DIR, "libllmopt_b200.so")
 
 OK = 0
 ERR_INVALID_ARGUMENT = 1

@@ -156,7 +156,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
   return true;
 }
 
-// 5-D TMA tile load (no multicast) into shared memory, completing on `bar`.
+// 5-D TMA tile load into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2, int c3, int c4) {
   asm volatile(
