@@ -34,6 +34,8 @@ size_t generic_smem(int d) {
 
 template <int KV_DT, int Q_DT>
 __global__ void __launch_bounds__(kThreads) attn_generic_kernel(const AttnArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int D = a.head_dim;
   const int tid = threadIdx.x;
   extern __shared__ float sm[];
@@ -226,7 +228,7 @@ cudaError_t generic_launch(const AttnArgs& a, cudaStream_t stream) {
   if (gx > 0x7fffffffLL || a.kv_heads > 65535 || gz > 65535) return cudaErrorInvalidConfiguration;
   dim3 grid((unsigned)gx, (unsigned)a.kv_heads, (unsigned)gz);
   void* args[] = {const_cast<AttnArgs*>(&a)};
-  return cudaLaunchKernel(fn, grid, dim3(kThreads), args, smem, stream);
+  return launch_pdl(fn, grid, dim3(kThreads), args, smem, stream);
 }
 
 }  // namespace llmopt

@@ -4,6 +4,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -14,6 +15,29 @@
 #include "../../include/llmopt_b200.h"
 #include "common.cuh"
 #include "kernels.h"
+
+namespace llmopt {
+
+cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args, size_t smem,
+                       cudaStream_t stream) {
+  static const bool enabled = [] {
+    const char* v = std::getenv("LLMOPT_B200_PDL");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = enabled ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace llmopt
 
 namespace {
 

@@ -33,8 +33,15 @@ __device__ __forceinline__ bool balanced_touch(long long c, const SlotRange& r, 
   return lo < hi;
 }
 
-template <int O_DT>
+// One warp per output row.  Lanes first evaluate the row's partials in
+// parallel (validity, LSE, max, weight), then every lane accumulates its VEC
+// contiguous dims of the row from each partial in turn - loads that do not
+// depend on each other, so many stay in flight even when a long sequence has
+// dozens of partials.  VEC == 0 is the scalar path for head_dim % 32 != 0.
+template <int O_DT, int VEC>
 __global__ void __launch_bounds__(kWarpsPerCta * 32) combine_kernel(const AttnArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * kWarpsPerCta + warp;
@@ -64,50 +71,89 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) combine_kernel(const AttnAr
     r.first = s * a.plan.splits;
     r.count = cnt;
   }
-
-  auto slot_of = [&](long long i) -> long long {
-    return balanced ? s + (r.first + i) : r.first + i;
+  // Partial i of this row: its row index in the workspace, or -1 if that CTA
+  // did not touch the sequence (balanced plan) or saw only masked keys.
+  auto partial_row = [&](long long i, float* lse) -> long long {
+    if (i >= r.count) return -1;
+    if (balanced && !balanced_touch(r.first + i, r, a.plan.ctas)) return -1;
+    const long long slot = balanced ? s + (r.first + i) : r.first + i;
+    const long long prow = (slot * a.num_heads + h) * a.q_len + qi;
+    *lse = a.part_lse[prow];
+    return *lse == -INFINITY ? -1 : prow;
   };
-  auto valid_of = [&](long long i) -> bool {
-    return balanced ? balanced_touch(r.first + i, r, a.plan.ctas) : true;
-  };
 
-  // pass 1: max LSE
   float mx = -INFINITY;
   for (long long i = lane; i < r.count; i += 32) {
-    if (!valid_of(i)) continue;
-    const float l = a.part_lse[(slot_of(i) * a.num_heads + h) * a.q_len + qi];
-    mx = fmaxf(mx, l);
+    float l;
+    if (partial_row(i, &l) >= 0) mx = fmaxf(mx, l);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
 
-  float acc[kMaxDimPerLane];
+  constexpr int kAcc = VEC > 0 ? VEC : kMaxDimPerLane;
+  float acc[kAcc];
 #pragma unroll
-  for (int k = 0; k < kMaxDimPerLane; ++k) acc[k] = 0.f;
+  for (int k = 0; k < kAcc; ++k) acc[k] = 0.f;
   float wsum = 0.f;
   if (mx != -INFINITY) {
-    for (long long i = 0; i < r.count; ++i) {
-      if (!valid_of(i)) continue;
-      const long long prow = (slot_of(i) * a.num_heads + h) * a.q_len + qi;
-      const float l = a.part_lse[prow];
-      if (l == -INFINITY) continue;
-      const float w = expf(l - mx);
+    for (long long base = 0; base < r.count; base += 32) {
+      float l = -INFINITY, w = 0.f;
+      long long prow = partial_row(base + lane, &l);
+      if (prow >= 0) w = expf(l - mx);
       wsum += w;
-      const float* src = a.part_o + prow * D;
+      const int n = r.count - base < 32 ? (int)(r.count - base) : 32;
+#pragma unroll 4
+      for (int k = 0; k < n; ++k) {
+        const float wk = __shfl_sync(0xffffffffu, w, k);
+        const long long pk = __shfl_sync(0xffffffffu, prow, k);
+        if (wk == 0.f) continue;  // warp-uniform
+        const float* src = a.part_o + pk * D;
+        if constexpr (VEC == 4) {
+          const float4 v = *reinterpret_cast<const float4*>(src + lane * 4);
+          acc[0] = fmaf(wk, v.x, acc[0]);
+          acc[1] = fmaf(wk, v.y, acc[1]);
+          acc[2] = fmaf(wk, v.z, acc[2]);
+          acc[3] = fmaf(wk, v.w, acc[3]);
+        } else if constexpr (VEC == 2) {
+          const float2 v = *reinterpret_cast<const float2*>(src + lane * 2);
+          acc[0] = fmaf(wk, v.x, acc[0]);
+          acc[1] = fmaf(wk, v.y, acc[1]);
+        } else if constexpr (VEC == 8) {
+          const float4 v0 = *reinterpret_cast<const float4*>(src + lane * 8);
+          const float4 v1 = *reinterpret_cast<const float4*>(src + lane * 8 + 4);
+          acc[0] = fmaf(wk, v0.x, acc[0]);
+          acc[1] = fmaf(wk, v0.y, acc[1]);
+          acc[2] = fmaf(wk, v0.z, acc[2]);
+          acc[3] = fmaf(wk, v0.w, acc[3]);
+          acc[4] = fmaf(wk, v1.x, acc[4]);
+          acc[5] = fmaf(wk, v1.y, acc[5]);
+          acc[6] = fmaf(wk, v1.z, acc[6]);
+          acc[7] = fmaf(wk, v1.w, acc[7]);
+        } else if constexpr (VEC == 1) {
+          acc[0] = fmaf(wk, src[lane], acc[0]);
+        } else {
 #pragma unroll
-      for (int k = 0; k < kMaxDimPerLane; ++k) {
-        const int d = lane + 32 * k;
-        if (d < D) acc[k] = fmaf(w, src[d], acc[k]);
+          for (int kk = 0; kk < kMaxDimPerLane; ++kk) {
+            const int d = lane + 32 * kk;
+            if (d < D) acc[kk] = fmaf(wk, src[d], acc[kk]);
+          }
+        }
       }
     }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   const long long obase = s * a.o_s + (long long)h * a.o_h + (long long)qi * a.o_t;
+  if constexpr (VEC > 0) {
 #pragma unroll
-  for (int k = 0; k < kMaxDimPerLane; ++k) {
-    const int d = lane + 32 * k;
-    if (d < D) store_f32<O_DT>(a.out, obase + d, acc[k] * inv);
+    for (int k = 0; k < VEC; ++k) store_f32<O_DT>(a.out, obase + lane * VEC + k, acc[k] * inv);
+  } else {
+#pragma unroll
+    for (int kk = 0; kk < kMaxDimPerLane; ++kk) {
+      const int d = lane + 32 * kk;
+      if (d < D) store_f32<O_DT>(a.out, obase + d, acc[kk] * inv);
+    }
   }
   if (a.lse != nullptr && lane == 0) {
     a.lse[row] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
@@ -127,6 +173,8 @@ template <int O_DT, int L_DT>
 __global__ void merge_states_kernel(const void* o1, const void* o2, const void* l1,
                                     const void* l2, void* out, void* lse_out, long long rows,
                                     int head_dim) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long n = rows * head_dim;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
@@ -153,15 +201,25 @@ cudaError_t combine_launch(const AttnArgs& a, cudaStream_t stream) {
   if (nrows <= 0) return cudaSuccess;
   const long long grid = (nrows + kWarpsPerCta - 1) / kWarpsPerCta;
   if (grid > 0x7fffffffLL || a.head_dim > 32 * kMaxDimPerLane) return cudaErrorInvalidValue;
+  const int vec = (a.head_dim % 32 == 0 && a.head_dim <= 256) ? a.head_dim / 32 : 0;
   const void* fn = nullptr;
-  switch (a.out_dtype) {
-    case kF32: fn = reinterpret_cast<const void*>(&combine_kernel<kF32>); break;
-    case kF16: fn = reinterpret_cast<const void*>(&combine_kernel<kF16>); break;
-    case kBF16: fn = reinterpret_cast<const void*>(&combine_kernel<kBF16>); break;
-    default: return cudaErrorInvalidValue;
+#define LLMOPT_COMBINE_CASE(DT)                                                   \
+  if (a.out_dtype == DT) {                                                        \
+    switch (vec) {                                                                \
+      case 1: fn = reinterpret_cast<const void*>(&combine_kernel<DT, 1>); break;  \
+      case 2: fn = reinterpret_cast<const void*>(&combine_kernel<DT, 2>); break;  \
+      case 4: fn = reinterpret_cast<const void*>(&combine_kernel<DT, 4>); break;  \
+      case 8: fn = reinterpret_cast<const void*>(&combine_kernel<DT, 8>); break;  \
+      default: fn = reinterpret_cast<const void*>(&combine_kernel<DT, 0>); break; \
+    }                                                                             \
   }
+  LLMOPT_COMBINE_CASE(kF32)
+  LLMOPT_COMBINE_CASE(kF16)
+  LLMOPT_COMBINE_CASE(kBF16)
+#undef LLMOPT_COMBINE_CASE
+  if (fn == nullptr) return cudaErrorInvalidValue;
   void* args[] = {const_cast<AttnArgs*>(&a)};
-  return cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kWarpsPerCta * 32), args, 0, stream);
+  return launch_pdl(fn, dim3((unsigned)grid), dim3(kWarpsPerCta * 32), args, 0, stream);
 }
 
 cudaError_t merge_states_launch(const void* o1, const void* o2, const void* l1, const void* l2,
@@ -185,7 +243,7 @@ cudaError_t merge_states_launch(const void* o1, const void* o2, const void* l1, 
   if (blocks > 148 * 16) blocks = 148 * 16;
   void* args[] = {const_cast<void**>(&o1), const_cast<void**>(&o2), const_cast<void**>(&l1),
                   const_cast<void**>(&l2), &out, &lse_out, &rows, &head_dim};
-  return cudaLaunchKernel(fn, dim3((unsigned)blocks), dim3(256), args, 0, stream);
+  return launch_pdl(fn, dim3((unsigned)blocks), dim3(256), args, 0, stream);
 }
 
 }  // namespace llmopt

@@ -204,6 +204,18 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
   }
 }
 
+// Programmatic dependent launch: block until the previous kernel in the stream
+// has finished and its writes are visible.  Every kernel here calls it before
+// touching global memory, so launches can overlap the previous kernel's tail.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Let the next kernel in the stream start launching; it still waits for this
+// grid's completion (and memory visibility) in its own griddep_wait().
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // 2^x on the special-function unit (MUFU.EX2); exact 0 for -inf.
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;

@@ -91,6 +91,8 @@ __global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
     decode_tma_kernel(const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const AttnArgs a, const int hpc,
                       const int nstages) {
+  griddep_wait();
+  griddep_launch_dependents();
   constexpr int kSubs = D / kSub;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -544,7 +546,7 @@ cudaError_t decode_tma_launch(const AttnArgs& a, const DecodeLaunch& launch,
   int stages = launch.stages;
   void* args[] = {const_cast<CUtensorMap*>(&tmk), const_cast<CUtensorMap*>(&tmv),
                   const_cast<AttnArgs*>(&a), &hpc, &stages};
-  return cudaLaunchKernel(fn, grid, block, args, launch.smem_bytes, stream);
+  return launch_pdl(fn, grid, block, args, launch.smem_bytes, stream);
 }
 
 }  // namespace llmopt

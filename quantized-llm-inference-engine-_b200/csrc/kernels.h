@@ -9,6 +9,12 @@
 
 namespace llmopt {
 
+// cudaLaunchKernel with programmatic stream serialization, so the launch of a
+// kernel overlaps the tail of the previous one (each kernel starts with
+// griddepcontrol.wait).  LLMOPT_B200_PDL=0 turns it off.
+cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args, size_t smem,
+                       cudaStream_t stream);
+
 // Everything the attention kernels read, in one POD passed by value.
 struct AttnArgs {
   // query [batch, num_heads, q_len, head_dim]

@@ -93,6 +93,8 @@ __device__ __forceinline__ void copy_row(const void* src, long long sbase, long 
 // write(): grid (batch, ceil(q_len / kRowsPerCta)).
 template <int IN_DT, int OUT_DT>
 __global__ void __launch_bounds__(kThreads) kv_write_kernel(const KvWriteArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long s = blockIdx.x;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -156,6 +158,8 @@ __global__ void __launch_bounds__(kThreads) kv_write_kernel(const KvWriteArgs a)
 // write_decode(): one warp pair per sequence (warp 0: K, warp 1: V).
 template <int IN_DT, int OUT_DT>
 __global__ void __launch_bounds__(64) kv_write_decode_kernel(const KvWriteArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long s = blockIdx.x;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -184,6 +188,8 @@ __global__ void __launch_bounds__(64) kv_write_decode_kernel(const KvWriteArgs a
 // gather(): grid (batch, ceil(max_len / kRowsPerCta)); one warp per position.
 template <int DT>
 __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a, int vec) {
+  griddep_wait();
+  griddep_launch_dependents();
   const long long s = blockIdx.x;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -264,7 +270,7 @@ cudaError_t kv_write_launch(const KvWriteArgs& a, cudaStream_t stream) {
   const long long gy = (a.q_len + kRowsPerCta - 1) / kRowsPerCta;
   if (a.batch > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidConfiguration;
   void* args[] = {const_cast<KvWriteArgs*>(&a)};
-  return cudaLaunchKernel(fn, dim3((unsigned)a.batch, (unsigned)gy), dim3(kThreads), args, 0,
+  return launch_pdl(fn, dim3((unsigned)a.batch, (unsigned)gy), dim3(kThreads), args, 0,
                           stream);
 }
 
@@ -274,7 +280,7 @@ cudaError_t kv_write_decode_launch(const KvWriteArgs& a, cudaStream_t stream) {
   if (fn == nullptr) return cudaErrorInvalidValue;
   if (a.batch > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   void* args[] = {const_cast<KvWriteArgs*>(&a)};
-  return cudaLaunchKernel(fn, dim3((unsigned)a.batch), dim3(64), args, 0, stream);
+  return launch_pdl(fn, dim3((unsigned)a.batch), dim3(64), args, 0, stream);
 }
 
 cudaError_t gather_launch(const GatherArgs& a, cudaStream_t stream) {
@@ -297,7 +303,7 @@ cudaError_t gather_launch(const GatherArgs& a, cudaStream_t stream) {
     default: return cudaErrorInvalidValue;
   }
   void* args[] = {const_cast<GatherArgs*>(&a), &vec};
-  return cudaLaunchKernel(fn, dim3((unsigned)a.batch, (unsigned)gy), dim3(kThreads), args, 0,
+  return launch_pdl(fn, dim3((unsigned)a.batch, (unsigned)gy), dim3(kThreads), args, 0,
                           stream);
 }
 

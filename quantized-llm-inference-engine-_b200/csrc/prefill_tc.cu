@@ -99,6 +99,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq,
                       const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   using L = Layout<D>;
   constexpr int kSubs = L::kSubs;
   const int warp = threadIdx.x >> 5;
@@ -480,7 +482,7 @@ cudaError_t prefill_tc_launch(const AttnArgs& a, const CUtensorMap& tmq, const C
   if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   void* args[] = {const_cast<CUtensorMap*>(&tmq), const_cast<CUtensorMap*>(&tmk),
                   const_cast<CUtensorMap*>(&tmv), const_cast<AttnArgs*>(&a)};
-  return cudaLaunchKernel(fn, dim3((unsigned)grid), dim3(kThreads), args, smem, stream);
+  return launch_pdl(fn, dim3((unsigned)grid), dim3(kThreads), args, smem, stream);
 }
 
 }  // namespace llmopt
