@@ -5,24 +5,30 @@
 // k_pos <= ctx - q_len + i, softmax, P V) when the query rows of one KV head
 // form a real dense contraction (q_len * group > 16) on a 16-bit cache.
 //
-// One CTA owns 128 query rows of one (sequence, KV head): kTQ = 128 / group
+// One CTA owns 128 query rows of one (sequence, KV head): 128 / group
 // consecutive chunk tokens x the group's query heads, rows ordered
-// [head][token].  It walks that sequence's keys in tiles of 128 (8 KV blocks
-// of 16 tokens) up to the causal limit of its last row:
+// [head][token].  It walks that sequence's keys in tiles of 64 (4 KV blocks of
+// 16 tokens) up to the causal limit of its last row.  Two CTAs fit on an SM
+// (~113 KB of shared memory, 256 tensor-memory columns each), so one CTA's
+// tensor-core work overlaps the other's softmax:
 //
-//   TMA warp   Q once (4-D tensor map over the query), then per key tile the
-//              8 blocks' K and V rows through the block table (5-D map over the
-//              cache, one 16-token box per block and 64-dim slice), into a
-//              2-stage ring.  -1 table entries are not loaded.
+//   TMA warp   Q once (4-D tensor map over the query); then per key tile the 4
+//              blocks' K rows and V rows through the block table (5-D map over
+//              the cache, one 16-token box per block and 64-dim slice).  K and V
+//              have separate 2-stage rings, so K of tile j+2 streams in as soon
+//              as S(j) is computed, and V of tile j+2 as soon as P(j)V(j) is.
+//              -1 table entries are not loaded.
 //   MMA warp   one thread issues tcgen05.mma kind::f16: S = Q K^T (M=128,
-//              N=128, K=head_dim) into tensor memory, then O += P V (N=head_dim,
-//              K=128 keys) with P from shared memory and V as an MN-major
-//              operand.  Commits signal the softmax warps and free the stage.
+//              N=64, K=head_dim) into one of two tensor-memory S buffers, then
+//              O += P V (N=head_dim, K=64 keys) with P from shared memory and V
+//              as an MN-major operand.  Commits signal the softmax warps and
+//              free the K / V stages.
 //   softmax    4 warps, one thread per row (= TMEM lane): tcgen05.ld of the S
-//              row, mask (block validity, context, causal), online softmax in
-//              fp32 with a lazy running max (O in TMEM is rescaled only when the
-//              row max grows by more than 2^8, which keeps every exp <= 256),
-//              P written as bf16/fp16 into a 128B-swizzled K-major tile.
+//              row, mask (block validity, context, causal; skipped for interior
+//              tiles), online softmax in fp32 with a lazy running max (O in
+//              TMEM is rescaled only when the row max grows by more than 2^8,
+//              which keeps every exp <= 256), P written as bf16/fp16 into a
+//              128B-swizzled K-major tile.
 //   epilogue   O / l from TMEM to the output, plus the natural-log LSE.
 //
 // Stale rows (unloaded blocks, slots past the context) are zeroed in V before
@@ -39,63 +45,52 @@ namespace {
 
 constexpr int kBS = 16;
 constexpr int kM = 128;                  // query rows per CTA = TMEM lanes
-constexpr int kN = 128;                  // keys per tile
+constexpr int kN = 64;                   // keys per tile
 constexpr int kBlocksPerTile = kN / kBS;
-constexpr int kStages = 2;
+constexpr int kStages = 2;               // per ring (K and V)
+constexpr int kBitsRing = 8;             // tile valid-block bits, indexed tile % 8
 constexpr int kSoftmaxWarps = 4;
 constexpr int kTmaWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr int kThreads = 6 * 32;
-constexpr int kTile = kM * 128;          // one [128 rows x 128 B] swizzled sub-tile (16 KB)
+constexpr int kQTile = kM * 128;         // [128 rows x 128 B] swizzled sub-tile (16 KB)
+constexpr int kKTile = kN * 128;         // [64 keys x 128 B] swizzled sub-tile (8 KB)
 constexpr int kBlockBytes = kBS * 128;   // one 16-row box (2 KB)
 constexpr float kRescaleLog2 = 8.0f;
-constexpr uint32_t kTmemCols = 256;      // S: 128 columns, O: head_dim (<= 128) columns
+constexpr uint32_t kTmemCols = 256;      // S0, S1: 64 columns each; O: head_dim (<= 128)
 
 template <int D>
 struct Layout {
   static constexpr int kSubs = D / 64;
   static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kSubs * kTile;
-  static constexpr int kV = kK + kStages * kSubs * kTile;
-  static constexpr int kP = kV + kStages * kSubs * kTile;
-  static constexpr int kBar = kP + 2 * kTile;
-  static constexpr int kBytes = kBar + 128;
+  static constexpr int kK = kQ + kSubs * kQTile;
+  static constexpr int kV = kK + kStages * kSubs * kKTile;
+  static constexpr int kP = kV + kStages * kSubs * kKTile;
+  static constexpr int kBar = kP + kQTile;     // P: [128 rows x 64 keys] = one 16 KB tile
+  static constexpr int kBytes = kBar + 256;
 };
 
 struct Bars {
   uint64_t q_full;
-  uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
-  uint64_t s_full;
+  uint64_t k_full[kStages];
+  uint64_t k_empty[kStages];
+  uint64_t v_full[kStages];
+  uint64_t v_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t bits_full[2];
   uint64_t p_full;
   uint64_t o_done;
   uint32_t tmem_base;
+  uint32_t tile_bits[kBitsRing];   // written by the TMA warp before k_full
+  uint32_t s_bits[2];              // relayed by the MMA warp with bits_full
 };
 
 __device__ __forceinline__ void wait_or_flag(uint64_t* bar, unsigned parity, unsigned* err) {
   if (!mbar_wait(bar, parity)) record_error(err, kErrWaitTimeout);
 }
 
-// Valid-block bits of key tile j (bit i: block j*8+i is loaded) for one sequence.
-__device__ __forceinline__ unsigned tile_blocks(const AttnArgs& a, long long s, int j,
-                                                long long n_keys, unsigned* err, bool flag) {
-  unsigned bits = 0;
-#pragma unroll
-  for (int i = 0; i < kBlocksPerTile; ++i) {
-    const long long b = (long long)j * kBlocksPerTile + i;
-    if (b * kBS >= n_keys) break;
-    const long long id = load_index(a.table, a.table_i64, s * a.table_stride + b);
-    if (id >= 0 && id < a.num_blocks) {
-      bits |= 1u << i;
-    } else if (id >= a.num_blocks && flag) {
-      record_error(err, kErrBlockId);
-    }
-  }
-  return bits;
-}
-
 template <int D, int KV_DT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq,
                       const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
@@ -125,10 +120,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     record_error(a.err, kErrTableWidth);
   }
 
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* sm = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = smem_raw;
   Bars* bars = reinterpret_cast<Bars*>(sm + L::kBar);
+  // The swizzled tiles need a 1024-byte aligned base; refuse to run without it.
+  const bool misaligned = (smem_addr(sm) & 1023u) != 0;
   unsigned char* sQ = sm + L::kQ;
   unsigned char* sK = sm + L::kK;
   unsigned char* sV = sm + L::kV;
@@ -137,10 +133,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(&bars->kv_full[i], 1);
-      mbar_init(&bars->kv_empty[i], 1);
+      mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
+      mbar_init(&bars->v_full[i], 1);
+      mbar_init(&bars->v_empty[i], 1);
     }
-    mbar_init(&bars->s_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->bits_full[i], 1);
+    }
     mbar_init(&bars->p_full, kSoftmaxWarps * 32);
     mbar_init(&bars->o_done, 1);
     mbar_init_fence();
@@ -153,28 +154,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t tmem_s = tmem;
-  const uint32_t tmem_o = tmem + kN;
+  const uint32_t tmem_o = tmem + 2 * kN;
 
-  if (warp == kTmaWarp) {
+  if (misaligned) {
+    if (threadIdx.x == 0) record_error(a.err, kErrWaitTimeout);
+  } else if (warp == kTmaWarp) {
     // ------------------------------------------------------------- TMA producer
     if (lane == 0) {
       prefetch_tensormap(&tmq);
       prefetch_tensormap(&tmk);
       prefetch_tensormap(&tmv);
-      mbar_arrive_expect_tx(&bars->q_full, (unsigned)(kSubs * kTile));
+      mbar_arrive_expect_tx(&bars->q_full, (unsigned)(kSubs * kQTile));
 #pragma unroll
       for (int sub = 0; sub < kSubs; ++sub) {
-        tc::tma_load_4d(sQ + sub * kTile, &tmq, &bars->q_full, sub * 64, t0, kh * group,
+        tc::tma_load_4d(sQ + sub * kQTile, &tmq, &bars->q_full, sub * 64, t0, kh * group,
                         (int)s);
       }
     }
     for (int j = 0; j < n_tiles; ++j) {
       const int st = j % kStages;
-      if (j >= kStages && lane == 0) {
-        wait_or_flag(&bars->kv_empty[st], (unsigned)((j / kStages - 1) & 1), a.err);
-      }
-      __syncwarp();
       int id = 0;
       bool valid = false;
       if (lane < kBlocksPerTile) {
@@ -190,19 +188,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const unsigned mask = __ballot_sync(0xffffffffu, valid);
+      const unsigned bytes = (unsigned)(__popc(mask) * kSubs * kBlockBytes);
+      // K of tile j: its stage is free once S(j - 2) has been computed.
       if (lane == 0) {
-        mbar_arrive_expect_tx(&bars->kv_full[st],
-                              (unsigned)(__popc(mask) * kSubs * 2 * kBlockBytes));
+        if (j >= kStages) {
+          wait_or_flag(&bars->k_empty[st], (unsigned)((j / kStages - 1) & 1), a.err);
+        }
+        bars->tile_bits[j % kBitsRing] = mask;
+        mbar_arrive_expect_tx(&bars->k_full[st], bytes);
       }
       __syncwarp();
       if (valid) {
-        unsigned char* kdst = sK + st * kSubs * kTile + lane * kBlockBytes;
-        unsigned char* vdst = sV + st * kSubs * kTile + lane * kBlockBytes;
+        unsigned char* kdst = sK + st * kSubs * kKTile + lane * kBlockBytes;
 #pragma unroll
         for (int sub = 0; sub < kSubs; ++sub) {
-          tma_load_5d(kdst + sub * kTile, &tmk, &bars->kv_full[st], sub * 64, kh, 0, id,
+          tma_load_5d(kdst + sub * kKTile, &tmk, &bars->k_full[st], sub * 64, kh, 0, id,
                       a.layer);
-          tma_load_5d(vdst + sub * kTile, &tmv, &bars->kv_full[st], sub * 64, kh, 0, id,
+        }
+      }
+      // V of tile j: its stage is free once P(j - 2) V(j - 2) has run.
+      if (lane == 0) {
+        if (j >= kStages) {
+          wait_or_flag(&bars->v_empty[st], (unsigned)((j / kStages - 1) & 1), a.err);
+        }
+        mbar_arrive_expect_tx(&bars->v_full[st], bytes);
+      }
+      __syncwarp();
+      if (valid) {
+        unsigned char* vdst = sV + st * kSubs * kKTile + lane * kBlockBytes;
+#pragma unroll
+        for (int sub = 0; sub < kSubs; ++sub) {
+          tma_load_5d(vdst + sub * kKTile, &tmv, &bars->v_full[st], sub * 64, kh, 0, id,
                       a.layer);
         }
       }
@@ -212,7 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait_or_flag(&bars->q_full, 0, a.err);
       const int first = n_tiles > kStages ? n_tiles - kStages : 0;
       for (int j = first; j < n_tiles; ++j) {
-        wait_or_flag(&bars->kv_full[j % kStages], (unsigned)((j / kStages) & 1), a.err);
+        wait_or_flag(&bars->k_full[j % kStages], (unsigned)((j / kStages) & 1), a.err);
+        wait_or_flag(&bars->v_full[j % kStages], (unsigned)((j / kStages) & 1), a.err);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -223,11 +240,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t q_addr = smem_addr(sQ);
     const uint32_t p_addr = smem_addr(sP);
 
-    // Zero V rows of tile j that hold no valid key (unloaded block / past ctx).
-    auto prepare_v = [&](int j) {
+    // S(j) = Q K(j)^T into S buffer j % 2; relays the tile's valid-block bits.
+    auto issue_qk = [&](int j) {
       const int st = j % kStages;
-      const unsigned bits = tile_blocks(a, s, j, n_keys, a.err, false);
-      unsigned char* v = sV + st * kSubs * kTile;
+      wait_or_flag(&bars->k_full[st], (unsigned)((j / kStages) & 1), a.err);
+      if (lane == 0) {
+        bars->s_bits[j & 1] = bars->tile_bits[j % kBitsRing];
+        mbar_arrive(&bars->bits_full[j & 1]);
+        tc::fence_after_sync();
+        const uint32_t k_addr = smem_addr(sK + st * kSubs * kKTile);
+        const uint32_t tmem_s = tmem + (uint32_t)((j & 1) * kN);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t koff = (kk & 3) * 32;
+          tc::mma_f16(tmem_s, tc::smem_desc_sw128(q_addr + (kk >> 2) * kQTile + koff, 16, 1024),
+                      tc::smem_desc_sw128(k_addr + (kk >> 2) * kKTile + koff, 16, 1024),
+                      idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc::commit(&bars->s_full[j & 1]);
+        tc::commit(&bars->k_empty[st]);
+      }
+      __syncwarp();
+    };
+    // Zero V rows of tile j that hold no valid key, then O += P(j) V(j).
+    auto issue_pv = [&](int j) {
+      const int st = j % kStages;
+      wait_or_flag(&bars->v_full[st], (unsigned)((j / kStages) & 1), a.err);
+      const unsigned bits = bars->tile_bits[j % kBitsRing];
+      unsigned char* v = sV + st * kSubs * kKTile;
       for (int i = 0; i < kBlocksPerTile; ++i) {
         const long long b = (long long)j * kBlocksPerTile + i;
         int first_bad = 0;                       // rows [first_bad, 16) are zeroed
@@ -242,60 +282,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int rest = e % (kSubs * 8);
           const int sub = rest >> 3;
           const int ch = rest & 7;
-          *reinterpret_cast<uint4*>(v + sub * kTile + (i * kBS + r) * 128 + ch * 16) =
+          *reinterpret_cast<uint4*>(v + sub * kKTile + (i * kBS + r) * 128 + ch * 16) =
               make_uint4(0u, 0u, 0u, 0u);
         }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-    };
-    auto issue_qk = [&](int j) {
-      const int st = j % kStages;
-      const uint32_t k_addr = smem_addr(sK + st * kSubs * kTile);
       if (lane == 0) {
         tc::fence_after_sync();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kTile + (kk & 3) * 32;
-          tc::mma_f16(tmem_s, tc::smem_desc_sw128(q_addr + off, 16, 1024),
-                      tc::smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
-        }
-        tc::commit(&bars->s_full);
-      }
-      __syncwarp();
-    };
-    auto issue_pv = [&](int j) {
-      const int st = j % kStages;
-      const uint32_t v_addr = smem_addr(sV + st * kSubs * kTile);
-      if (lane == 0) {
-        tc::fence_after_sync();
+        const uint32_t v_addr = smem_addr(v);
 #pragma unroll
         for (int kk = 0; kk < kN / 16; ++kk) {
-          const uint32_t a_off = (kk >> 2) * kTile + (kk & 3) * 32;
-          tc::mma_f16(tmem_o, tc::smem_desc_sw128(p_addr + a_off, 16, 1024),
-                      tc::smem_desc_sw128(v_addr + kk * 16 * 128, kTile, 1024), idesc_pv,
+          tc::mma_f16(tmem_o, tc::smem_desc_sw128(p_addr + kk * 32, 16, 1024),
+                      tc::smem_desc_sw128(v_addr + kk * 16 * 128, kKTile, 1024), idesc_pv,
                       (j > 0 || kk > 0) ? 1u : 0u);
         }
         tc::commit(&bars->o_done);
-        tc::commit(&bars->kv_empty[st]);
+        tc::commit(&bars->v_empty[st]);
       }
       __syncwarp();
     };
 
     if (n_tiles > 0) {
       wait_or_flag(&bars->q_full, 0, a.err);
-      wait_or_flag(&bars->kv_full[0], 0, a.err);
-      prepare_v(0);
       issue_qk(0);
+      if (n_tiles > 1) issue_qk(1);
       for (int j = 0; j < n_tiles; ++j) {
-        wait_or_flag(&bars->p_full, (unsigned)(j & 1), a.err);
-        if (j + 1 < n_tiles) {
-          wait_or_flag(&bars->kv_full[(j + 1) % kStages], (unsigned)(((j + 1) / kStages) & 1),
-                       a.err);
-          prepare_v(j + 1);
-          issue_qk(j + 1);
-        }
+        wait_or_flag(&bars->p_full, (unsigned)(j & 1), a.err);   // S(j) read, P(j) written
         issue_pv(j);
+        if (j + 2 < n_tiles) issue_qk(j + 2);                     // reuses S buffer j % 2
       }
     }
   } else {
@@ -313,28 +328,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.f;
 
     for (int j = 0; j < n_tiles; ++j) {
-      const unsigned bits = tile_blocks(a, s, j, n_keys, a.err, false);
-      wait_or_flag(&bars->s_full, (unsigned)(j & 1), a.err);
+      const unsigned par = (unsigned)((j >> 1) & 1);
+      wait_or_flag(&bars->bits_full[j & 1], par, a.err);
+      const unsigned bits = bars->s_bits[j & 1];
+      wait_or_flag(&bars->s_full[j & 1], par, a.err);
       tc::fence_after_sync();
       float sv[kN];
 #pragma unroll
       for (int c = 0; c < kN / 32; ++c) {
         float tmp[32];
-        tc::tmem_ld32(tmem_s + lane_off + c * 32, tmp);
+        tc::tmem_ld32(tmem + (uint32_t)((j & 1) * kN) + lane_off + c * 32, tmp);
 #pragma unroll
         for (int i = 0; i < 32; ++i) sv[c * 32 + i] = tmp[i];
       }
       tc::tmem_wait_ld();
       const long long kbase = (long long)j * kN;
+      // Interior tiles (every block loaded, inside the context and at or before
+      // this row's causal limit) need no per-key mask.
+      const bool full = bits == (1u << kBlocksPerTile) - 1 && kbase + kN <= ctx_s &&
+                        kbase + kN - 1 <= qpos;
       float rowmax = -INFINITY;
+      if (full) {
 #pragma unroll
-      for (int c = 0; c < kN; ++c) {
-        const long long kpos = kbase + c;
-        const bool ok = ((bits >> (c / kBS)) & 1u) && kpos < ctx_s && kpos <= qpos;
-        float xv = sv[c];
-        xv = capped ? tanhf(xv * a.scale / a.softcap) * (a.softcap * kLog2e) : xv * scale_log2;
-        sv[c] = ok ? xv : -INFINITY;
-        rowmax = fmaxf(rowmax, sv[c]);
+        for (int c = 0; c < kN; ++c) {
+          sv[c] = capped ? tanhf(sv[c] * a.scale / a.softcap) * (a.softcap * kLog2e)
+                         : sv[c] * scale_log2;
+          rowmax = fmaxf(rowmax, sv[c]);
+        }
+      } else {
+        const long long lim = qpos < ctx_s - 1 ? qpos : ctx_s - 1;   // last visible key
+#pragma unroll
+        for (int c = 0; c < kN; ++c) {
+          const bool ok = ((bits >> (c / kBS)) & 1u) && kbase + c <= lim;
+          float xv = capped ? tanhf(sv[c] * a.scale / a.softcap) * (a.softcap * kLog2e)
+                            : sv[c] * scale_log2;
+          sv[c] = ok ? xv : -INFINITY;
+          rowmax = fmaxf(rowmax, sv[c]);
+        }
       }
       const float m_new = rowmax > m_used + kRescaleLog2 ? rowmax : m_used;
       const float m_sub = m_new == -INFINITY ? 0.f : m_new;
@@ -348,6 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[c / 2] = pack2<KV_DT>(p0, p1);
       }
       if (j > 0) {
+        // P(j - 1) V(j - 1) done: the P tile is free and O is stable.
         wait_or_flag(&bars->o_done, (unsigned)((j - 1) & 1), a.err);
         tc::fence_after_sync();
         if (m_new != m_used && m_used != -INFINITY) {
@@ -367,13 +398,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       m_used = m_new;
       l += rowsum;
-      // P row r into the 128B-swizzled K-major tile (keys 0-63 | 64-127).
+      // P row r into the 128B-swizzled K-major tile (64 keys = 8 chunks of 16 B).
       unsigned char* prow = sP + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
       for (int c = 0; c < kN / 8; ++c) {
-        const int sub = c >> 3;
-        const int ch = c & 7;
-        *reinterpret_cast<uint4*>(prow + sub * kTile + ((ch ^ (r & 7)) << 4)) =
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -445,7 +474,7 @@ const void* select_prefill(const AttnArgs& a) {
 }
 
 size_t prefill_smem(int head_dim) {
-  return (head_dim == 128 ? Layout<128>::kBytes : Layout<64>::kBytes) + 1024;
+  return head_dim == 128 ? Layout<128>::kBytes : Layout<64>::kBytes;
 }
 
 }  // namespace
