@@ -15,7 +15,8 @@ namespace {
 
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
-constexpr int kRowsPerCta = 16;
+constexpr int kRowsPerCta = 16;       // gather: positions per CTA
+constexpr int kWriteRowsPerCta = 4;   // write: one token row per warp, many CTAs in flight
 
 template <int DT>
 struct Vec8 {
@@ -90,7 +91,7 @@ __device__ __forceinline__ void copy_row(const void* src, long long sbase, long 
   }
 }
 
-// write(): grid (batch, ceil(q_len / kRowsPerCta)).
+// write(): grid (batch, ceil(q_len / kWriteRowsPerCta)).
 template <int IN_DT, int OUT_DT>
 __global__ void __launch_bounds__(kThreads) kv_write_kernel(const KvWriteArgs a) {
   griddep_wait();
@@ -139,8 +140,8 @@ __global__ void __launch_bounds__(kThreads) kv_write_kernel(const KvWriteArgs a)
   }
 
   const long long row_elems = (long long)a.kv_heads * a.head_dim;
-  const int t0 = blockIdx.y * kRowsPerCta;
-  const int t1 = t0 + kRowsPerCta < a.q_len ? t0 + kRowsPerCta : a.q_len;
+  const int t0 = blockIdx.y * kWriteRowsPerCta;
+  const int t1 = t0 + kWriteRowsPerCta < a.q_len ? t0 + kWriteRowsPerCta : a.q_len;
   for (int i = t0 + warp; i < t1; i += kWarps) {
     const long long pos = start + i;
     const long long c = floordiv(pos, bs);
@@ -267,7 +268,7 @@ cudaError_t kv_write_launch(const KvWriteArgs& a, cudaStream_t stream) {
   if (a.batch <= 0 || a.q_len <= 0) return cudaSuccess;
   const void* fn = select_write(a.in_dtype, a.kv_dtype, false);
   if (fn == nullptr) return cudaErrorInvalidValue;
-  const long long gy = (a.q_len + kRowsPerCta - 1) / kRowsPerCta;
+  const long long gy = (a.q_len + kWriteRowsPerCta - 1) / kWriteRowsPerCta;
   if (a.batch > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidConfiguration;
   void* args[] = {const_cast<KvWriteArgs*>(&a)};
   return launch_pdl(fn, dim3((unsigned)a.batch, (unsigned)gy), dim3(kThreads), args, 0,

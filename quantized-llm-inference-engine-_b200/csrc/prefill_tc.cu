@@ -347,36 +347,51 @@ __global__ void __launch_bounds__(kThreads, 2)
       // this row's causal limit) need no per-key mask.
       const bool full = bits == (1u << kBlocksPerTile) - 1 && kbase + kN <= ctx_s &&
                         kbase + kN - 1 <= qpos;
-      float rowmax = -INFINITY;
-      if (full) {
+      if (capped) {
+        // tanh soft-cap, in log2 units; monotonic, so masking after it is exact.
 #pragma unroll
         for (int c = 0; c < kN; ++c) {
-          sv[c] = capped ? tanhf(sv[c] * a.scale / a.softcap) * (a.softcap * kLog2e)
-                         : sv[c] * scale_log2;
-          rowmax = fmaxf(rowmax, sv[c]);
+          sv[c] = tanhf(sv[c] * a.scale / a.softcap) * (a.softcap * kLog2e);
         }
-      } else {
+      } else if (!(scale_log2 > 0.f)) {
+        // A non-positive scale does not commute with max: scale first.
+#pragma unroll
+        for (int c = 0; c < kN; ++c) sv[c] *= scale_log2;
+      }
+      if (!full) {
         const long long lim = qpos < ctx_s - 1 ? qpos : ctx_s - 1;   // last visible key
 #pragma unroll
         for (int c = 0; c < kN; ++c) {
           const bool ok = ((bits >> (c / kBS)) & 1u) && kbase + c <= lim;
-          float xv = capped ? tanhf(sv[c] * a.scale / a.softcap) * (a.softcap * kLog2e)
-                            : sv[c] * scale_log2;
-          sv[c] = ok ? xv : -INFINITY;
-          rowmax = fmaxf(rowmax, sv[c]);
+          sv[c] = ok ? sv[c] : -INFINITY;
         }
       }
+      // Row max over 8 independent chains (scores are raw unless capped; the
+      // positive scale commutes with max and is folded into the exp below).
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+#pragma unroll
+      for (int c = 8; c < kN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
+      const float m01 = fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3]));
+      const float m23 = fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+      const float sl = (capped || !(scale_log2 > 0.f)) ? 1.f : scale_log2;  // -> log2 units
+      const float rowmax = fmaxf(m01, m23) * sl;
       const float m_new = rowmax > m_used + kRescaleLog2 ? rowmax : m_used;
       const float m_sub = m_new == -INFINITY ? 0.f : m_new;
-      float rowsum = 0.f;
+      float sum8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
       uint32_t pk[kN / 2];
 #pragma unroll
       for (int c = 0; c < kN; c += 2) {
-        const float p0 = fast_exp2(sv[c] - m_sub);
-        const float p1 = fast_exp2(sv[c + 1] - m_sub);
-        rowsum += p0 + p1;
+        const float p0 = fast_exp2(fmaf(sv[c], sl, -m_sub));
+        const float p1 = fast_exp2(fmaf(sv[c + 1], sl, -m_sub));
+        sum8[(c >> 1) & 7] += p0 + p1;
         pk[c / 2] = pack2<KV_DT>(p0, p1);
       }
+      const float rowsum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
+                           ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       if (j > 0) {
         // P(j - 1) V(j - 1) done: the P tile is free and O is stable.
         wait_or_flag(&bars->o_done, (unsigned)((j - 1) & 1), a.err);
