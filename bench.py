@@ -58,6 +58,9 @@ def parse_args(argv=None):
     p.add_argument("--ctx-lo", type=int, default=1024)
     p.add_argument("--ctx-hi", type=int, default=8192)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--transport", choices=("peer", "nccl"), default="peer",
+                   help="N>1 output all-gather: fused into the combine kernel over NVLink "
+                        "peer memory, or NCCL all_gather_into_tensor after it")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--config", choices=("c2", "c3", "c4", "c5"), default="c2",
@@ -332,8 +335,13 @@ def run_ours(args) -> None:
     attn = pkg.PagedAttention(qh, kvh, HEAD_DIM)
     head_major = torch.empty((qh, B, 1, HEAD_DIM), dtype=torch.bfloat16, device=dev)
     out_view = head_major.permute(1, 0, 2, 3)
+    peer = world > 1 and args.transport == "peer"
     gathered = (torch.empty((HEADS, B, 1, HEAD_DIM), dtype=torch.bfloat16, device=dev)
-                if world > 1 else None)
+                if world > 1 and not peer else None)
+    # With the peer transport the combine kernel also delivers every rank's
+    # heads to every rank (NVLink stores + on-device barrier).
+    sharded_step = (pdist.ShardedPagedAttention(HEADS, KV_HEADS, HEAD_DIM, transport="peer")
+                    if peer else None)
 
     def step(ev=None):
         if ev is not None:
@@ -341,16 +349,24 @@ def run_ours(args) -> None:
         cache.write_decode(0, table, offs, knew, vnew)
         if ev is not None:
             ev[1].record()
-        attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out_view,
-                              phases=_lib.PHASE_SPLIT)
+        if peer:
+            sharded_step.forward(q, cache, 0, table, ctx, 1, phases=_lib.PHASE_SPLIT)
+        else:
+            attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out_view,
+                                  phases=_lib.PHASE_SPLIT)
         if ev is not None:
             ev[2].record()
-        attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out_view,
-                              phases=_lib.PHASE_COMBINE)
+        if peer:
+            sharded_step.forward(q, cache, 0, table, ctx, 1, phases=_lib.PHASE_COMBINE)
+        else:
+            attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out_view,
+                                  phases=_lib.PHASE_COMBINE)
         if ev is not None:
             ev[3].record()
-        if world > 1:
+        if gathered is not None:
             dist.all_gather_into_tensor(gathered, head_major)
+        if ev is not None:
+            ev[4].record()
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -360,7 +376,7 @@ def run_ours(args) -> None:
 
     for _ in range(max(args.warmup, 3)):
         step()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local)
@@ -376,6 +392,7 @@ def run_ours(args) -> None:
     append_ms = statistics.fmean(e[0].elapsed_time(e[1]) for e in evs)
     decode_ms = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
     combine_ms = statistics.fmean(e[2].elapsed_time(e[3]) for e in evs)
+    gather_ms = statistics.fmean(e[3].elapsed_time(e[4]) for e in evs)
     if world > 1:
         t = torch.tensor([ms_total], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -408,15 +425,19 @@ def run_ours(args) -> None:
         for hv, t in zip(views(host), srcs):
             hv.copy_(t.cpu())
         q_d, k_d, v_d, table_d, ctx_d, offs_d = views(dev_buf)
-        out_shape = (B, HEADS if world > 1 else qh, 1, HEAD_DIM)
-        out_h = torch.empty(out_shape, dtype=torch.bfloat16, pin_memory=True)
-        sharded = pdist.ShardedPagedAttention(HEADS, KV_HEADS, HEAD_DIM) if world > 1 else None
+        # Each rank reads back its own heads of the result, so the job as a whole
+        # copies the output to the host exactly once.
+        out_h = torch.empty((B, qh, 1, HEAD_DIM), dtype=torch.bfloat16, pin_memory=True)
+        sharded = (pdist.ShardedPagedAttention(HEADS, KV_HEADS, HEAD_DIM,
+                                               transport=args.transport)
+                   if world > 1 else None)
 
         def e2e_step():
             dev_buf.copy_(host, non_blocking=True)
             cache.write_decode(0, table_d, offs_d, k_d, v_d)
             if world > 1:
                 out = sharded.forward(q_d, cache, 0, table_d, ctx_d, 1)
+                out = out[:, shard.q_lo:shard.q_hi]
             else:
                 out = attn.forward(q_d, cache, 0, table_d, ctx_d, 1)
             out_h.copy_(out, non_blocking=True)
@@ -444,6 +465,11 @@ def run_ours(args) -> None:
                "ms_per_step": round(e_ms / args.steps, 4),
                "decode_tok_s": round(B / (e_ms / args.steps * 1e-3), 1)}
 
+        if sharded is not None:
+            sharded.close()
+    if sharded_step is not None:
+        sharded_step.close()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(wl, args.seed)
@@ -456,6 +482,12 @@ def run_ours(args) -> None:
         return
     peak, peak_kind = measured_hbm_peak()
     achieved = dec_bytes / (decode_ms * 1e-3) / 1e9
+    gather_desc = (" combine fused with the all-gather over NVLink peer stores" if peer
+                   else " + NCCL all-gather")
+    kernel_ms = {"append": round(append_ms, 5), "decode_split": round(decode_ms, 5),
+                 ("combine_gather" if peer else "combine"): round(combine_ms, 5)}
+    if gathered is not None:
+        kernel_ms["nccl_all_gather"] = round(gather_ms, 5)
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -471,10 +503,10 @@ def run_ours(args) -> None:
         "data": "synthetic: seeded ctx U[1024,8192], random block tables, K/V/q 0.5*N(0,1) bf16",
         "config": {
             "workload": "config2: Llama-3-8B-shaped paged decode step (KV append + split-K "
-                        "decode + LSE combine" + (" + NCCL all-gather" if world > 1 else "") + ")",
+                        "decode + LSE combine" + (gather_desc if world > 1 else "") + ")",
             "global_batch": B, "seq_len": f"U[{args.ctx_lo},{args.ctx_hi}]",
             "heads": HEADS, "kv_heads": KV_HEADS, "head_dim": HEAD_DIM, "block_size": BLOCK,
-            "parallelism": (f"kv-head shard x{world} (tables replicated, NCCL all-gather)"
+            "parallelism": (f"kv-head shard x{world} (tables replicated,{gather_desc})"
                             if world > 1 else "single GPU"),
             "per_gpu": f"{args.batch * world} seqs x {kvh} KV heads",
             "l2": f"inputs larger than L2 (KV pool {2 * cache.key_cache.nbytes / 1e9:.2f} GB "
@@ -482,8 +514,7 @@ def run_ours(args) -> None:
             "split": "auto (balanced split-K over SMs)",
         },
         "decode_tok_s": round(B / (ms_step * 1e-3), 1),
-        "kernel_ms": {"append": round(append_ms, 5), "decode_split": round(decode_ms, 5),
-                      "combine": round(combine_ms, 5)},
+        "kernel_ms": kernel_ms,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": profiled_traffic(),

@@ -176,6 +176,54 @@ LLMOPT_API int llmopt_paged_attention_noalloc(const void* query, int32_t q_dtype
                            int64_t batch, int32_t num_heads, int32_t q_len, float scale,
                            float softcap, int64_t split_tokens, uint32_t* err, void* stream);
 
+/* ---- head-sharded groups (one process per GPU) ---------------------------
+ * No llmopt counterpart: llmopt runs on one device.  With KV heads split over
+ * `world` GPUs (rank r owns query heads [r*H, (r+1)*H) of H*world), the only
+ * exchange is an all-gather of the attention output.  These entry points do
+ * it inside the combine kernel: each merged row is stored straight into every
+ * rank's gathered output over NVLink, and the kernel ends with a bounded
+ * cross-rank barrier on flags in peer memory.
+ *
+ * Peer buffers are plain cudaMalloc allocations shared between processes with
+ * CUDA IPC: llmopt_peer_alloc returns the local pointer and a
+ * LLMOPT_PEER_HANDLE_BYTES handle to send to the other ranks (any host
+ * channel), llmopt_peer_open maps a peer's handle, llmopt_peer_close unmaps
+ * it, llmopt_peer_free releases a local buffer (after every peer closed it).
+ * These allocate and synchronise; call them at set-up, not per step.
+ */
+#define LLMOPT_PEER_HANDLE_BYTES 64
+#define LLMOPT_MAX_PEERS 8
+/* Bytes of a rank's flag buffer: LLMOPT_MAX_PEERS arrival slots + a CTA counter. */
+#define LLMOPT_PEER_FLAGS_BYTES 64
+LLMOPT_API int llmopt_peer_alloc(int32_t device, size_t bytes, void** ptr, void* handle);
+LLMOPT_API int llmopt_peer_open(int32_t device, const void* handle, void** ptr);
+LLMOPT_API int llmopt_peer_close(int32_t device, void* ptr);
+LLMOPT_API int llmopt_peer_free(int32_t device, void* ptr);
+
+/* llmopt_paged_attention_phase for this rank's heads, whose COMBINE phase also
+ * performs the all-gather.  gathered[r] / flags[r] are rank r's gathered
+ * output ([world*num_heads, batch, q_len, head_dim] of out_dtype, head-major)
+ * and flag buffer (LLMOPT_PEER_FLAGS_BYTES, zeroed before first use), as
+ * mapped in this process; gathered[rank] / flags[rank] are this rank's own.
+ * Every rank makes the same sequence of calls with the same shapes, each with
+ * an `epoch` one above its previous call (starting at 1).  When the COMBINE
+ * kernel ends, this rank's gathered output holds every rank's heads.  Peers
+ * write a call's rows into gathered[] while this rank may still be reading
+ * the previous call's: alternate two gathered buffers between calls.  A peer
+ * that never arrives makes the barrier give up after about a second with
+ * LLMOPT_DEVERR_WAIT_TIMEOUT set in `err`.  Everything else (workspace, lse of
+ * this rank's heads, split_tokens, phases) is as in llmopt_paged_attention_phase. */
+LLMOPT_API int llmopt_paged_attention_gather(
+    const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h, int64_t q_t,
+    const void* key_cache, const void* value_cache, int32_t kv_dtype, int32_t num_layers,
+    int32_t num_blocks, int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+    int32_t layer_idx, const void* block_table, int32_t table_is_i64, int64_t table_width,
+    int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
+    void* const* gathered, uint32_t* const* flags, int32_t world, int32_t rank, uint32_t epoch,
+    int32_t out_dtype, float* lse, int64_t batch, int32_t num_heads, int32_t q_len, float scale,
+    float softcap, int64_t split_tokens, void* workspace, size_t workspace_bytes,
+    uint32_t* err, void* stream, int32_t phases);
+
 /*
  * Exact log-sum-exp merge of two partial attention states.  Replaces
  * merge_states (paged_attention.py:30-55).  o1/o2/out are contiguous

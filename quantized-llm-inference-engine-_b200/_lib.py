@@ -35,6 +35,10 @@ PHASE_SPLIT = 1
 PHASE_COMBINE = 2
 PHASE_ALL = 3
 
+PEER_HANDLE_BYTES = 64
+MAX_PEERS = 8
+PEER_FLAGS_BYTES = 64
+
 _EXC = {
     ERR_INVALID_ARGUMENT: ValueError,
     ERR_UNSUPPORTED: ValueError,
@@ -75,6 +79,15 @@ SIGNATURES = {
         _p, _i32, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
         _p, _i32, _i64, _i64, _p, _i32, _p, _i32, _i64, _i64, _i64, _p,
         _i64, _i32, _i32, _f32, _f32, _i64, _p, _p],
+    "llmopt_peer_alloc": [_i32, ctypes.c_size_t, ctypes.POINTER(_p), _p],
+    "llmopt_peer_open": [_i32, _p, ctypes.POINTER(_p)],
+    "llmopt_peer_close": [_i32, _p],
+    "llmopt_peer_free": [_i32, _p],
+    "llmopt_paged_attention_gather": [
+        _p, _i32, _i64, _i64, _i64, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+        _p, _i32, _i64, _i64, _p, _i32,
+        ctypes.POINTER(_p), ctypes.POINTER(_p), _i32, _i32, ctypes.c_uint32,  # peers, epoch
+        _i32, _p, _i64, _i32, _i32, _f32, _f32, _i64, _p, ctypes.c_size_t, _p, _p, _i32],
     "llmopt_merge_states": [_p, _p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _p],
     "llmopt_kv_write": [
         _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64,

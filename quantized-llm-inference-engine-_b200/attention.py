@@ -152,7 +152,8 @@ class PagedAttention:
     def forward_with_lse(self, query: torch.Tensor, cache, layer_idx: int,
                          block_ids: torch.Tensor, context_lens: torch.Tensor,
                          query_lens: int | None = None, want_lse: bool = True,
-                         out: torch.Tensor | None = None, phases: int = _lib.PHASE_ALL):
+                         out: torch.Tensor | None = None, phases: int = _lib.PHASE_ALL,
+                         gather=None):
         """``forward`` plus the natural-log LSE ``[seq, num_heads, q_len]`` (fp32).
 
         ``out`` may be any ``[seq, num_heads, q_len, head_dim]`` view with a unit
@@ -160,6 +161,10 @@ class PagedAttention:
         writes into it directly.  ``phases`` selects the split-K kernel
         (``PHASE_SPLIT``), the combine (``PHASE_COMBINE``) or both; issuing the two
         halves as two calls with the same arguments equals one full call.
+        ``gather`` (used by ``dist.PeerGroup``) makes the combine also deliver
+        the output to every rank of a head-sharded group; ``out`` is then the
+        caller's ``[seq, num_heads, q_len, head_dim]`` view of this rank's
+        slice of the gathered buffer.
         """
         seq_len = query.shape[0]
         q_len = query_lens if query_lens is not None else query.shape[2]
@@ -216,19 +221,26 @@ class PagedAttention:
         err = rt.err_word(device)
         if rt.CHECK and seq_len and int(ctx[:seq_len].max().item()) > table.shape[1] * cache.block_size:
             raise IndexError("context_lens exceed the block table width")
-        st = L.llmopt_paged_attention_phase(
-            query.data_ptr(), rt.DTYPE_CODE[query.dtype], query.stride(0), query.stride(1),
-            query.stride(2),
-            cache.key_cache.data_ptr(), cache.value_cache.data_ptr(), kv_code,
-            cache.num_layers, cache.num_blocks, cache.block_size, cache.num_kv_heads,
-            cache.head_dim, layer,
-            table.data_ptr(), t64, table.shape[1], table.stride(0),
-            ctx.data_ptr(), c64,
-            out.data_ptr(), rt.dtype_code(out.dtype, "out"), out.stride(0), out.stride(1),
-            out.stride(2),
-            lse.data_ptr() if lse is not None else None,
-            seq_len, self.num_heads, q_len, float(self.scale), float(self.config.softcap), split,
-            ws.data_ptr(), ws.numel(), err.data_ptr(), rt.stream_handle(device), int(phases))
+        common = (query.data_ptr(), rt.DTYPE_CODE[query.dtype], query.stride(0),
+                  query.stride(1), query.stride(2),
+                  cache.key_cache.data_ptr(), cache.value_cache.data_ptr(), kv_code,
+                  cache.num_layers, cache.num_blocks, cache.block_size, cache.num_kv_heads,
+                  cache.head_dim, layer,
+                  table.data_ptr(), t64, table.shape[1], table.stride(0),
+                  ctx.data_ptr(), c64)
+        tail = (seq_len, self.num_heads, q_len, float(self.scale), float(self.config.softcap),
+                split, ws.data_ptr(), ws.numel(), err.data_ptr(), rt.stream_handle(device),
+                int(phases))
+        lse_ptr = lse.data_ptr() if lse is not None else None
+        if gather is None:
+            st = L.llmopt_paged_attention_phase(
+                *common, out.data_ptr(), rt.dtype_code(out.dtype, "out"), out.stride(0),
+                out.stride(1), out.stride(2), lse_ptr, *tail)
+        else:
+            bufs, flags, world, rank, epoch = gather
+            st = L.llmopt_paged_attention_gather(
+                *common, bufs, flags, world, rank, epoch, rt.dtype_code(out.dtype, "out"),
+                lse_ptr, *tail)
         _lib.check(st, "PagedAttention.forward")
         if rt.CHECK:
             rt.raise_on_device_errors(device, "PagedAttention.forward")

@@ -1,14 +1,17 @@
 // extern "C" entry points declared in include/llmopt_b200.h: argument checks,
-// split planning, TMA descriptor cache and kernel dispatch.  No entry point
-// allocates device memory or synchronises the stream.
+// split planning, TMA descriptor cache and kernel dispatch.  Apart from the
+// llmopt_peer_* buffer routines, no entry point allocates device memory or
+// synchronises the stream.
 #include <cudaTypedefs.h>
 
 #include <cstdarg>
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <mutex>
+#include <set>
 #include <string>
 #include <tuple>
 
@@ -18,12 +21,38 @@
 
 namespace llmopt {
 
+namespace {
+std::mutex g_carveout_mu;
+std::set<std::pair<int, const void*>> g_carveout_done;
+}  // namespace
+
+// Every kernel of this library asks for the largest shared-memory carveout.
+// An SM changes its L1 / shared split only when idle; with programmatic
+// dependent launch the next kernel's CTAs are placed while the previous
+// kernel's CTAs are still resident, so a small-shared kernel (combine, KV
+// append) left at the default split would cap how many decode / prefill CTAs
+// fit on that SM for the whole of their run - a one-wave grid then runs
+// partly as a second wave.
+cudaError_t ensure_max_shared_carveout(const void* fn) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(g_carveout_mu);
+  if (g_carveout_done.count({device, fn})) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess) g_carveout_done.insert({device, fn});
+  return e;
+}
+
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args, size_t smem,
                        cudaStream_t stream) {
   static const bool enabled = [] {
     const char* v = std::getenv("LLMOPT_B200_PDL");
     return !(v != nullptr && v[0] == '0');
   }();
+  cudaError_t ce = ensure_max_shared_carveout(fn);
+  if (ce != cudaSuccess) return ce;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -396,18 +425,20 @@ int llmopt_paged_attention(const void* query, int32_t q_dtype, int64_t q_s, int6
       LLMOPT_PHASE_ALL);
 }
 
-int llmopt_paged_attention_phase(const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h,
-                                 int64_t q_t, const void* key_cache, const void* value_cache,
-                                 int32_t kv_dtype, int32_t num_layers, int32_t num_blocks,
-                                 int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
-                                 int32_t layer_idx, const void* block_table,
-                                 int32_t table_is_i64, int64_t table_width,
-                                 int64_t table_stride, const void* context_lens,
-                                 int32_t ctx_is_i64, void* out, int32_t out_dtype, int64_t o_s,
-                                 int64_t o_h, int64_t o_t, float* lse, int64_t batch,
-                                 int32_t num_heads, int32_t q_len, float scale, float softcap,
-                                 int64_t split_tokens, void* workspace, size_t workspace_bytes,
-                                 uint32_t* err, void* stream, int32_t phases) {
+namespace {
+
+// Body of llmopt_paged_attention_phase; with `peers` the combine phase also
+// delivers the output to every rank of the head-sharded group.
+int phase_impl(const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h, int64_t q_t,
+               const void* key_cache, const void* value_cache, int32_t kv_dtype,
+               int32_t num_layers, int32_t num_blocks, int32_t block_size,
+               int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+               const void* block_table, int32_t table_is_i64, int64_t table_width,
+               int64_t table_stride, const void* context_lens, int32_t ctx_is_i64, void* out,
+               int32_t out_dtype, int64_t o_s, int64_t o_h, int64_t o_t, float* lse,
+               int64_t batch, int32_t num_heads, int32_t q_len, float scale, float softcap,
+               int64_t split_tokens, void* workspace, size_t workspace_bytes, uint32_t* err,
+               void* stream, int32_t phases, const PeerArgs* peers) {
   if (phases < 1 || phases > LLMOPT_PHASE_ALL) {
     return fail(LLMOPT_ERR_INVALID_ARGUMENT, "phases must be 1, 2 or 3");
   }
@@ -501,11 +532,157 @@ int llmopt_paged_attention_phase(const void* query, int32_t q_dtype, int64_t q_s
                                     : "generic launch");
     }
   }
-  if ((phases & LLMOPT_PHASE_COMBINE) && !c.prefill) {
+  if ((phases & LLMOPT_PHASE_COMBINE) && peers != nullptr) {
+    const int elem = out_dtype == kF32 ? 4 : 2;
+    cudaError_t e = c.prefill ? push_gather_launch(a, *peers, elem, s)
+                              : combine_gather_launch(a, *peers, s);
+    if (e != cudaSuccess) return cuda_fail(e, c.prefill ? "push_gather launch" : "combine_gather launch");
+  } else if ((phases & LLMOPT_PHASE_COMBINE) && !c.prefill) {
     cudaError_t e = combine_launch(a, s);
     if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   }
   return ok();
+}
+
+}  // namespace
+
+int llmopt_paged_attention_phase(const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h,
+                                 int64_t q_t, const void* key_cache, const void* value_cache,
+                                 int32_t kv_dtype, int32_t num_layers, int32_t num_blocks,
+                                 int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                                 int32_t layer_idx, const void* block_table,
+                                 int32_t table_is_i64, int64_t table_width,
+                                 int64_t table_stride, const void* context_lens,
+                                 int32_t ctx_is_i64, void* out, int32_t out_dtype, int64_t o_s,
+                                 int64_t o_h, int64_t o_t, float* lse, int64_t batch,
+                                 int32_t num_heads, int32_t q_len, float scale, float softcap,
+                                 int64_t split_tokens, void* workspace, size_t workspace_bytes,
+                                 uint32_t* err, void* stream, int32_t phases) {
+  return phase_impl(query, q_dtype, q_s, q_h, q_t, key_cache, value_cache, kv_dtype, num_layers,
+                    num_blocks, block_size, num_kv_heads, head_dim, layer_idx, block_table,
+                    table_is_i64, table_width, table_stride, context_lens, ctx_is_i64, out,
+                    out_dtype, o_s, o_h, o_t, lse, batch, num_heads, q_len, scale, softcap,
+                    split_tokens, workspace, workspace_bytes, err, stream, phases, nullptr);
+}
+
+// ---- head-sharded groups: peer memory and the gathered entry -----------------
+static_assert(sizeof(cudaIpcMemHandle_t) == LLMOPT_PEER_HANDLE_BYTES, "IPC handle size");
+static_assert(kMaxPeers == LLMOPT_MAX_PEERS, "peer count");
+
+namespace {
+
+// Runs fn with `device` current and restores the caller's device afterwards.
+int on_device(int32_t device, const std::function<int()>& fn) {
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  const int st = fn();
+  cudaSetDevice(prev);
+  return st;
+}
+
+}  // namespace
+
+int llmopt_peer_alloc(int32_t device, size_t bytes, void** ptr, void* handle) {
+  if (ptr == nullptr || handle == nullptr || bytes == 0) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "peer_alloc needs bytes > 0, ptr and handle");
+  }
+  *ptr = nullptr;
+  return on_device(device, [&]() -> int {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(peer buffer)");
+    e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) {
+      e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p);
+    }
+    if (e != cudaSuccess) {
+      cudaFree(p);
+      return cuda_fail(e, "peer buffer setup");
+    }
+    *ptr = p;
+    return ok();
+  });
+}
+
+int llmopt_peer_open(int32_t device, const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "peer_open needs handle and ptr");
+  }
+  *ptr = nullptr;
+  return on_device(device, [&]() -> int {
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    *ptr = p;
+    return ok();
+  });
+}
+
+int llmopt_peer_close(int32_t device, void* ptr) {
+  if (ptr == nullptr) return ok();
+  return on_device(device, [&]() -> int {
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "cudaIpcCloseMemHandle");
+  });
+}
+
+int llmopt_peer_free(int32_t device, void* ptr) {
+  if (ptr == nullptr) return ok();
+  return on_device(device, [&]() -> int {
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "cudaFree(peer buffer)");
+  });
+}
+
+int llmopt_paged_attention_gather(
+    const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h, int64_t q_t,
+    const void* key_cache, const void* value_cache, int32_t kv_dtype, int32_t num_layers,
+    int32_t num_blocks, int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+    int32_t layer_idx, const void* block_table, int32_t table_is_i64, int64_t table_width,
+    int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
+    void* const* gathered, uint32_t* const* flags, int32_t world, int32_t rank, uint32_t epoch,
+    int32_t out_dtype, float* lse, int64_t batch, int32_t num_heads, int32_t q_len, float scale,
+    float softcap, int64_t split_tokens, void* workspace, size_t workspace_bytes,
+    uint32_t* err, void* stream, int32_t phases) {
+  if (world < 1 || world > LLMOPT_MAX_PEERS || rank < 0 || rank >= world) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "rank %d of world %d (at most %d ranks)", rank,
+                world, LLMOPT_MAX_PEERS);
+  }
+  if (gathered == nullptr || flags == nullptr) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null peer array");
+  }
+  PeerArgs p{};
+  for (int r = 0; r < world; ++r) {
+    if (gathered[r] == nullptr || flags[r] == nullptr) {
+      return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null peer pointer for rank %d", r);
+    }
+    if (reinterpret_cast<uintptr_t>(gathered[r]) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(flags[r]) % 16 != 0) {
+      return fail(LLMOPT_ERR_INVALID_ARGUMENT, "peer buffers must be 16-byte aligned");
+    }
+    p.out[r] = gathered[r];
+    p.flags[r] = flags[r];
+  }
+  p.counter = flags[rank] + LLMOPT_MAX_PEERS;
+  p.epoch = epoch;
+  p.world = world;
+  p.rank = rank;
+  const int64_t o_t = head_dim;
+  const int64_t o_s = (int64_t)q_len * head_dim;
+  const int64_t o_h = batch * o_s;
+  const size_t elem = out_dtype == kF32 ? 4 : 2;
+  unsigned char* own = static_cast<unsigned char*>(gathered[rank]) +
+                       (size_t)rank * num_heads * (size_t)o_h * elem;
+  return phase_impl(query, q_dtype, q_s, q_h, q_t, key_cache, value_cache, kv_dtype, num_layers,
+                    num_blocks, block_size, num_kv_heads, head_dim, layer_idx, block_table,
+                    table_is_i64, table_width, table_stride, context_lens, ctx_is_i64, own,
+                    out_dtype, o_s, o_h, o_t, lse, batch, num_heads, q_len, scale, softcap,
+                    split_tokens, workspace, workspace_bytes, err, stream, phases, &p);
 }
 
 int llmopt_merge_states(const void* o1, const void* o2, const void* l1, const void* l2,

@@ -38,6 +38,11 @@ __device__ __forceinline__ bool balanced_touch(long long c, const SlotRange& r, 
 // contiguous dims of the row from each partial in turn - loads that do not
 // depend on each other, so many stay in flight even when a long sequence has
 // dozens of partials.  VEC == 0 is the scalar path for head_dim % 32 != 0.
+// Merges one output row; `emit(d0, vals, n)` stores n consecutive dims from d0.
+template <int VEC, class Emit>
+__device__ __forceinline__ void combine_row(const AttnArgs& a, long long row, int lane,
+                                            Emit&& emit);
+
 template <int O_DT, int VEC>
 __global__ void __launch_bounds__(kWarpsPerCta * 32) combine_kernel(const AttnArgs a) {
   griddep_wait();
@@ -47,6 +52,129 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) combine_kernel(const AttnAr
   const long long row = (long long)blockIdx.x * kWarpsPerCta + warp;
   const long long nrows = a.batch * a.num_heads * (long long)a.q_len;
   if (row >= nrows) return;
+  const int qi = (int)(row % a.q_len);
+  const long long sh = row / a.q_len;
+  const int h = (int)(sh % a.num_heads);
+  const long long s = sh / a.num_heads;
+  const long long obase = s * a.o_s + (long long)h * a.o_h + (long long)qi * a.o_t;
+  combine_row<VEC>(a, row, lane, [&](int d0, const float* v, int n) {
+    for (int k = 0; k < n; ++k) store_f32<O_DT>(a.out, obase + d0 + k, v[k]);
+  });
+}
+
+// Arrival of one CTA at the cross-rank barrier that closes a gathered call.
+// The CTA's stores (local and over NVLink) are ordered before its arrival by
+// the barrier plus thread 0's system-scope fence (fences are cumulative).  The
+// last CTA of this rank then writes `epoch` into its slot of every rank's
+// flags with release semantics and waits, with acquire loads, until every
+// rank's slot in its own flags has reached `epoch`: after that every rank's
+// rows are in this rank's gathered output.  The wait gives up after
+// kWaitLimitCycles and records kErrWaitTimeout instead of hanging.
+__device__ __forceinline__ void peer_barrier(const PeerArgs& p, unsigned* err) {
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  const unsigned arrived = atomicAdd(p.counter, 1u);
+  if (arrived != gridDim.x - 1) return;
+  __threadfence_system();
+  for (int r = 0; r < p.world; ++r) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flags[r] + p.rank), "r"(p.epoch)
+                 : "memory");
+  }
+  const unsigned* mine = p.flags[p.rank];
+  const long long t0 = clock64();
+  bool timed_out = false;
+  for (int r = 0; r < p.world && !timed_out; ++r) {
+    while (true) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
+      if ((int)(v - p.epoch) >= 0) break;
+      if (clock64() - t0 > kWaitLimitCycles) {
+        record_error(err, kErrWaitTimeout);
+        timed_out = true;
+        break;
+      }
+    }
+  }
+  *p.counter = 0u;
+}
+
+// n (1, 2, 4 or 8) consecutive output values as one store where the width allows.
+template <int O_DT>
+__device__ __forceinline__ void store_run(void* base, long long idx, const float* v, int n) {
+  if constexpr (O_DT == kF32) {
+    float* dst = static_cast<float*>(base) + idx;
+    if (n == 4) {
+      *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+      return;
+    }
+    if (n == 8) {
+      reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+      return;
+    }
+  } else {
+    unsigned short* dst = static_cast<unsigned short*>(base) + idx;
+    if (n == 2 || n == 4 || n == 8) {
+      unsigned w[4];
+      for (int k = 0; k < n / 2; ++k) w[k] = pack2<O_DT>(v[2 * k], v[2 * k + 1]);
+      if (n == 2) *reinterpret_cast<unsigned*>(dst) = w[0];
+      if (n == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+      if (n == 8) *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      return;
+    }
+  }
+  for (int k = 0; k < n; ++k) store_f32<O_DT>(base, idx + k, v[k]);
+}
+
+// Combine + all-gather: each merged row goes to every rank's gathered output
+// at head rank * num_heads + h ([H_total, batch, q_len, head_dim]), then the
+// peer barrier, so when the kernel ends this rank's gathered output is whole.
+template <int O_DT, int VEC>
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+    combine_gather_kernel(const AttnArgs a, const PeerArgs p) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * kWarpsPerCta + warp;
+  const long long nrows = a.batch * a.num_heads * (long long)a.q_len;
+  if (row < nrows) {
+    const int qi = (int)(row % a.q_len);
+    const long long sh = row / a.q_len;
+    const int h = (int)(sh % a.num_heads);
+    const long long s = sh / a.num_heads;
+    const long long gh = (long long)p.rank * a.num_heads + h;
+    const long long gbase = ((gh * a.batch + s) * a.q_len + qi) * (long long)a.head_dim;
+    combine_row<VEC>(a, row, lane, [&](int d0, const float* v, int n) {
+      for (int r = 0; r < p.world; ++r) store_run<O_DT>(p.out[r], gbase + d0, v, n);
+    });
+  }
+  peer_barrier(p, a.err);
+}
+
+// This rank's contiguous slice of its gathered output, copied to every peer
+// at the same offset in units of T (uint4 when the slice allows, else 2 bytes).
+template <class T>
+__global__ void __launch_bounds__(256) push_gather_kernel(const AttnArgs a, const PeerArgs p,
+                                                          long long off_units,
+                                                          long long n_units) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const T* src = static_cast<const T*>(p.out[p.rank]) + off_units;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_units;
+       i += (long long)gridDim.x * blockDim.x) {
+    const T v = src[i];
+    for (int r = 0; r < p.world; ++r) {
+      if (r != p.rank) static_cast<T*>(p.out[r])[off_units + i] = v;
+    }
+  }
+  peer_barrier(p, a.err);
+}
+
+template <int VEC, class Emit>
+__device__ __forceinline__ void combine_row(const AttnArgs& a, long long row, int lane,
+                                            Emit&& emit) {
   const int qi = (int)(row % a.q_len);
   const long long sh = row / a.q_len;
   const int h = (int)(sh % a.num_heads);
@@ -144,15 +272,19 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) combine_kernel(const AttnAr
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-  const long long obase = s * a.o_s + (long long)h * a.o_h + (long long)qi * a.o_t;
   if constexpr (VEC > 0) {
+    float v[VEC];
 #pragma unroll
-    for (int k = 0; k < VEC; ++k) store_f32<O_DT>(a.out, obase + lane * VEC + k, acc[k] * inv);
+    for (int k = 0; k < VEC; ++k) v[k] = acc[k] * inv;
+    emit(lane * VEC, v, VEC);
   } else {
 #pragma unroll
     for (int kk = 0; kk < kMaxDimPerLane; ++kk) {
       const int d = lane + 32 * kk;
-      if (d < D) store_f32<O_DT>(a.out, obase + d, acc[kk] * inv);
+      if (d < D) {
+        const float v = acc[kk] * inv;
+        emit(d, &v, 1);
+      }
     }
   }
   if (a.lse != nullptr && lane == 0) {
@@ -220,6 +352,49 @@ cudaError_t combine_launch(const AttnArgs& a, cudaStream_t stream) {
   if (fn == nullptr) return cudaErrorInvalidValue;
   void* args[] = {const_cast<AttnArgs*>(&a)};
   return launch_pdl(fn, dim3((unsigned)grid), dim3(kWarpsPerCta * 32), args, 0, stream);
+}
+
+cudaError_t combine_gather_launch(const AttnArgs& a, const PeerArgs& p, cudaStream_t stream) {
+  const long long nrows = a.batch * a.num_heads * (long long)a.q_len;
+  if (nrows <= 0) return cudaSuccess;
+  const long long grid = (nrows + kWarpsPerCta - 1) / kWarpsPerCta;
+  if (grid > 0x7fffffffLL || a.head_dim > 32 * kMaxDimPerLane) return cudaErrorInvalidValue;
+  const int vec = (a.head_dim % 32 == 0 && a.head_dim <= 256) ? a.head_dim / 32 : 0;
+  const void* fn = nullptr;
+#define LLMOPT_GATHER_CASE(DT)                                                           \
+  if (a.out_dtype == DT) {                                                               \
+    switch (vec) {                                                                       \
+      case 1: fn = reinterpret_cast<const void*>(&combine_gather_kernel<DT, 1>); break;  \
+      case 2: fn = reinterpret_cast<const void*>(&combine_gather_kernel<DT, 2>); break;  \
+      case 4: fn = reinterpret_cast<const void*>(&combine_gather_kernel<DT, 4>); break;  \
+      case 8: fn = reinterpret_cast<const void*>(&combine_gather_kernel<DT, 8>); break;  \
+      default: fn = reinterpret_cast<const void*>(&combine_gather_kernel<DT, 0>); break; \
+    }                                                                                    \
+  }
+  LLMOPT_GATHER_CASE(kF32)
+  LLMOPT_GATHER_CASE(kF16)
+  LLMOPT_GATHER_CASE(kBF16)
+#undef LLMOPT_GATHER_CASE
+  if (fn == nullptr) return cudaErrorInvalidValue;
+  void* args[] = {const_cast<AttnArgs*>(&a), const_cast<PeerArgs*>(&p)};
+  return launch_pdl(fn, dim3((unsigned)grid), dim3(kWarpsPerCta * 32), args, 0, stream);
+}
+
+cudaError_t push_gather_launch(const AttnArgs& a, const PeerArgs& p, int elem_bytes,
+                               cudaStream_t stream) {
+  const long long slice = a.batch * a.num_heads * (long long)a.q_len * a.head_dim * elem_bytes;
+  const long long off = (long long)p.rank * slice;
+  const bool wide = slice % 16 == 0 && off % 16 == 0;
+  const int unit = wide ? 16 : 2;
+  const long long n_units = slice / unit;
+  long long grid = (n_units + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  if (grid < 1) grid = 1;
+  long long off_units = off / unit;
+  void* args[] = {const_cast<AttnArgs*>(&a), const_cast<PeerArgs*>(&p), &off_units, const_cast<long long*>(&n_units)};
+  const void* fn = wide ? reinterpret_cast<const void*>(&push_gather_kernel<uint4>)
+                        : reinterpret_cast<const void*>(&push_gather_kernel<unsigned short>);
+  return launch_pdl(fn, dim3((unsigned)grid), dim3(256), args, 0, stream);
 }
 
 cudaError_t merge_states_launch(const void* o1, const void* o2, const void* l1, const void* l2,

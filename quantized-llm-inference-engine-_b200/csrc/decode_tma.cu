@@ -513,7 +513,8 @@ bool decode_tma_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch)
   }
   if (smem > 227 * 1024) return false;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-      cudaSuccess) {
+          cudaSuccess ||
+      ensure_max_shared_carveout(fn) != cudaSuccess) {
     return false;
   }
   int occ = 0;

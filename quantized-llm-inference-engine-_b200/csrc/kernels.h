@@ -12,6 +12,8 @@ namespace llmopt {
 // cudaLaunchKernel with programmatic stream serialization, so the launch of a
 // kernel overlaps the tail of the previous one (each kernel starts with
 // griddepcontrol.wait).  LLMOPT_B200_PDL=0 turns it off.
+// Sets the largest shared-memory carveout on `fn` (once per device).
+cudaError_t ensure_max_shared_carveout(const void* fn);
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args, size_t smem,
                        cudaStream_t stream);
 
@@ -80,6 +82,26 @@ cudaError_t generic_launch(const AttnArgs& a, cudaStream_t stream);
 
 // Merge of split partials into the output (+ optional LSE).
 cudaError_t combine_launch(const AttnArgs& a, cudaStream_t stream);
+
+// Peers of a head-sharded group for the fused combine + all-gather.  Every
+// rank's gathered output is [world * num_heads, batch, q_len, head_dim]
+// (num_heads = this rank's heads); rank r owns heads [r*num_heads, (r+1)*num_heads).
+constexpr int kMaxPeers = 8;
+struct PeerArgs {
+  void* out[kMaxPeers];          // each rank's gathered output (device pointers, peer-mapped)
+  unsigned* flags[kMaxPeers];    // each rank's arrival flags: u32[kMaxPeers], slot = source rank
+  unsigned* counter;             // this rank's CTA arrival counter (0 between calls)
+  unsigned epoch;                // written to every peer's flag slot by this call
+  int world;
+  int rank;
+};
+// Combine that stores each merged row into every rank's gathered output over
+// NVLink, then barriers with the peers through their flags (bounded wait).
+cudaError_t combine_gather_launch(const AttnArgs& a, const PeerArgs& p, cudaStream_t stream);
+// Copies this rank's slice of its gathered output (already written by a
+// kernel that stores the output directly) to every peer, then the same barrier.
+cudaError_t push_gather_launch(const AttnArgs& a, const PeerArgs& p, int elem_bytes,
+                               cudaStream_t stream);
 
 // merge_states
 cudaError_t merge_states_launch(const void* o1, const void* o2, const void* l1, const void* l2,

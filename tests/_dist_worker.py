@@ -1,8 +1,10 @@
 """One rank of the multi-GPU head-sharding check (launched by test_gpu_dist.py via torchrun).
 
 Every rank builds the same seeded decode and prefill cases, keeps its KV heads'
-slice of the pool, runs ShardedPagedAttention (local kernels + NCCL all-gather)
-and compares the gathered [seq, H, q_len, D] output with the CPU oracle.
+slice of the pool, runs ShardedPagedAttention with both transports (NCCL
+all-gather, and the combine kernel's own NVLink peer stores + barrier), several
+calls each, and compares the gathered [seq, H, q_len, D] output with the CPU
+oracle.
 Rank 0 prints one "OK <world>" line when every rank passed.
 """
 
@@ -25,7 +27,7 @@ from cases import build_paged_case  # noqa: E402
 from oracle import paged_oracle as po  # noqa: E402
 
 
-def check_case(case, dev, pkg, pdist) -> float:
+def check_case(case, dev, pkg, pdist, transport="nccl", repeats=1) -> float:
     world, rank = dist.get_world_size(), dist.get_rank()
     H, KVH = case["heads"], case["kv_heads"]
     shard = pdist.shard_heads(H, KVH, world, rank)
@@ -35,16 +37,34 @@ def check_case(case, dev, pkg, pdist) -> float:
     vc = to_dev(case["value_cache"], "bf16", dev)
     cache.key_cache.copy_(kc[:, :, :, shard.kv_lo:shard.kv_hi])
     cache.value_cache.copy_(vc[:, :, :, shard.kv_lo:shard.kv_hi])
-    attn = pdist.ShardedPagedAttention(H, KVH, d)
+    attn = pdist.ShardedPagedAttention(H, KVH, d, transport=transport)
     q = to_dev(case["query"], "bf16", dev)
     table = torch.from_numpy(case["block_ids"]).to(dev)
     ctx = torch.from_numpy(case["context_lens"]).to(dev)
-    out = attn.forward(attn.local_query(q), cache, 0, table, ctx, case["q_len"])
-    torch.cuda.synchronize(dev)
     want, _ = po.paged_attention(case["query"], "bf16", case["key_cache"], case["value_cache"],
                                  "bf16", 0, case["block_ids"], case["context_lens"], H, KVH,
                                  q_len=case["q_len"], acc=np.float32)
-    return float(np.abs(out.float().cpu().numpy() - want).max())
+    worst = 0.0
+    outs = []
+    for i in range(repeats):
+        # Alternate the whole call with the split / combine halves.
+        if i % 2 == 0:
+            out = attn.forward(attn.local_query(q), cache, 0, table, ctx, case["q_len"])
+        else:
+            attn.forward(attn.local_query(q), cache, 0, table, ctx, case["q_len"],
+                         phases=pkg._lib.PHASE_SPLIT)
+            out = attn.forward(attn.local_query(q), cache, 0, table, ctx, case["q_len"],
+                               phases=pkg._lib.PHASE_COMBINE)
+        outs.append(out)
+        torch.cuda.synchronize(dev)
+        worst = max(worst, float(np.abs(out.float().cpu().numpy() - want).max()))
+    if repeats > 1:
+        # The previous call's gathered view is still intact (two alternating buffers).
+        worst = max(worst, float(np.abs(outs[-2].float().cpu().numpy() - want).max()))
+    if pkg._runtime.read_and_clear_errors(dev):
+        worst = float("inf")
+    attn.close()
+    return worst
 
 
 def main() -> None:
@@ -59,10 +79,11 @@ def main() -> None:
     decode = build_paged_case(70, batch=6, heads=32, kv_heads=8, head_dim=128, block_size=16,
                               ctx=[1, 17, 300, 1000, 64, 2048], kv_kind="bf16", q_kind="bf16",
                               value_scale=0.5)
-    errs.append(check_case(decode, dev, pkg, pdist))
     prefill = build_paged_case(71, batch=3, heads=32, kv_heads=8, head_dim=128, block_size=16,
                                ctx=[100, 300, 64], kv_kind="bf16", q_kind="bf16", q_len=48)
-    errs.append(check_case(prefill, dev, pkg, pdist))
+    for transport in ("nccl", "peer"):
+        errs.append(check_case(decode, dev, pkg, pdist, transport, repeats=3))
+        errs.append(check_case(prefill, dev, pkg, pdist, transport, repeats=2))
     worst = torch.tensor([max(errs)], device=dev)
     dist.all_reduce(worst, op=dist.ReduceOp.MAX)
     if rank == 0:

@@ -77,3 +77,91 @@ def test_head_major_all_gather_world2():
         assert p.exitcode == 0
     assert all(ok for _, ok, _ in results)
     assert all(shape == (3, 8, 2, 4) for _, _, shape in results)
+
+
+class _FakePeerMemory:
+    """Host stand-in for CUDA IPC: handles encode (rank, pointer), mappings are logged."""
+
+    def __init__(self, rank: int):
+        self.rank = rank
+        self.next = 1
+        self.live: dict[int, int] = {}
+        self.opened: list[int] = []
+        self.closed: list[int] = []
+        self.freed: list[int] = []
+
+    def alloc(self, nbytes):
+        ptr = (self.rank + 1) << 32 | self.next << 8
+        self.next += 1
+        self.live[ptr] = nbytes
+        return ptr, f"{self.rank}:{ptr}".encode()
+
+    def open(self, handle):
+        owner, ptr = handle.decode().split(":")
+        assert int(owner) != self.rank, "a rank must not map its own handle"
+        mapped = int(ptr) | 1   # a distinct address for the mapping
+        self.opened.append(mapped)
+        return mapped
+
+    def close(self, ptr):
+        assert ptr in self.opened and ptr not in self.closed
+        self.closed.append(ptr)
+
+    def free(self, ptr):
+        assert ptr in self.live
+        del self.live[ptr]
+        self.freed.append(ptr)
+
+
+def _peer_group_worker(rank: int, world: int, port: int, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    from importlib import import_module
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        d = import_module("quantized-llm-inference-engine-_b200.dist")
+        mem = _FakePeerMemory(rank)
+        pg = d.PeerGroup(device=torch.device("cpu"), memory=mem)
+        checks = []
+        # Flags: own allocation at [rank], every other slot is that peer's mapping.
+        f = pg._flags
+        checks.append(f.ptrs[rank] == f.local)
+        checks.append(all(((p >> 32) - 1) == r and p & 1 for r, p in enumerate(f.ptrs)
+                          if r != rank))
+        e1, w1, bufs1, flags1 = pg.next_call(1000)
+        e2, w2, bufs2, _ = pg.next_call(1000)
+        checks.append((e1, w1, e2, w2) == (1, 1, 2, 0))
+        checks.append(len(mem.live) == 3)                      # flags + two buffers, no regrowth
+        checks.append(all(b.nbytes == 1 << 20 for b in pg._bufs))
+        checks.append(list(bufs1) == pg._bufs[1].ptrs and list(bufs2) == pg._bufs[0].ptrs)
+        checks.append(list(flags1) == f.ptrs)
+        old = [b.local for b in pg._bufs]
+        e3, w3, _, _ = pg.next_call((2 << 20) + 1)            # grows collectively
+        checks.append((e3, w3) == (3, 1))
+        checks.append(all(b.nbytes == 4 << 20 for b in pg._bufs))
+        checks.append(sorted(mem.freed) == sorted(old))
+        pg.close()
+        checks.append(not mem.live and sorted(mem.closed) == sorted(mem.opened))
+        checks.append(len(mem.opened) == 5 * (world - 1))   # flags + 2 + 2 buffers per peer
+        result_q.put((rank, checks))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_group_exchange_and_growth_world2():
+    load_package()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_group_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, checks in results:
+        assert all(checks), (rank, checks)
