@@ -64,6 +64,11 @@ enum {
 #define LLMOPT_DEVERR_BLOCK_ID 1u      /* block id >= num_blocks (access skipped)     */
 #define LLMOPT_DEVERR_TABLE_WIDTH 2u   /* position beyond the block-table row         */
 #define LLMOPT_DEVERR_WAIT_TIMEOUT 4u  /* a bounded on-device wait gave up            */
+/* Set together with LLMOPT_DEVERR_WAIT_TIMEOUT: which wait gave up. */
+#define LLMOPT_DEVERR_WAIT_DATA 0x100u  /* a consumer waiting for a staged K/V tile     */
+#define LLMOPT_DEVERR_WAIT_SLOT 0x200u  /* the copy issuer waiting for a free slot      */
+#define LLMOPT_DEVERR_WAIT_DRAIN 0x400u /* the copy issuer waiting for its last copies  */
+#define LLMOPT_DEVERR_WAIT_PEER 0x800u  /* the cross-rank barrier of a gathered call    */
 
 /* split_tokens argument of the attention entry points. */
 #define LLMOPT_SPLIT_AUTO 0LL  /* balanced split-K chosen from context and SM count */

@@ -27,6 +27,10 @@ ERR_INDEX = 5
 DEVERR_BLOCK_ID = 1
 DEVERR_TABLE_WIDTH = 2
 DEVERR_WAIT_TIMEOUT = 4
+DEVERR_WAIT_DATA = 0x100
+DEVERR_WAIT_SLOT = 0x200
+DEVERR_WAIT_DRAIN = 0x400
+DEVERR_WAIT_PEER = 0x800
 
 SPLIT_AUTO = 0
 SPLIT_NONE = -1

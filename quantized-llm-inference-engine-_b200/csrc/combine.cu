@@ -66,19 +66,22 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) combine_kernel(const AttnAr
 // The CTA's stores (local and over NVLink) are ordered before its arrival by
 // the barrier plus thread 0's system-scope fence (fences are cumulative).  The
 // last CTA of this rank then writes `epoch` into its slot of every rank's
-// flags with release semantics and waits, with acquire loads, until every
-// rank's slot in its own flags has reached `epoch`: after that every rank's
-// rows are in this rank's gathered output.  The wait gives up after
-// kWaitLimitCycles and records kErrWaitTimeout instead of hanging.
+// flags (release: a fence, then relaxed stores) and polls its own flags until
+// every rank's slot has reached `epoch` (then an acquire fence): after that
+// every rank's rows are in this rank's gathered output.  The wait gives up
+// after kWaitLimitCycles and records kErrWaitTimeout instead of hanging.
 __device__ __forceinline__ void peer_barrier(const PeerArgs& p, unsigned* err) {
   __syncthreads();
   if (threadIdx.x != 0) return;
   __threadfence_system();
   const unsigned arrived = atomicAdd(p.counter, 1u);
   if (arrived != gridDim.x - 1) return;
+  // One release fence covers every flag store after it (fence + relaxed
+  // stores is a release pattern), so the stores to the peers are issued back
+  // to back instead of each waiting for the previous one to be acknowledged.
   __threadfence_system();
   for (int r = 0; r < p.world; ++r) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flags[r] + p.rank), "r"(p.epoch)
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p.flags[r] + p.rank), "r"(p.epoch)
                  : "memory");
   }
   const unsigned* mine = p.flags[p.rank];
@@ -87,15 +90,18 @@ __device__ __forceinline__ void peer_barrier(const PeerArgs& p, unsigned* err) {
   for (int r = 0; r < p.world && !timed_out; ++r) {
     while (true) {
       unsigned v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
+      asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
       if ((int)(v - p.epoch) >= 0) break;
       if (clock64() - t0 > kWaitLimitCycles) {
-        record_error(err, kErrWaitTimeout);
+        record_error(err, kErrWaitTimeout | kErrWaitPeer);
         timed_out = true;
         break;
       }
     }
   }
+  // Acquire side of the pattern: the peers' rows are visible to this grid's
+  // completion (and so to every later kernel on the stream) after this fence.
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
   *p.counter = 0u;
 }
 

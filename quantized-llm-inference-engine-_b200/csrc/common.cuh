@@ -20,6 +20,11 @@ enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
 constexpr unsigned kErrBlockId = 1u;
 constexpr unsigned kErrTableWidth = 2u;
 constexpr unsigned kErrWaitTimeout = 4u;
+// Which wait gave up (set together with kErrWaitTimeout).
+constexpr unsigned kErrWaitData = 0x100u;   // consumer waiting for a staged tile
+constexpr unsigned kErrWaitSlot = 0x200u;   // producer waiting for a free ring slot
+constexpr unsigned kErrWaitDrain = 0x400u;  // producer waiting for its last copies
+constexpr unsigned kErrWaitPeer = 0x800u;   // cross-rank barrier of a gathered call
 
 // About one second at B200 clocks: a wait that long means a lost producer.
 constexpr long long kWaitLimitCycles = 2000000000LL;

@@ -221,7 +221,7 @@ __global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
           const int st = (int)(it % nstages);
           const long long round = it / nstages;
           if (round > 0 && !mbar_wait(&sm.empty[st], (unsigned)((round - 1) & 1))) {
-            record_error(a.err, kErrWaitTimeout);
+            record_error(a.err, kErrWaitTimeout | kErrWaitSlot);
           }
           sm.meta[st] = nt_i;
           if (nt_i > 0) {
@@ -250,7 +250,7 @@ __global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
       const long long first = total > nstages ? total - nstages : 0;
       for (long long it = first; it < total; ++it) {
         if (!mbar_wait(&sm.full[it % nstages], (unsigned)((it / nstages) & 1))) {
-          record_error(a.err, kErrWaitTimeout);
+          record_error(a.err, kErrWaitTimeout | kErrWaitDrain);
         }
       }
     }
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
     for (long long f = cur; f < seg_end; ++f, ++it) {
       const int st = (int)(it % nstages);
       if (!mbar_wait(&sm.full[st], (unsigned)((it / nstages) & 1))) {
-        record_error(a.err, kErrWaitTimeout);
+        record_error(a.err, kErrWaitTimeout | kErrWaitData);
       }
       const int ntok = sm.meta[st];
       if (ntok > 0) {
