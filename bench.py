@@ -376,7 +376,12 @@ def run_ours(args) -> None:
 
     for _ in range(max(args.warmup, 3)):
         step()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    # Per-kernel events break the programmatic-launch overlap between the
+    # step's kernels, so only every EVERY-th timed step carries them; the step
+    # time itself is the whole timed region.
+    every = 10
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)]
+           for _ in range((args.steps + every - 1) // every)]
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local)
@@ -384,7 +389,7 @@ def run_ours(args) -> None:
     sampler.start()
     start.record()
     for i in range(args.steps):
-        step(evs[i])
+        step(evs[i // every] if i % every == 0 else None)
     end.record()
     torch.cuda.synchronize(dev)
     clocks = sampler.stop()
@@ -424,33 +429,69 @@ def run_ours(args) -> None:
 
         for hv, t in zip(views(host), srcs):
             hv.copy_(t.cpu())
-        q_d, k_d, v_d, table_d, ctx_d, offs_d = views(dev_buf)
-        # Each rank reads back its own heads of the result, so the job as a whole
-        # copies the output to the host exactly once.
-        out_h = torch.empty((B, qh, 1, HEAD_DIM), dtype=torch.bfloat16, pin_memory=True)
+        # Two device input slots and two pinned output slots: step i's inputs
+        # cross PCIe on one copy stream while step i-1 computes, and its result
+        # comes back on another copy stream while step i+1 computes.  Every
+        # copy of every step is inside the timed region.
+        dev_bufs = [dev_buf, torch.empty(total, dtype=torch.uint8, device=dev)]
+        slots_in = [views(b) for b in dev_bufs]
+        # Each rank reads back its own heads of the result (head-major, contiguous),
+        # so the job as a whole copies the output to the host exactly once.
+        out_shape = (qh, B, 1, HEAD_DIM) if world > 1 else (B, qh, 1, HEAD_DIM)
+        out_h = [torch.empty(out_shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
+        out_d = [torch.empty((B, qh, 1, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+                 for _ in range(2)]
         sharded = (pdist.ShardedPagedAttention(HEADS, KV_HEADS, HEAD_DIM,
                                                transport=args.transport)
                    if world > 1 else None)
+        comp = torch.cuda.current_stream(dev)
+        h2d_stream = torch.cuda.Stream(dev)
+        d2h_stream = torch.cuda.Stream(dev)
+        in_ready = [torch.cuda.Event() for _ in range(2)]
+        comp_done = [torch.cuda.Event() for _ in range(2)]
+        out_done = [torch.cuda.Event() for _ in range(2)]
+        for ev_list in (comp_done, out_done):
+            for ev in ev_list:
+                ev.record(comp)
+
+        counter = [0]   # one count across warm-up and timed steps: slots keep alternating
 
         def e2e_step():
-            dev_buf.copy_(host, non_blocking=True)
+            slot = counter[0] & 1
+            counter[0] += 1
+            with torch.cuda.stream(h2d_stream):
+                h2d_stream.wait_event(comp_done[slot])      # step i-2 no longer reads the slot
+                dev_bufs[slot].copy_(host, non_blocking=True)
+                in_ready[slot].record(h2d_stream)
+            comp.wait_event(in_ready[slot])
+            comp.wait_event(out_done[slot])                 # step i-2's result has left
+            q_d, k_d, v_d, table_d, ctx_d, offs_d = slots_in[slot]
             cache.write_decode(0, table_d, offs_d, k_d, v_d)
             if world > 1:
-                out = sharded.forward(q_d, cache, 0, table_d, ctx_d, 1)
-                out = out[:, shard.q_lo:shard.q_hi]
+                full = sharded.forward(q_d, cache, 0, table_d, ctx_d, 1)
+                res = full.permute(1, 0, 2, 3)[shard.q_lo:shard.q_hi]
             else:
-                out = attn.forward(q_d, cache, 0, table_d, ctx_d, 1)
-            out_h.copy_(out, non_blocking=True)
+                res = attn.forward_with_lse(q_d, cache, 0, table_d, ctx_d, 1, want_lse=False,
+                                            out=out_d[slot])[0]
+            comp_done[slot].record(comp)
+            with torch.cuda.stream(d2h_stream):
+                d2h_stream.wait_event(comp_done[slot])
+                out_h[slot].copy_(res, non_blocking=True)
+                out_done[slot].record(d2h_stream)
 
         for _ in range(max(args.warmup, 3)):
             e2e_step()
         e_start = torch.cuda.Event(enable_timing=True)
         e_end = torch.cuda.Event(enable_timing=True)
         barrier()
-        e_start.record()
+        e_start.record(comp)
+        h2d_stream.wait_stream(comp)
+        d2h_stream.wait_stream(comp)
         for _ in range(args.steps):
             e2e_step()
-        e_end.record()
+        comp.wait_stream(h2d_stream)
+        comp.wait_stream(d2h_stream)
+        e_end.record(comp)
         torch.cuda.synchronize(dev)
         e_ms = e_start.elapsed_time(e_end)
         if world > 1:
@@ -461,7 +502,8 @@ def run_ours(args) -> None:
         e2e = {"value": round(world * (dec_bytes + app_bytes) / (e_ms / args.steps * 1e-3) / 1e9,
                               2),
                "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()),
+               "d2h_bytes_per_step": int(out_h[0].numel() * out_h[0].element_size()),
+               "copies": "pipelined: H2D and D2H on two copy streams, two slots each",
                "ms_per_step": round(e_ms / args.steps, 4),
                "decode_tok_s": round(B / (e_ms / args.steps * 1e-3), 1)}
 
@@ -620,8 +662,11 @@ def run_extra(args) -> None:
     attn = pkg.PagedAttention(qh, kvh, HEAD_DIM)
     head_major = torch.empty((qh, B, q_len, HEAD_DIM), dtype=torch.bfloat16, device=dev)
     out_view = head_major.permute(1, 0, 2, 3)
+    peer = world > 1 and args.transport == "peer"
     gathered = (torch.empty((H, B, q_len, HEAD_DIM), dtype=torch.bfloat16, device=dev)
-                if world > 1 else None)
+                if world > 1 and not peer else None)
+    sharded = (pdist.ShardedPagedAttention(H, KVH, HEAD_DIM, transport="peer")
+               if peer else None)
 
     def step(ev=None):
         if ev is not None:
@@ -632,15 +677,20 @@ def run_extra(args) -> None:
             cache.write_decode(0, table, offs, knew, vnew)
         if ev is not None:
             ev[1].record()
-        attn.forward_with_lse(q, cache, 0, table, ctx, q_len, want_lse=False, out=out_view)
+        if peer:
+            sharded.forward(q, cache, 0, table, ctx, q_len)
+        else:
+            attn.forward_with_lse(q, cache, 0, table, ctx, q_len, want_lse=False, out=out_view)
         if ev is not None:
             ev[2].record()
-        if world > 1:
+        if gathered is not None:
             dist.all_gather_into_tensor(gathered, head_major)
 
     for _ in range(max(args.warmup, 3)):
         step()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    every = 10   # per-kernel events on every 10th step only (they break launch overlap)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)]
+           for _ in range((args.steps + every - 1) // every)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize(dev)
     if world > 1:
@@ -649,7 +699,7 @@ def run_extra(args) -> None:
     sampler.start()
     start.record()
     for i in range(args.steps):
-        step(evs[i])
+        step(evs[i // every] if i % every == 0 else None)
     end.record()
     torch.cuda.synchronize(dev)
     clocks = sampler.stop()
@@ -663,6 +713,8 @@ def run_extra(args) -> None:
     attn_ms = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
     if rank == 0:
         line = {"config": args.config, "workload": wl["note"], "n_gpus": world,
+                "exchange": (("combine fused with the all-gather (NVLink peer stores)" if peer
+                              else "NCCL all-gather") if world > 1 else None),
                 "scaling": wl["scaling"], "steps": args.steps, "ms_per_step": round(ms_step, 5),
                 "append_ms": round(append_ms, 5), "attention_ms": round(attn_ms, 5),
                 "clocks": clocks}
@@ -696,6 +748,8 @@ def run_extra(args) -> None:
                 line["l2_reuse_logical_over_unique"] = round(
                     int(wl["ctx"].sum()) / wl["unique_tokens"], 2)
         print(json.dumps(line), flush=True)
+    if sharded is not None:
+        sharded.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
