@@ -24,6 +24,10 @@
  *   llmopt_kv_write         <- PagedKVCache.write  src/llmopt/cache/paged_cache.py:175-232
  *   llmopt_kv_write_decode  <- PagedKVCache.write_decode  paged_cache.py:234-261
  *   llmopt_paged_gather     <- PagedKVCache.gather  paged_cache.py:263-312
+ *   llmopt_rope_kv_append   <- the rotary + append statements of
+ *                              PagedAttentionLayer.forward  src/llmopt/model/layers.py:106-134
+ *                              (RotaryEmbedding.forward, apply_rotary_pos_emb
+ *                              src/llmopt/model/rotary.py:16-46, 103-121)
  */
 #ifndef LLMOPT_B200_H_
 #define LLMOPT_B200_H_
@@ -64,6 +68,7 @@ enum {
 #define LLMOPT_DEVERR_BLOCK_ID 1u      /* block id >= num_blocks (access skipped)     */
 #define LLMOPT_DEVERR_TABLE_WIDTH 2u   /* position beyond the block-table row         */
 #define LLMOPT_DEVERR_WAIT_TIMEOUT 4u  /* a bounded on-device wait gave up            */
+#define LLMOPT_DEVERR_POSITION 8u      /* rotary position outside the table (skipped)  */
 /* Set together with LLMOPT_DEVERR_WAIT_TIMEOUT: which wait gave up. */
 #define LLMOPT_DEVERR_WAIT_DATA 0x100u  /* a consumer waiting for a staged K/V tile     */
 #define LLMOPT_DEVERR_WAIT_SLOT 0x200u  /* the copy issuer waiting for a free slot      */
@@ -286,6 +291,35 @@ LLMOPT_API int llmopt_paged_gather(const void* key_cache, const void* value_cach
                         int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
                         int64_t batch, int64_t max_len, void* out_keys, void* out_values,
                         uint8_t* valid, uint32_t* err, void* stream);
+
+/*
+ * Rotary embedding of q and k fused with the K/V append: the statements of
+ * PagedAttentionLayer.forward between the projections and attention
+ * (layers.py:106-134).  q_proj [batch * q_len, num_heads * head_dim], k_proj /
+ * v_proj [batch * q_len, num_kv_heads * head_dim] (rows of tokens, row strides
+ * q_row / k_row / v_row, unit inner stride, dtype in_dtype = the model dtype);
+ * positions [batch * q_len]; cos_table / sin_table [max_positions, head_dim]
+ * (table_dtype; RotaryEmbedding.cos_cached / sin_cached).  The cos/sin rows are
+ * cast to in_dtype, q and k rotated as x * cos + rotate_half(x) * sin with each
+ * product and the sum rounded to in_dtype (bit-identical to the reference's
+ * tensor ops); the rotated query goes to q_out (in_dtype, strides (seq, head,
+ * token) of a [batch, num_heads, q_len, head_dim] view), the rotated k and the
+ * v rows to the cache at the offsets, cast to kv_dtype, with the rules of
+ * llmopt_kv_write_decode when q_len == 1 and llmopt_kv_write otherwise.
+ * head_dim must be even.  A position >= max_positions or < -max_positions
+ * skips its token and sets LLMOPT_DEVERR_POSITION (the reference raises
+ * ValueError after a host sync; no sync happens here).
+ */
+LLMOPT_API int llmopt_rope_kv_append(
+    const void* q_proj, const void* k_proj, const void* v_proj, int32_t in_dtype, int64_t q_row,
+    int64_t k_row, int64_t v_row, const void* positions, int32_t pos_is_i64,
+    const void* cos_table, const void* sin_table, int32_t table_dtype, int64_t max_positions,
+    void* q_out, int64_t qo_s, int64_t qo_h, int64_t qo_t, void* key_cache, void* value_cache,
+    int32_t kv_dtype, int32_t num_layers, int32_t num_blocks, int32_t block_size,
+    int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx, const void* block_table,
+    int32_t table_is_i64, int64_t table_width, int64_t table_stride, const void* token_offsets,
+    int32_t off_is_i64, int64_t batch, int32_t num_heads, int32_t q_len, uint32_t* err,
+    void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

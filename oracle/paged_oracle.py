@@ -16,6 +16,10 @@ that the CUDA kernels can be compared against it on identical inputs:
   (``_expand_kv`` :189-210, ``_build_mask`` :212-229, ``_forward_dense``
   :231-250, ``_forward_split`` :252-293)
 * ``merge_states``             src/llmopt/attention/paged_attention.py:30-55
+* the rotary + KV-append half of ``PagedAttentionLayer.forward``
+  src/llmopt/model/layers.py:106-134 (``RotaryEmbedding.forward``
+  src/llmopt/model/rotary.py:103-121, ``apply_rotary_pos_emb`` :23-46,
+  ``rotate_half`` :16-20)
 
 Parity of this restatement is pinned against golden vectors produced by the
 reference implementation itself (``tests/golden/make_golden.py`` imports the
@@ -51,6 +55,7 @@ __all__ = [
     "write",
     "write_decode",
     "merge_states",
+    "rope_append",
     "paged_attention",
     "attention_lse",
     "decode_bytes",
@@ -233,6 +238,66 @@ def write_decode(key_cache: np.ndarray, value_cache: np.ndarray, kind: str, laye
     for s in range(B):
         key_cache[layer, blocks[s], slot[s]] = convert(keys[s], in_kind, kind)
         value_cache[layer, blocks[s], slot[s]] = convert(values[s], in_kind, kind)
+
+
+# ---------------------------------------------------------------------------
+# rotary embedding + KV append
+# ---------------------------------------------------------------------------
+
+def _round_kind(x: np.ndarray, kind: str) -> np.ndarray:
+    """float32 values rounded to ``kind`` and widened back (one torch op's result)."""
+    return to_f32(from_f32(np.asarray(x, dtype=np.float32), kind), kind)
+
+
+def _rotate(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, kind: str) -> np.ndarray:
+    """``x * cos + rotate_half(x) * sin`` with every torch op rounded to ``kind``
+    (rotary.py:16-20, :46): two products, then their sum."""
+    half = x.shape[-1] // 2
+    rot = np.concatenate((-x[..., half:], x[..., :half]), axis=-1)   # exact negation
+    a = _round_kind(x * cos, kind)
+    b = _round_kind(rot * sin, kind)
+    return _round_kind(a + b, kind)
+
+
+def rope_append(q_proj: np.ndarray, k_proj: np.ndarray, v_proj: np.ndarray, model_kind: str,
+                positions: np.ndarray, cos_table: np.ndarray, sin_table: np.ndarray,
+                table_kind: str, key_cache: np.ndarray, value_cache: np.ndarray, kv_kind: str,
+                layer: int, block_ids: np.ndarray, token_offsets: np.ndarray, seq: int,
+                q_len: int, heads: int, kv_heads: int) -> np.ndarray:
+    """Restates the rotary + KV-append steps of ``PagedAttentionLayer.forward``
+    (layers.py:106-134).
+
+    ``q_proj`` / ``k_proj`` / ``v_proj`` are the projection outputs
+    ``[seq * q_len, heads * D]`` / ``[seq * q_len, kv_heads * D]`` of kind
+    ``model_kind``; ``positions`` is ``[seq * q_len]``.  The cos/sin rows of the
+    positions are cast to the model kind (rotary.py:116-120), q and k are
+    rotated with per-op rounding (rotary.py:46), and the rotated k with the
+    unrotated v are appended to the cache through ``write_decode`` when
+    ``q_len == 1`` and ``write`` otherwise (layers.py:125-132).  Mutates the
+    caches; returns the rotated query ``[seq, q_len, heads, D]`` of
+    ``model_kind`` (the reference keeps it as a permuted view).
+    """
+    d = cos_table.shape[-1]
+    positions = np.asarray(positions).astype(np.int64)
+    n_pos = cos_table.shape[0]
+    if positions.size and int(positions.max()) >= n_pos:          # rotary.py:111-115
+        raise ValueError(f"position {int(positions.max())} exceeds table length {n_pos}")
+    cos = _round_kind(to_f32(cos_table, table_kind)[positions], model_kind)   # [T, D]
+    sin = _round_kind(to_f32(sin_table, table_kind)[positions], model_kind)
+    cos = cos.reshape(seq, q_len, 1, d)
+    sin = sin.reshape(seq, q_len, 1, d)
+    q = to_f32(q_proj, model_kind).reshape(seq, q_len, heads, d)
+    k = to_f32(k_proj, model_kind).reshape(seq, q_len, kv_heads, d)
+    v = v_proj.reshape(seq, q_len, kv_heads, d)
+    q_rot = from_f32(_rotate(q, cos, sin, model_kind), model_kind)
+    k_rot = from_f32(_rotate(k, cos, sin, model_kind), model_kind)
+    if q_len == 1:
+        write_decode(key_cache, value_cache, kv_kind, layer, block_ids, token_offsets,
+                     k_rot[:, 0], v[:, 0], model_kind)
+    else:
+        write(key_cache, value_cache, kv_kind, layer, block_ids, token_offsets, k_rot, v,
+              model_kind)
+    return q_rot
 
 
 # ---------------------------------------------------------------------------

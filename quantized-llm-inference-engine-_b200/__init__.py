@@ -22,6 +22,7 @@ from ._lib import check, lib, version
 from .attention import AttentionBackend, PagedAttention, PagedAttentionConfig, merge_states
 from .cache import PagedKVCache
 from .install import install, uninstall
+from .rope import RotaryEmbedding, rope_kv_append
 
 __all__ = [
     "AttentionBackend",
@@ -29,6 +30,8 @@ __all__ = [
     "PagedAttentionConfig",
     "PagedKVCache",
     "merge_states",
+    "RotaryEmbedding",
+    "rope_kv_append",
     "install",
     "uninstall",
     "lib",

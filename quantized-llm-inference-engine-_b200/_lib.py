@@ -27,6 +27,7 @@ ERR_INDEX = 5
 DEVERR_BLOCK_ID = 1
 DEVERR_TABLE_WIDTH = 2
 DEVERR_WAIT_TIMEOUT = 4
+DEVERR_POSITION = 8
 DEVERR_WAIT_DATA = 0x100
 DEVERR_WAIT_SLOT = 0x200
 DEVERR_WAIT_DRAIN = 0x400
@@ -104,6 +105,13 @@ SIGNATURES = {
     "llmopt_paged_gather": [
         _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
         _p, _i32, _i64, _i64, _p, _i32, _i64, _i64, _p, _p, _p, _p, _p],
+    "llmopt_rope_kv_append": [
+        _p, _p, _p, _i32, _i64, _i64, _i64,           # q/k/v projections, dtype, row strides
+        _p, _i32, _p, _p, _i32, _i64,                 # positions, is64, cos, sin, dtype, rows
+        _p, _i64, _i64, _i64,                         # q_out, strides
+        _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,   # caches, dtype, L, NB, BS, KVH, D, layer
+        _p, _i32, _i64, _i64, _p, _i32,               # table, is64, width, stride, offsets, is64
+        _i64, _i32, _i32, _p, _p],                    # batch, heads, q_len, err, stream
 }
 
 _RESTYPES = {

@@ -893,6 +893,83 @@ int llmopt_paged_gather(const void* key_cache, const void* value_cache, int32_t 
 
 }  // extern "C"
 
+
+extern "C" int llmopt_rope_kv_append(
+    const void* q_proj, const void* k_proj, const void* v_proj, int32_t in_dtype, int64_t q_row,
+    int64_t k_row, int64_t v_row, const void* positions, int32_t pos_is_i64,
+    const void* cos_table, const void* sin_table, int32_t table_dtype, int64_t max_positions,
+    void* q_out, int64_t qo_s, int64_t qo_h, int64_t qo_t, void* key_cache, void* value_cache,
+    int32_t kv_dtype, int32_t num_layers, int32_t num_blocks, int32_t block_size,
+    int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx, const void* block_table,
+    int32_t table_is_i64, int64_t table_width, int64_t table_stride, const void* token_offsets,
+    int32_t off_is_i64, int64_t batch, int32_t num_heads, int32_t q_len, uint32_t* err,
+    void* stream) {
+  if (!valid_dtype(in_dtype) || !valid_dtype(table_dtype)) {
+    return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported input or table dtype");
+  }
+  int st = check_cache_args(kv_dtype, num_layers, num_blocks, block_size, num_kv_heads, head_dim,
+                            layer_idx, table_width, table_stride);
+  if (st != LLMOPT_OK) return st;
+  if (head_dim % 2 != 0) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "head_dim must be even for rotary embeddings");
+  }
+  if (num_heads < 1 || num_heads % num_kv_heads != 0) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "num_heads must be divisible by num_kv_heads");
+  }
+  if (batch < 0 || q_len < 0 || max_positions < 1) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
+  }
+  if (batch == 0 || q_len == 0) return ok();
+  if (table_width == 0) return fail(LLMOPT_ERR_INDEX, "empty block table");
+  if (!q_proj || !k_proj || !v_proj || !positions || !cos_table || !sin_table || !q_out ||
+      !key_cache || !value_cache || !block_table || !token_offsets) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null pointer argument");
+  }
+  if (q_row < (int64_t)num_heads * head_dim || k_row < (int64_t)num_kv_heads * head_dim ||
+      v_row < (int64_t)num_kv_heads * head_dim) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "projection row stride shorter than a row");
+  }
+  RopeArgs a{};
+  a.q_in = q_proj;
+  a.k_in = k_proj;
+  a.v_in = v_proj;
+  a.in_dtype = in_dtype;
+  a.q_row = q_row;
+  a.k_row = k_row;
+  a.v_row = v_row;
+  a.positions = positions;
+  a.pos_i64 = pos_is_i64 ? 1 : 0;
+  a.cos_t = cos_table;
+  a.sin_t = sin_table;
+  a.tab_dtype = table_dtype;
+  a.max_pos = max_positions;
+  a.q_out = q_out;
+  a.qo_s = qo_s;
+  a.qo_h = qo_h;
+  a.qo_t = qo_t;
+  a.k_cache = key_cache;
+  a.v_cache = value_cache;
+  a.kv_dtype = kv_dtype;
+  a.num_layers = num_layers;
+  a.num_blocks = num_blocks;
+  a.block_size = block_size;
+  a.kv_heads = num_kv_heads;
+  a.head_dim = head_dim;
+  a.layer = layer_idx;
+  a.table = block_table;
+  a.table_i64 = table_is_i64 ? 1 : 0;
+  a.table_width = table_width;
+  a.table_stride = table_stride;
+  a.offsets = token_offsets;
+  a.off_i64 = off_is_i64 ? 1 : 0;
+  a.batch = batch;
+  a.num_heads = num_heads;
+  a.q_len = q_len;
+  a.err = err;
+  cudaError_t e = rope_append_launch(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope_append launch");
+  return ok();
+}
 // ---------------------------------------------------------------------------
 // llmopt_paged_attention_noalloc: paged attention whose split-K scratch is a
 // fixed array compiled into this library instead of caller-provided memory.

@@ -20,6 +20,7 @@ enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
 constexpr unsigned kErrBlockId = 1u;
 constexpr unsigned kErrTableWidth = 2u;
 constexpr unsigned kErrWaitTimeout = 4u;
+constexpr unsigned kErrPosition = 8u;       // rotary position outside the table (token skipped)
 // Which wait gave up (set together with kErrWaitTimeout).
 constexpr unsigned kErrWaitData = 0x100u;   // consumer waiting for a staged tile
 constexpr unsigned kErrWaitSlot = 0x200u;   // producer waiting for a free ring slot

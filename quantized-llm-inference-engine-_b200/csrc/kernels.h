@@ -132,6 +132,38 @@ struct KvWriteArgs {
 cudaError_t kv_write_launch(const KvWriteArgs& a, cudaStream_t stream);
 cudaError_t kv_write_decode_launch(const KvWriteArgs& a, cudaStream_t stream);
 
+// Rotary embedding of q and k fused with the K/V append (the attention layer's
+// step before attention).
+struct RopeArgs {
+  const void* q_in;              // [tokens, heads * head_dim] rows, model dtype
+  const void* k_in;              // [tokens, kv_heads * head_dim]
+  const void* v_in;
+  int in_dtype;
+  long long q_row, k_row, v_row; // token-row strides (elements)
+  const void* positions;         // [tokens] = [batch * q_len]
+  int pos_i64;
+  const void* cos_t;             // [max_pos, head_dim]
+  const void* sin_t;
+  int tab_dtype;
+  long long max_pos;
+  void* q_out;                   // rotated query, model dtype, strides (seq, head, token)
+  long long qo_s, qo_h, qo_t;
+  void* k_cache;
+  void* v_cache;
+  int kv_dtype;
+  int num_layers, num_blocks, block_size, kv_heads, head_dim, layer;
+  const void* table;
+  int table_i64;
+  long long table_width, table_stride;
+  const void* offsets;
+  int off_i64;
+  long long batch;
+  int num_heads;
+  int q_len;
+  unsigned* err;
+};
+cudaError_t rope_append_launch(const RopeArgs& a, cudaStream_t stream);
+
 struct GatherArgs {
   const void* k_cache;
   const void* v_cache;

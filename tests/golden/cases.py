@@ -220,6 +220,67 @@ WRITE_CASES = {
 }
 
 
+# ---------------------------------------------------------------------------
+# Rotary embedding + KV append cases (bit-exact)
+# ---------------------------------------------------------------------------
+
+def case_rope(seed: int = 30, model_kind: str = "bf16", kv_kind: str = "bf16", q_len: int = 1,
+              heads: int = 8, kv_heads: int = 2, head_dim: int = 64, max_pos: int = 96,
+              base: float = 10000.0) -> dict:
+    """The rotary + append step of the attention layer.  Decode (q_len 1) uses
+    write_decode with a -1 entry (redirected to block 0) and a negative offset;
+    chunks use write with odd offsets and a -1 that stops a sequence's walk.
+    Positions include 0 and the last table row."""
+    rng = np.random.default_rng(seed)
+    bs = 8
+    if q_len == 1:
+        seq, width, nb = 6, 5, 32
+        table = np.full((seq, width), -1, dtype=np.int64)
+        perm = rng.permutation(nb)
+        for s in range(seq):
+            table[s] = perm[(5 * s) % 27:(5 * s) % 27 + 5]
+        table[2, 1] = -1
+        offsets = np.array([0, 7, 9, 3, 33, -1], dtype=np.int64)
+        positions = np.array([0, 7, max_pos - 1, 3, 33, 50], dtype=np.int64)
+    else:
+        seq, width, nb = 3, 6, 30
+        table = np.full((seq, width), -1, dtype=np.int64)
+        perm = rng.permutation(nb)
+        table[0, :4] = perm[0:4]
+        table[1, :6] = perm[4:10]
+        table[2, :2] = perm[10:12]               # -1 at column 2 stops the walk
+        offsets = np.array([3, 13, 5], dtype=np.int64)
+        positions = np.concatenate([off + np.arange(q_len) for off in offsets]).astype(np.int64)
+        positions[-1] = max_pos - 1
+    T = seq * q_len
+    q_proj = from_f32(_normal(rng, (T, heads * head_dim), 2.0), model_kind)
+    k_proj = from_f32(_normal(rng, (T, kv_heads * head_dim), 2.0), model_kind)
+    v_proj = from_f32(_normal(rng, (T, kv_heads * head_dim), 2.0), model_kind)
+    shape = (2, nb, bs, kv_heads, head_dim)
+    kc = from_f32(_normal(rng, shape), kv_kind)
+    vc = from_f32(_normal(rng, shape), kv_kind)
+    return dict(q_proj=q_proj, k_proj=k_proj, v_proj=v_proj, positions=positions,
+                key_cache=kc, value_cache=vc, block_ids=table, token_offsets=offsets,
+                model_kind=model_kind, kv_kind=kv_kind, layer=1, seq=seq, q_len=q_len,
+                heads=heads, kv_heads=kv_heads, head_dim=head_dim, max_pos=max_pos, base=base)
+
+
+ROPE_CASES = {
+    "rope_decode_bf16": lambda: case_rope(),
+    "rope_chunk_bf16": lambda: case_rope(seed=31, q_len=11, heads=4, kv_heads=2, head_dim=32),
+    "rope_chunk_f32_to_bf16": lambda: case_rope(seed=32, model_kind="f32", q_len=7, heads=6,
+                                                kv_heads=3, head_dim=16),
+    "rope_decode_f16_to_f32": lambda: case_rope(seed=33, model_kind="f16", kv_kind="f32",
+                                                head_dim=128, heads=4, kv_heads=1),
+}
+
+
+def rope_checksum(case: dict) -> str:
+    return checksum(case["q_proj"], case["k_proj"], case["v_proj"], case["positions"],
+                    case["key_cache"], case["value_cache"], case["block_ids"],
+                    case["token_offsets"])
+
+
 def write_checksum(case: dict) -> str:
     return checksum(case["key_cache"], case["value_cache"], case["block_ids"],
                     case["token_offsets"], case["keys"], case["values"])

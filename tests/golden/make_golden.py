@@ -2,7 +2,7 @@
 
 Run once, in a container where the reference source is present::
 
-    python tests/golden/make_golden.py /path/to/reference/src
+    python tests/golden/make_golden.py /path/to/reference/src [--only=rope]
 
 It imports ``llmopt.attention`` / ``llmopt.cache`` from that path, runs them
 on CPU on the seeded inputs of ``cases.py`` (plus the reference's own
@@ -19,6 +19,9 @@ Recorded per attention run:
   (only for non-fp32 caches): a loose pin (2e-2 absolute);
 * ``lse`` - ``torch.logsumexp`` of the reference's masked, scaled scores (the
   formula of ``_forward_split``), for the LSE parity check.
+
+Rotary + append cases (``rope_*.npz``) record the reference's cos/sin tables,
+the rotated query and the caches after the append, bit for bit.
 """
 
 from __future__ import annotations
@@ -153,6 +156,47 @@ def make_write(name: str, build, PagedKVCache) -> dict:
     return out
 
 
+def make_rope(build, RotaryEmbedding, apply_rotary_pos_emb, PagedKVCache) -> dict:
+    """Runs the rotary + append statements of ``PagedAttentionLayer.forward``
+    (layers.py:106-134) with the reference's own RotaryEmbedding, rotation and
+    cache, on CPU."""
+    import torch
+
+    case = build()
+    out = {"checksum": np.array(cases.rope_checksum(case))}
+    seq, q_len = case["seq"], case["q_len"]
+    H, KVH, D = case["heads"], case["kv_heads"], case["head_dim"]
+    mk = case["model_kind"]
+    rotary = RotaryEmbedding(D, case["max_pos"], case["base"])
+    q = _torch_from(case["q_proj"], mk).view(seq, q_len, H, D).permute(0, 2, 1, 3)
+    k = _torch_from(case["k_proj"], mk).view(seq, q_len, KVH, D).permute(0, 2, 1, 3)
+    v = _torch_from(case["v_proj"], mk).view(seq, q_len, KVH, D).permute(0, 2, 1, 3)
+    positions = torch.from_numpy(case["positions"].copy())
+    cos, sin = rotary(positions, dtype=q.dtype)
+    cos = cos.view(seq, q_len, D).unsqueeze(1)
+    sin = sin.view(seq, q_len, D).unsqueeze(1)
+    q, k = apply_rotary_pos_emb(q, k, cos, sin)
+    batched_k = k.permute(0, 2, 1, 3).contiguous()
+    batched_v = v.permute(0, 2, 1, 3).contiguous()
+    L, nb, bs, _, _ = case["key_cache"].shape
+    cache = PagedKVCache(L, nb, bs, KVH, D, dtype=_kind_dtype(case["kv_kind"]))
+    cache.key_cache.copy_(_torch_from(case["key_cache"], case["kv_kind"]))
+    cache.value_cache.copy_(_torch_from(case["value_cache"], case["kv_kind"]))
+    table = torch.from_numpy(case["block_ids"].copy())
+    offs = torch.from_numpy(case["token_offsets"].copy())
+    if q_len == 1:
+        cache.write_decode(case["layer"], table, offs, batched_k[:, 0], batched_v[:, 0])
+    else:
+        cache.write(case["layer"], table, offs, batched_k, batched_v)
+    out["cos_table"] = rotary.cos_cached.numpy().copy()
+    out["sin_table"] = rotary.sin_cached.numpy().copy()
+    out["q_rot"] = _np_from(q.permute(0, 2, 1, 3), mk)          # [seq, q_len, H, D]
+    # Only the written layer is stored; the test checks the others are untouched.
+    out["key_layer"] = _np_from(cache.key_cache[case["layer"]], case["kv_kind"])
+    out["value_layer"] = _np_from(cache.value_cache[case["layer"]], case["kv_kind"])
+    return out
+
+
 def make_fixture(PagedAttention, PagedAttentionConfig, PagedKVCache, BlockPool) -> dict:
     """The reference's ``tests/test_paged_attention.py`` fixture and its four checks,
     with ``pool.append`` run before the chain is read (the shipped order raises)."""
@@ -221,7 +265,7 @@ def make_merge(merge_states) -> dict:
             "out": o.numpy(), "lse": lse.numpy()}
 
 
-def main(ref_src: str) -> None:
+def main(ref_src: str, only: str | None = None) -> None:
     sys.path.insert(0, ref_src)
     import torch
 
@@ -230,6 +274,15 @@ def main(ref_src: str) -> None:
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     meta = {"torch": torch.__version__, "numpy": np.__version__}
+    if only == "rope":
+        from llmopt.model.rotary import RotaryEmbedding, apply_rotary_pos_emb
+
+        for name, build in cases.ROPE_CASES.items():
+            out = make_rope(build, RotaryEmbedding, apply_rotary_pos_emb, PagedKVCache)
+            out["versions"] = np.array(str(meta))
+            np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+            print("wrote", name)
+        return
     for name, build in cases.ATTENTION_CASES.items():
         out = make_attention(name, build, PagedAttention, PagedAttentionConfig, PagedKVCache)
         out["versions"] = np.array(str(meta))
@@ -237,6 +290,13 @@ def main(ref_src: str) -> None:
         print("wrote", name)
     for name, build in cases.WRITE_CASES.items():
         out = make_write(name, build, PagedKVCache)
+        out["versions"] = np.array(str(meta))
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+        print("wrote", name)
+    from llmopt.model.rotary import RotaryEmbedding, apply_rotary_pos_emb
+
+    for name, build in cases.ROPE_CASES.items():
+        out = make_rope(build, RotaryEmbedding, apply_rotary_pos_emb, PagedKVCache)
         out["versions"] = np.array(str(meta))
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
         print("wrote", name)
@@ -250,4 +310,6 @@ def main(ref_src: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLMOPT_REFERENCE_SRC", ""))
+    argv = [a for a in sys.argv[1:] if not a.startswith("--only=")]
+    only = next((a.split("=", 1)[1] for a in sys.argv[1:] if a.startswith("--only=")), None)
+    main(argv[0] if argv else os.environ.get("LLMOPT_REFERENCE_SRC", ""), only)

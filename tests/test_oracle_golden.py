@@ -67,6 +67,37 @@ def test_oracle_write_bit_exact(name):
     assert_bits_equal(vc, gold["value_cache"], case["kv_kind"], f"{name} V")
 
 
+@pytest.mark.parametrize("name", list(cases.ROPE_CASES))
+def test_oracle_rope_append_bit_exact(name):
+    case = cases.ROPE_CASES[name]()
+    gold = load_golden(name)
+    assert str(gold["checksum"]) == cases.rope_checksum(case), "seeded inputs drifted"
+    kc, vc = case["key_cache"].copy(), case["value_cache"].copy()
+    q_rot = po.rope_append(case["q_proj"], case["k_proj"], case["v_proj"], case["model_kind"],
+                           case["positions"], gold["cos_table"], gold["sin_table"], "f32", kc, vc,
+                           case["kv_kind"], case["layer"], case["block_ids"],
+                           case["token_offsets"], case["seq"], case["q_len"], case["heads"],
+                           case["kv_heads"])
+    assert_bits_equal(q_rot, gold["q_rot"], case["model_kind"], f"{name} q")
+    assert_bits_equal(kc[case["layer"]], gold["key_layer"], case["kv_kind"], f"{name} K")
+    assert_bits_equal(vc[case["layer"]], gold["value_layer"], case["kv_kind"], f"{name} V")
+    other = [i for i in range(kc.shape[0]) if i != case["layer"]]
+    assert_bits_equal(kc[other], case["key_cache"][other], case["kv_kind"], f"{name} K other")
+
+
+def test_oracle_rope_rejects_position_past_table():
+    case = cases.ROPE_CASES["rope_decode_bf16"]()
+    gold = load_golden("rope_decode_bf16")
+    pos = case["positions"].copy()
+    pos[0] = case["max_pos"]
+    with pytest.raises(ValueError):
+        po.rope_append(case["q_proj"], case["k_proj"], case["v_proj"], case["model_kind"], pos,
+                       gold["cos_table"], gold["sin_table"], "f32", case["key_cache"].copy(),
+                       case["value_cache"].copy(), case["kv_kind"], case["layer"],
+                       case["block_ids"], case["token_offsets"], case["seq"], case["q_len"],
+                       case["heads"], case["kv_heads"])
+
+
 def test_oracle_reference_fixture():
     """The reference's own test_paged_attention.py fixture and checks."""
     g = load_golden("ref_fixture")
