@@ -63,10 +63,15 @@ def parse_args(argv=None):
                         "peer memory, or NCCL all_gather_into_tensor after it")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--config", choices=("c2", "c3", "c4", "c5"), default="c2",
+    p.add_argument("--config", choices=("c2", "c3", "c4", "c5", "rope", "step"), default="c2",
                    help="c2 (default, the headline line): Llama-3-8B decode; c3: chunked "
                         "prefill; c4: 128k-context decode sharded by KV head (strong "
-                        "scaling); c5: shared-prefix decode (strong scaling)")
+                        "scaling); c5: shared-prefix decode (strong scaling); rope: the "
+                        "fused rotary + KV append of a 16 x 256-token prefill chunk and of "
+                        "a 64-sequence decode step (weak scaling by KV head); step: a whole "
+                        "decode step (device-side metadata advance, rotary append, "
+                        "attention) replayed from a CUDA graph vs launched eagerly, beside "
+                        "the reference runner's host-side metadata build")
     return p.parse_args(argv)
 
 
@@ -755,10 +760,275 @@ def run_extra(args) -> None:
         dist.destroy_process_group()
 
 
+def run_rope(args) -> None:
+    """Fused rotary + KV append (one kernel) against the same steps as the
+    reference layer writes them (layers.py:106-134) in torch ops on the GPU
+    followed by the KV write kernel.  Llama-3-8B heads, bf16, 500k rope base."""
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    pkg = importlib.import_module(PACKAGE)
+    pdist = importlib.import_module(f"{PACKAGE}.dist")
+    shard = pdist.shard_heads(HEADS, KV_HEADS, world, rank)
+    qh, kvh, D = shard.q_heads, shard.kv_heads, HEAD_DIM
+    rot = pkg.RotaryEmbedding(D, 16384, 500000.0, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3000 + rank)
+    peak, peak_kind = measured_hbm_peak()
+    results = {}
+    for name, B, q_len in (("prefill_chunk", 16, 256), ("decode", 64, 1)):
+        rng = np.random.default_rng(args.seed + q_len)
+        ctx0 = rng.integers(1024, 8192, size=B)
+        width = (int(ctx0.max()) + q_len + BLOCK - 1) // BLOCK + 1
+        nblk = B * width
+        table = torch.from_numpy(rng.permutation(nblk).reshape(B, width).astype(np.int32)).to(dev)
+        offs = torch.from_numpy(ctx0.astype(np.int64)).to(dev)
+        pos = (offs[:, None] + torch.arange(q_len, device=dev)[None]).reshape(-1)
+        T = B * q_len
+        qp = torch.randn((T, qh * D), generator=g, device=dev).to(torch.bfloat16)
+        kp = torch.randn((T, kvh * D), generator=g, device=dev).to(torch.bfloat16)
+        vp = torch.randn((T, kvh * D), generator=g, device=dev).to(torch.bfloat16)
+        cache = pkg.PagedKVCache(1, nblk, BLOCK, kvh, D, dtype=torch.bfloat16, device=dev)
+
+        def fused():
+            return pkg.rope_kv_append(qp, kp, vp, pos, rot, cache, 0, table, token_offsets=offs,
+                                      q_len=q_len, num_heads=qh)
+
+        def unfused():
+            cos = rot.cos_cached[pos].to(torch.bfloat16).view(B, q_len, D).unsqueeze(1)
+            sin = rot.sin_cached[pos].to(torch.bfloat16).view(B, q_len, D).unsqueeze(1)
+            q = qp.view(B, q_len, qh, D).permute(0, 2, 1, 3)
+            k = kp.view(B, q_len, kvh, D).permute(0, 2, 1, 3)
+            v = vp.view(B, q_len, kvh, D).permute(0, 2, 1, 3)
+
+            def rotate_half(x):
+                return torch.cat((-x[..., D // 2:], x[..., :D // 2]), dim=-1)
+            q = q * cos + rotate_half(q) * sin
+            k = k * cos + rotate_half(k) * sin
+            bk = k.permute(0, 2, 1, 3).contiguous()
+            bv = v.permute(0, 2, 1, 3).contiguous()
+            if q_len == 1:
+                cache.write_decode(0, table, offs, bk[:, 0], bv[:, 0])
+            else:
+                cache.write(0, table, offs, bk, bv)
+            return q
+
+        def timed(fn, n):
+            # Device time: the call is captured once in a CUDA graph and replayed,
+            # so host launch overhead (which dominates the small decode shape)
+            # is not measured for either path.
+            for _ in range(max(args.warmup, 3)):
+                fn()
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                fn()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize(dev)
+            if world > 1:
+                dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(n):
+                graph.replay()
+            b.record()
+            torch.cuda.synchronize(dev)
+            del graph
+            ms = a.elapsed_time(b) / n
+            if world > 1:
+                t = torch.tensor([ms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            return ms
+
+        sampler = ClockSampler(local)
+        sampler.start()
+        f_ms = timed(fused, args.steps)
+        clocks = sampler.stop()
+        u_ms = timed(unfused, max(args.steps // 4, 10))
+        # Algorithmic bytes: q/k/v rows read, rotated q and the K/V cache rows written,
+        # the two fp32 table rows read per token.
+        nbytes = T * ((qh + 2 * kvh) * D * 2 * 2 + 2 * D * 4)
+        results[name] = {"tokens_per_gpu": T, "fused_us": round(f_ms * 1e3, 2),
+                         "unfused_torch_us": round(u_ms * 1e3, 2),
+                         "speedup": round(u_ms / f_ms, 2),
+                         "GBps_per_gpu": round(nbytes / (f_ms * 1e-3) / 1e9, 1),
+                         "bytes_per_launch": int(nbytes), "clocks": clocks}
+        del cache
+        torch.cuda.empty_cache()
+    if rank == 0:
+        pre = results["prefill_chunk"]
+        achieved = pre["GBps_per_gpu"]
+        line = {"config": "rope", "metric": "fused rotary + KV append GB/s (whole job)",
+                "unit": "GB/s", "value": round(achieved * world, 1), "n_gpus": world,
+                "scaling": "weak", "steps": args.steps, "dtype": "bf16",
+                "data": "synthetic: projections N(0,1) bf16, positions = offsets U[1024,8192) + "
+                        "token index, random block tables",
+                "workload": "Llama-3-8B heads (32 q / 8 KV, head_dim 128), rope base 500000; "
+                            "value = 16 x 256-token prefill chunk",
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": round(achieved / peak, 4),
+                             "kernel": "rope_append_kernel", "peak_kind": f"{peak_kind} hbm_gbs"},
+                "shapes": results}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_step(args) -> None:
+    """One Llama-3-8B decode step for 64 sequences on one GPU: DecodeStepState
+    advance + fused rotary append + split-K attention + combine, captured once
+    in a CUDA graph and replayed, against the same calls launched eagerly, and
+    the host work the reference runner does per step to build the same
+    metadata (model_runner.py:169-230: a Python loop over requests, torch.full
+    of the table on the device, one copy per table row)."""
+    import time
+
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pkg = importlib.import_module(PACKAGE)
+    B, H, KVH, D = 64, HEADS, KV_HEADS, HEAD_DIM
+    rng = np.random.default_rng(args.seed)
+    ctx0 = rng.integers(1024, 8192, size=B)
+    width = int((ctx0.max() + 4 * (args.steps + args.warmup) + 64) // BLOCK) + 2
+    nblk = B * width
+    perm = rng.permutation(nblk)
+    blocks = {f"r{i}": [int(x) for x in perm[i * width:i * width + int(ctx0[i]) // BLOCK + 1]]
+              for i in range(B)}
+    used = {rid: len(b) for rid, b in blocks.items()}
+    committed = {f"r{i}": int(ctx0[i]) for i in range(B)}
+    cache = pkg.PagedKVCache(1, nblk, BLOCK, KVH, D, dtype=torch.bfloat16, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4000)
+    for t in (cache.key_cache, cache.value_cache):
+        for i in range(0, t.shape[1], 4096):
+            sl = t[:, i:i + 4096]
+            sl.copy_(torch.randn(sl.shape, generator=g, device=dev) * 0.5)
+    rot = pkg.RotaryEmbedding(D, 16384, 500000.0, device=dev)
+    attn = pkg.PagedAttention(H, KVH, D)
+    qp = torch.randn((B, H * D), generator=g, device=dev).to(torch.bfloat16)
+    kp = torch.randn((B, KVH * D), generator=g, device=dev).to(torch.bfloat16)
+    vp = torch.randn((B, KVH * D), generator=g, device=dev).to(torch.bfloat16)
+    state = pkg.DecodeStepState(B, width, device=dev, capacity=256)
+    for rid in committed:
+        state.admit(rid, blocks[rid], committed[rid])
+    table, ctx, offs, pos = state.step()
+    for rid in committed:
+        committed[rid] += 1
+    out = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device=dev)
+
+    def schedule():
+        # host decisions of one step: a block for every sequence crossing into a new one
+        for rid in committed:
+            if committed[rid] // BLOCK >= used[rid]:
+                state.append_block(rid, blocks_spare.pop())
+                used[rid] += 1
+            committed[rid] += 1
+    taken = {x for b in blocks.values() for x in b}
+    blocks_spare = [int(x) for x in perm if int(x) not in taken]
+
+    def device_step():
+        state.launch(batch=B)
+        q = pkg.rope_kv_append(qp, kp, vp, pos, rot, cache, 0, table, token_offsets=offs,
+                               q_len=1, num_heads=H)
+        attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out)
+
+    stage_updates = state.stage
+
+    steps = args.steps
+    for _ in range(max(args.warmup, 3)):
+        schedule()
+        stage_updates()
+        device_step()
+    torch.cuda.synchronize(dev)
+    # eager: host launches every kernel of every step
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    a.record()
+    for _ in range(steps):
+        schedule()
+        stage_updates()
+        device_step()
+    b.record()
+    torch.cuda.synchronize(dev)
+    eager_wall = (time.perf_counter() - t0) / steps * 1e3
+    eager_dev = a.elapsed_time(b) / steps
+    # graph: one replay per step (the update count is read on the device)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        state._dev[0] = 0
+        device_step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    for rid in committed:
+        committed[rid] += 1
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        device_step()
+    sampler = ClockSampler(0)
+    sampler.start()
+    t0 = time.perf_counter()
+    a.record()
+    for _ in range(steps):
+        schedule()
+        stage_updates()
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize(dev)
+    graph_wall = (time.perf_counter() - t0) / steps * 1e3
+    graph_dev = a.elapsed_time(b) / steps
+    clocks = sampler.stop()
+    del graph
+    # the reference runner's per-step host metadata build, for the same batch
+    reqs = list(committed)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        w = max(len(v) for v in blocks.values())
+        tab = torch.full((B, w), -1, dtype=torch.int32, device=dev)
+        for row, rid in enumerate(reqs):
+            tab[row, :len(blocks[rid])] = torch.tensor(blocks[rid], dtype=torch.int32)
+        torch.tensor([committed[r] + 1 for r in reqs], dtype=torch.long, device=dev)
+        torch.tensor([committed[r] for r in reqs], dtype=torch.long, device=dev)
+        torch.cat([torch.tensor([committed[r]], dtype=torch.long) for r in reqs]).to(dev)
+    torch.cuda.synchronize(dev)
+    ref_meta = (time.perf_counter() - t0) / steps * 1e3
+    ok = pkg._runtime.read_and_clear_errors(dev) == 0
+    line = {"config": "step", "metric": "decode step latency (one layer), ms", "unit": "ms",
+            "higher_is_better": False, "n_gpus": 1, "steps": steps, "dtype": "bf16",
+            "workload": "Llama-3-8B heads, 64 sequences, context U[1024,8192): metadata advance + "
+                        "fused rotary append + split-K attention + combine",
+            "graph_replay_ms": round(graph_wall, 4), "graph_device_ms": round(graph_dev, 4),
+            "eager_ms": round(eager_wall, 4), "eager_device_ms": round(eager_dev, 4),
+            "reference_host_metadata_ms": round(ref_meta, 4), "device_errors_clear": ok,
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "step":
+        run_step(args)
+    elif args.config == "rope":
+        run_rope(args)
     elif args.config != "c2":
         run_extra(args)
     else:

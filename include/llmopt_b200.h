@@ -24,6 +24,8 @@
  *   llmopt_kv_write         <- PagedKVCache.write  src/llmopt/cache/paged_cache.py:175-232
  *   llmopt_kv_write_decode  <- PagedKVCache.write_decode  paged_cache.py:234-261
  *   llmopt_paged_gather     <- PagedKVCache.gather  paged_cache.py:263-312
+ *   llmopt_decode_step_advance <- ModelRunner._build_decode + _finalize
+ *                              src/llmopt/engine/model_runner.py:169-230 (device-resident)
  *   llmopt_rope_kv_append   <- the rotary + append statements of
  *                              PagedAttentionLayer.forward  src/llmopt/model/layers.py:106-134
  *                              (RotaryEmbedding.forward, apply_rotary_pos_emb
@@ -320,6 +322,35 @@ LLMOPT_API int llmopt_rope_kv_append(
     int32_t table_is_i64, int64_t table_width, int64_t table_stride, const void* token_offsets,
     int32_t off_is_i64, int64_t batch, int32_t num_heads, int32_t q_len, uint32_t* err,
     void* stream);
+
+/*
+ * Decode-step metadata kept on the device.  Replaces the per-step host build
+ * of ModelRunner._build_decode + _finalize (model_runner.py:169-230): for a
+ * decode step the reference gives each request position = token offset =
+ * committed tokens, context length = committed + 1 and its block ids (-1
+ * padded) as a table row.  Here block_table [max_rows, table_width] (row
+ * stride table_stride, int32), context_lens, token_offsets and positions
+ * ([max_rows] int64) live on the device; updates (device memory, int64) is
+ * [count, then count records (op, row, a, b)], capacity records at most,
+ * applied in order:
+ *   LLMOPT_STEP_SET_BLOCK  table[row][a] = b
+ *   LLMOPT_STEP_ADMIT      row holds a new sequence with a committed tokens:
+ *                          context_lens[row] = a, table row set to -1
+ *   LLMOPT_STEP_MOVE       row takes row a's table row and context length
+ * then every row r < batch advances: token_offsets[r] = positions[r] =
+ * context_lens[r]; context_lens[r] += 1.  One launch, no host sync; the count
+ * is read on the device, so a captured graph replays with any update count.
+ * Bad rows or columns are skipped and flag LLMOPT_DEVERR_TABLE_WIDTH.
+ */
+#define LLMOPT_STEP_SET_BLOCK 0
+#define LLMOPT_STEP_ADMIT 1
+#define LLMOPT_STEP_MOVE 2
+LLMOPT_API int llmopt_decode_step_advance(const int64_t* updates, int64_t capacity,
+                                          int32_t* block_table, int64_t table_width,
+                                          int64_t table_stride, int64_t* context_lens,
+                                          int64_t* token_offsets, int64_t* positions,
+                                          int64_t max_rows, int64_t batch, uint32_t* err,
+                                          void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -16,6 +16,8 @@ that the CUDA kernels can be compared against it on identical inputs:
   (``_expand_kv`` :189-210, ``_build_mask`` :212-229, ``_forward_dense``
   :231-250, ``_forward_split`` :252-293)
 * ``merge_states``             src/llmopt/attention/paged_attention.py:30-55
+* ``ModelRunner._build_decode`` + ``_finalize`` (the decode step's metadata)
+  src/llmopt/engine/model_runner.py:169-230
 * the rotary + KV-append half of ``PagedAttentionLayer.forward``
   src/llmopt/model/layers.py:106-134 (``RotaryEmbedding.forward``
   src/llmopt/model/rotary.py:103-121, ``apply_rotary_pos_emb`` :23-46,
@@ -56,6 +58,7 @@ __all__ = [
     "write_decode",
     "merge_states",
     "rope_append",
+    "decode_step_metadata",
     "paged_attention",
     "attention_lse",
     "decode_bytes",
@@ -238,6 +241,27 @@ def write_decode(key_cache: np.ndarray, value_cache: np.ndarray, kind: str, laye
     for s in range(B):
         key_cache[layer, blocks[s], slot[s]] = convert(keys[s], in_kind, kind)
         value_cache[layer, blocks[s], slot[s]] = convert(values[s], in_kind, kind)
+
+
+# ---------------------------------------------------------------------------
+# decode-step metadata
+# ---------------------------------------------------------------------------
+
+def decode_step_metadata(committed: dict, block_map: dict, order=None):
+    """Restates ``ModelRunner._build_decode`` + ``_finalize`` (model_runner.py:169-230)
+    for a decode step: per request (rows in ``order``, default the dict order)
+    position = token offset = committed tokens (:180-183), context length =
+    committed + 1 (:184); the table is int32, ``-1`` padded, as wide as the
+    longest block list (at least 1, :208-214).  Returns (seq_ids, positions,
+    table, context_lens, token_offsets)."""
+    ids = list(order) if order is not None else list(committed)
+    width = max([len(v) for v in block_map.values()] + [1])
+    table = np.full((len(ids), width), -1, dtype=np.int32)
+    for row, rid in enumerate(ids):
+        b = block_map.get(rid, [])
+        table[row, :len(b)] = b
+    pos = np.array([committed[r] for r in ids], dtype=np.int64)
+    return ids, pos, table, pos + 1, pos.copy()
 
 
 # ---------------------------------------------------------------------------

@@ -23,6 +23,7 @@ from .attention import AttentionBackend, PagedAttention, PagedAttentionConfig, m
 from .cache import PagedKVCache
 from .install import install, uninstall
 from .rope import RotaryEmbedding, rope_kv_append
+from .step import DecodeStepState
 
 __all__ = [
     "AttentionBackend",
@@ -32,6 +33,7 @@ __all__ = [
     "merge_states",
     "RotaryEmbedding",
     "rope_kv_append",
+    "DecodeStepState",
     "install",
     "uninstall",
     "lib",

@@ -40,6 +40,10 @@ PHASE_SPLIT = 1
 PHASE_COMBINE = 2
 PHASE_ALL = 3
 
+STEP_SET_BLOCK = 0
+STEP_ADMIT = 1
+STEP_MOVE = 2
+
 PEER_HANDLE_BYTES = 64
 MAX_PEERS = 8
 PEER_FLAGS_BYTES = 64
@@ -112,6 +116,7 @@ SIGNATURES = {
         _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,   # caches, dtype, L, NB, BS, KVH, D, layer
         _p, _i32, _i64, _i64, _p, _i32,               # table, is64, width, stride, offsets, is64
         _i64, _i32, _i32, _p, _p],                    # batch, heads, q_len, err, stream
+    "llmopt_decode_step_advance": [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p],
 }
 
 _RESTYPES = {

@@ -966,8 +966,53 @@ extern "C" int llmopt_rope_kv_append(
   a.num_heads = num_heads;
   a.q_len = q_len;
   a.err = err;
+  // Paired accesses: 2 elements (4 bytes for 16-bit, 8 for fp32) at every
+  // row start, pair offset and table row.
+  {
+    const int es = in_dtype == kF32 ? 4 : 2;
+    const int ts = table_dtype == kF32 ? 4 : 2;
+    auto al = [](const void* p, int n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
+    const bool even = head_dim % 4 == 0 && q_row % 2 == 0 && k_row % 2 == 0 && qo_s % 2 == 0 &&
+                      qo_h % 2 == 0 && qo_t % 2 == 0;
+    a.pairs = even && al(q_proj, 2 * es) && al(k_proj, 2 * es) && al(q_out, 2 * es) &&
+              al(key_cache, 2 * (kv_dtype == kF32 ? 4 : 2)) && al(cos_table, 2 * ts) &&
+              al(sin_table, 2 * ts) ? 1 : 0;
+    const int per = kv_dtype == kF32 ? 4 : 8;
+    a.vrow16 = in_dtype == kv_dtype && head_dim % per == 0 && v_row % per == 0 &&
+               al(v_proj, 16) && al(value_cache, 16) ? 1 : 0;
+  }
   cudaError_t e = rope_append_launch(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rope_append launch");
+  return ok();
+}
+
+extern "C" int llmopt_decode_step_advance(const int64_t* updates, int64_t capacity,
+                                          int32_t* block_table, int64_t table_width,
+                                          int64_t table_stride, int64_t* context_lens,
+                                          int64_t* token_offsets, int64_t* positions,
+                                          int64_t max_rows, int64_t batch, uint32_t* err,
+                                          void* stream) {
+  if (capacity < 0 || table_width < 1 || table_stride < table_width || max_rows < 1 ||
+      batch < 0 || batch > max_rows) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid step-state shape");
+  }
+  if (!updates || !block_table || !context_lens || !token_offsets || !positions) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null pointer argument");
+  }
+  StepArgs a{};
+  a.updates = reinterpret_cast<const long long*>(updates);
+  a.capacity = capacity;
+  a.table = block_table;
+  a.table_width = table_width;
+  a.table_stride = table_stride;
+  a.ctx = reinterpret_cast<long long*>(context_lens);
+  a.offsets = reinterpret_cast<long long*>(token_offsets);
+  a.positions = reinterpret_cast<long long*>(positions);
+  a.max_rows = max_rows;
+  a.batch = batch;
+  a.err = err;
+  cudaError_t e = step_advance_launch(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "step_advance launch");
   return ok();
 }
 // ---------------------------------------------------------------------------

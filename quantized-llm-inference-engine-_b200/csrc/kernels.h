@@ -161,8 +161,25 @@ struct RopeArgs {
   int num_heads;
   int q_len;
   unsigned* err;
+  int pairs;   // 1: head_dim % 4 == 0 and every row/table address allows 2-element accesses
+  int vrow16;  // 1: v rows move as 16-byte vectors (same dtype, 16-byte aligned rows)
 };
 cudaError_t rope_append_launch(const RopeArgs& a, cudaStream_t stream);
+
+// Device-resident decode step metadata (step_state.cu).
+struct StepArgs {
+  const long long* updates;   // [1 + 4 * capacity]: count, then (op, row, a, b) records
+  long long capacity;
+  int* table;                 // [max_rows, table_stride] int32 block table
+  long long table_width, table_stride;
+  long long* ctx;             // [max_rows] context lengths (committed + this step)
+  long long* offsets;         // [max_rows] write offsets of the step
+  long long* positions;       // [max_rows] positions of the step (q_len 1)
+  long long max_rows;
+  long long batch;            // active rows [0, batch)
+  unsigned* err;
+};
+cudaError_t step_advance_launch(const StepArgs& a, cudaStream_t stream);
 
 struct GatherArgs {
   const void* k_cache;

@@ -56,6 +56,175 @@ __device__ __forceinline__ void rotate_pair(float x1, float x2, float c1, float 
   *o2 = op_round<DT>(__fadd_rn(a2, b2));
 }
 
+// Two consecutive elements of a 16- or 32-bit row as floats (8-byte or 4-byte load).
+template <int DT>
+__device__ __forceinline__ float2 load2(const void* p, long long i) {
+  if constexpr (DT == kF32) {
+    return *reinterpret_cast<const float2*>(static_cast<const float*>(p) + i);
+  } else if constexpr (DT == kF16) {
+    return __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(p) + i));
+  } else {
+    return __bfloat1622float2(
+        *reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(p) + i));
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void store2(void* p, long long i, float x, float y) {
+  if constexpr (DT == kF32) {
+    *reinterpret_cast<float2*>(static_cast<float*>(p) + i) = make_float2(x, y);
+  } else {
+    *reinterpret_cast<uint32_t*>(static_cast<typename ElemT<DT>::T*>(p) + i) = pack2<DT>(x, y);
+  }
+}
+
+__device__ __forceinline__ float2 load2_any(const void* p, int dt, long long i) {
+  if (dt == kF32) return *reinterpret_cast<const float2*>(static_cast<const float*>(p) + i);
+  if (dt == kF16) return load2<kF16>(p, i);
+  return load2<kBF16>(p, i);
+}
+
+// Rotates one head row from `src` (model dtype) into `dst` (dtype OUT_DT).
+template <int IN_DT, int OUT_DT>
+__device__ __forceinline__ void rotate_row(const RopeArgs& a, const void* src_base,
+                                           long long src, void* dst_base, long long dst,
+                                           long long pos, int lane) {
+  const int D = a.head_dim;
+  const int half = D / 2;
+  const long long trow = pos * D;
+  if (a.pairs) {
+    for (int e = 2 * lane; e < half; e += 64) {
+      const float2 c1 = load2_any(a.cos_t, a.tab_dtype, trow + e);
+      const float2 c2 = load2_any(a.cos_t, a.tab_dtype, trow + e + half);
+      const float2 s1 = load2_any(a.sin_t, a.tab_dtype, trow + e);
+      const float2 s2 = load2_any(a.sin_t, a.tab_dtype, trow + e + half);
+      const float2 x1 = load2<IN_DT>(src_base, src + e);
+      const float2 x2 = load2<IN_DT>(src_base, src + e + half);
+      float o1x, o2x, o1y, o2y;
+      rotate_pair<IN_DT>(x1.x, x2.x, op_round<IN_DT>(c1.x), op_round<IN_DT>(c2.x),
+                         op_round<IN_DT>(s1.x), op_round<IN_DT>(s2.x), &o1x, &o2x);
+      rotate_pair<IN_DT>(x1.y, x2.y, op_round<IN_DT>(c1.y), op_round<IN_DT>(c2.y),
+                         op_round<IN_DT>(s1.y), op_round<IN_DT>(s2.y), &o1y, &o2y);
+      store2<OUT_DT>(dst_base, dst + e, o1x, o1y);
+      store2<OUT_DT>(dst_base, dst + e + half, o2x, o2y);
+    }
+  } else {
+    for (int e = lane; e < half; e += 32) {
+      const float c1 = op_round<IN_DT>(load_any(a.cos_t, a.tab_dtype, trow + e));
+      const float c2 = op_round<IN_DT>(load_any(a.cos_t, a.tab_dtype, trow + e + half));
+      const float s1 = op_round<IN_DT>(load_any(a.sin_t, a.tab_dtype, trow + e));
+      const float s2 = op_round<IN_DT>(load_any(a.sin_t, a.tab_dtype, trow + e + half));
+      float o1, o2;
+      rotate_pair<IN_DT>(load_f32<IN_DT>(src_base, src + e),
+                         load_f32<IN_DT>(src_base, src + e + half), c1, c2, s1, s2, &o1, &o2);
+      store_f32<OUT_DT>(dst_base, dst + e, o1);
+      store_f32<OUT_DT>(dst_base, dst + e + half, o2);
+    }
+  }
+}
+
+constexpr int kRowsPerItem = 8;
+
+// One v head row to the cache (cast only): 16-byte vectors when allowed.
+template <int IN_DT, int KV_DT>
+__device__ __forceinline__ void copy_v_row(const RopeArgs& a, long long tok, int h,
+                                           long long dst, int lane) {
+  const int D = a.head_dim;
+  const long long src = tok * a.v_row + (long long)h * D;
+  const long long out = dst + (long long)h * D;
+  if (a.vrow16) {
+    using T = typename ElemT<KV_DT>::T;
+    const int per = 16 / (int)sizeof(T);
+    for (int e = lane * per; e < D; e += 32 * per) {
+      *reinterpret_cast<uint4*>(static_cast<T*>(a.v_cache) + out + e) =
+          *reinterpret_cast<const uint4*>(static_cast<const T*>(a.v_in) + src + e);
+    }
+  } else {
+    for (int e = lane; e < D; e += 32) {
+      store_f32<KV_DT>(a.v_cache, out + e, load_f32<IN_DT>(a.v_in, src + e));
+    }
+  }
+}
+
+// Up to kRowsPerItem rows [r0, r0 + 8) of one token on the paired path
+// (head_dim % 4 == 0, head_dim <= 256): lane l owns the element pairs
+// (2l + 64m, 2l + 64m + 1) of each half, m < 2.  The token's cos/sin pairs are
+// loaded once; each row's two input pairs per m are loaded for all rows first.
+template <int IN_DT, int KV_DT>
+__device__ __forceinline__ void rotate_rows_paired(const RopeArgs& a, long long s, int i,
+                                                   long long tok, long long pos, long long dst,
+                                                   int r0, int rows, int lane) {
+  const int D = a.head_dim;
+  const int half = D / 2;
+  const long long trow = pos * D;
+  float2 c1[2], c2[2], s1[2], s2[2];
+  bool live[2];
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    const int e = 2 * lane + 64 * m;
+    live[m] = e < half;
+    if (live[m]) {
+      c1[m] = load2_any(a.cos_t, a.tab_dtype, trow + e);
+      c2[m] = load2_any(a.cos_t, a.tab_dtype, trow + e + half);
+      s1[m] = load2_any(a.sin_t, a.tab_dtype, trow + e);
+      s2[m] = load2_any(a.sin_t, a.tab_dtype, trow + e + half);
+      c1[m] = make_float2(op_round<IN_DT>(c1[m].x), op_round<IN_DT>(c1[m].y));
+      c2[m] = make_float2(op_round<IN_DT>(c2[m].x), op_round<IN_DT>(c2[m].y));
+      s1[m] = make_float2(op_round<IN_DT>(s1[m].x), op_round<IN_DT>(s1[m].y));
+      s2[m] = make_float2(op_round<IN_DT>(s2[m].x), op_round<IN_DT>(s2[m].y));
+    }
+  }
+  // Loads of every rotated row of the item first.
+  float2 x1[kRowsPerItem][2], x2[kRowsPerItem][2];
+#pragma unroll
+  for (int j = 0; j < kRowsPerItem; ++j) {
+    const int r = r0 + j;
+    const bool rq = r < a.num_heads;
+    const bool rk = !rq && r < a.num_heads + a.kv_heads && dst >= 0;
+    const void* base = rq ? a.q_in : a.k_in;
+    const long long src = rq ? tok * a.q_row + (long long)r * D
+                             : tok * a.k_row + (long long)(r - a.num_heads) * D;
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const int e = 2 * lane + 64 * m;
+      if ((rq || rk) && r < rows && live[m]) {
+        x1[j][m] = load2<IN_DT>(base, src + e);
+        x2[j][m] = load2<IN_DT>(base, src + e + half);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kRowsPerItem; ++j) {
+    const int r = r0 + j;
+    if (r >= rows) break;
+    if (r < a.num_heads + a.kv_heads) {
+      const bool rq = r < a.num_heads;
+      if (!rq && dst < 0) continue;
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        if (!live[m]) continue;
+        const int e = 2 * lane + 64 * m;
+        float o1x, o2x, o1y, o2y;
+        rotate_pair<IN_DT>(x1[j][m].x, x2[j][m].x, c1[m].x, c2[m].x, s1[m].x, s2[m].x, &o1x,
+                           &o2x);
+        rotate_pair<IN_DT>(x1[j][m].y, x2[j][m].y, c1[m].y, c2[m].y, s1[m].y, s2[m].y, &o1y,
+                           &o2y);
+        if (rq) {
+          const long long out = s * a.qo_s + (long long)r * a.qo_h + (long long)i * a.qo_t;
+          store2<IN_DT>(a.q_out, out + e, o1x, o1y);
+          store2<IN_DT>(a.q_out, out + e + half, o2x, o2y);
+        } else {
+          const long long out = dst + (long long)(r - a.num_heads) * D;
+          store2<KV_DT>(a.k_cache, out + e, o1x, o1y);
+          store2<KV_DT>(a.k_cache, out + e + half, o2x, o2y);
+        }
+      }
+    } else if (dst >= 0) {
+      copy_v_row<IN_DT, KV_DT>(a, tok, r - a.num_heads - a.kv_heads, dst, lane);
+    }
+  }
+}
+
 template <int IN_DT, int KV_DT>
 __global__ void __launch_bounds__(kThreads) rope_append_kernel(const RopeArgs a) {
   griddep_wait();
@@ -123,19 +292,23 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(const RopeArgs a)
   const int t0 = blockIdx.y * kTokPerCta;
   const int ntok = a.q_len - t0 < kTokPerCta ? a.q_len - t0 : kTokPerCta;
   const int rows = a.num_heads + 2 * a.kv_heads;
-  for (int item = warp; item < ntok * rows; item += kWarps) {
-    const int ti = item / rows;
-    const int r = item - ti * rows;
+  const int groups = (rows + kRowsPerItem - 1) / kRowsPerItem;
+  // Work item = (token, group of kRowsPerItem consecutive rows): the token's
+  // position, cache row and cos/sin values are loaded once per item, and the
+  // item's rows issue all their loads before any of them is rotated.
+  for (int item = warp; item < ntok * groups; item += kWarps) {
+    const int ti = item / groups;
+    const int r0 = (item - ti * groups) * kRowsPerItem;
     const int i = t0 + ti;
     const long long tok = s * a.q_len + i;
     long long pos = load_index(a.positions, a.pos_i64, tok);
     if (pos >= a.max_pos || pos < -a.max_pos) {
-      if (lane == 0 && r == 0) record_error(a.err, kErrPosition);
+      if (lane == 0 && r0 == 0) record_error(a.err, kErrPosition);
       continue;
     }
     if (pos < 0) pos += a.max_pos;
-    long long dst = -1;                            // cache row of this token
-    if (r >= a.num_heads) {
+    long long dst = -1;                            // this token's cache row
+    if (r0 + kRowsPerItem > a.num_heads) {
       if (decode) {
         dst = dec_dst;
       } else {
@@ -148,46 +321,23 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(const RopeArgs a)
                 (long long)a.kv_heads * D;
         }
       }
-      if (dst < 0) continue;
     }
-    if (r < a.num_heads) {
-      // q head r -> q_out[s, r, i, :]
-      const long long src = tok * a.q_row + (long long)r * D;
-      const long long out = s * a.qo_s + (long long)r * a.qo_h + (long long)i * a.qo_t;
-      for (int e = lane; e < half; e += 32) {
-        const float c1 = op_round<IN_DT>(load_any(a.cos_t, a.tab_dtype, pos * D + e));
-        const float c2 = op_round<IN_DT>(load_any(a.cos_t, a.tab_dtype, pos * D + e + half));
-        const float s1 = op_round<IN_DT>(load_any(a.sin_t, a.tab_dtype, pos * D + e));
-        const float s2 = op_round<IN_DT>(load_any(a.sin_t, a.tab_dtype, pos * D + e + half));
-        float o1, o2;
-        rotate_pair<IN_DT>(load_f32<IN_DT>(a.q_in, src + e), load_f32<IN_DT>(a.q_in, src + e + half),
-                           c1, c2, s1, s2, &o1, &o2);
-        store_f32<IN_DT>(a.q_out, out + e, o1);
-        store_f32<IN_DT>(a.q_out, out + e + half, o2);
-      }
-    } else if (r < a.num_heads + a.kv_heads) {
-      // k head -> cache: rotated in the model dtype, then cast to the cache dtype
-      const int h = r - a.num_heads;
-      const long long src = tok * a.k_row + (long long)h * D;
-      const long long out = dst + (long long)h * D;
-      for (int e = lane; e < half; e += 32) {
-        const float c1 = op_round<IN_DT>(load_any(a.cos_t, a.tab_dtype, pos * D + e));
-        const float c2 = op_round<IN_DT>(load_any(a.cos_t, a.tab_dtype, pos * D + e + half));
-        const float s1 = op_round<IN_DT>(load_any(a.sin_t, a.tab_dtype, pos * D + e));
-        const float s2 = op_round<IN_DT>(load_any(a.sin_t, a.tab_dtype, pos * D + e + half));
-        float o1, o2;
-        rotate_pair<IN_DT>(load_f32<IN_DT>(a.k_in, src + e), load_f32<IN_DT>(a.k_in, src + e + half),
-                           c1, c2, s1, s2, &o1, &o2);
-        store_f32<KV_DT>(a.k_cache, out + e, o1);
-        store_f32<KV_DT>(a.k_cache, out + e + half, o2);
-      }
+    if (a.pairs && half <= 128) {
+      rotate_rows_paired<IN_DT, KV_DT>(a, s, i, tok, pos, dst, r0, rows, lane);
     } else {
-      // v head -> cache, cast only
-      const int h = r - a.num_heads - a.kv_heads;
-      const long long src = tok * a.v_row + (long long)h * D;
-      const long long out = dst + (long long)h * D;
-      for (int e = lane; e < D; e += 32) {
-        store_f32<KV_DT>(a.v_cache, out + e, load_f32<IN_DT>(a.v_in, src + e));
+      for (int r = r0; r < r0 + kRowsPerItem && r < rows; ++r) {
+        if (r >= a.num_heads && dst < 0) continue;
+        if (r < a.num_heads) {
+          rotate_row<IN_DT, IN_DT>(a, a.q_in, tok * a.q_row + (long long)r * D, a.q_out,
+                                   s * a.qo_s + (long long)r * a.qo_h + (long long)i * a.qo_t,
+                                   pos, lane);
+        } else if (r < a.num_heads + a.kv_heads) {
+          const int h = r - a.num_heads;
+          rotate_row<IN_DT, KV_DT>(a, a.k_in, tok * a.k_row + (long long)h * D, a.k_cache,
+                                   dst + (long long)h * D, pos, lane);
+        } else {
+          copy_v_row<IN_DT, KV_DT>(a, tok, r - a.num_heads - a.kv_heads, dst, lane);
+        }
       }
     }
   }

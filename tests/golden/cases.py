@@ -281,6 +281,62 @@ def rope_checksum(case: dict) -> str:
                     case["token_offsets"])
 
 
+# ---------------------------------------------------------------------------
+# Decode-step metadata scenario (requests joining, growing, leaving)
+# ---------------------------------------------------------------------------
+
+STEP_BLOCK_SIZE = 16
+STEP_SCRIPT = {
+    0: [("admit", "a", 30), ("admit", "b", 16), ("admit", "c", 5)],
+    3: [("release", "b"), ("admit", "d", 47)],
+    5: [("release", "a")],
+    6: [("admit", "e", 1), ("admit", "f", 63), ("admit", "g", 15)],
+    9: [("release", "c"), ("release", "f")],
+    11: [("admit", "h", 200)],
+}
+STEP_COUNT = 14
+
+
+def step_scenario():
+    """Yields, per decode step, (events, committed, block_map): the scheduling
+    events of the step (('admit', id, blocks, committed), ('append', id, block),
+    ('release', id)) and the state the reference's runner reads for it: the
+    committed tokens and block ids of every running request, in admission
+    order.  A request's blocks always cover the position its next token
+    takes; block ids come from a counter."""
+    bs = STEP_BLOCK_SIZE
+    next_block = [0]
+    committed: dict = {}
+    blocks: dict = {}
+
+    def take(n):
+        out = list(range(next_block[0], next_block[0] + n))
+        next_block[0] += n
+        return out
+
+    for step in range(STEP_COUNT):
+        events = []
+        for ev in STEP_SCRIPT.get(step, []):
+            if ev[0] == "release":
+                committed.pop(ev[1])
+                blocks.pop(ev[1])
+                events.append(("release", ev[1]))
+        for ev in STEP_SCRIPT.get(step, []):
+            if ev[0] == "admit":
+                rid, n = ev[1], ev[2]
+                committed[rid] = n
+                blocks[rid] = take(n // bs + 1)
+                events.append(("admit", rid, list(blocks[rid]), n))
+        for rid in committed:
+            if committed[rid] // bs >= len(blocks[rid]):
+                b = take(1)[0]
+                blocks[rid].append(b)
+                events.append(("append", rid, b))
+        yield events, dict(committed), {k: list(v) for k, v in blocks.items()}
+        for rid in committed:
+            committed[rid] += 1
+
+
 def write_checksum(case: dict) -> str:
     return checksum(case["key_cache"], case["value_cache"], case["block_ids"],
                     case["token_offsets"], case["keys"], case["values"])

@@ -2,7 +2,7 @@
 
 Run once, in a container where the reference source is present::
 
-    python tests/golden/make_golden.py /path/to/reference/src [--only=rope]
+    python tests/golden/make_golden.py /path/to/reference/src [--only=rope|step]
 
 It imports ``llmopt.attention`` / ``llmopt.cache`` from that path, runs them
 on CPU on the seeded inputs of ``cases.py`` (plus the reference's own
@@ -21,7 +21,9 @@ Recorded per attention run:
   formula of ``_forward_split``), for the LSE parity check.
 
 Rotary + append cases (``rope_*.npz``) record the reference's cos/sin tables,
-the rotated query and the caches after the append, bit for bit.
+the rotated query and the caches after the append, bit for bit;
+``step_metadata.npz`` the reference runner's decode metadata for every step of
+the request scenario in ``cases.step_scenario``.
 """
 
 from __future__ import annotations
@@ -197,6 +199,29 @@ def make_rope(build, RotaryEmbedding, apply_rotary_pos_emb, PagedKVCache) -> dic
     return out
 
 
+def make_step(ModelRunner) -> dict:
+    """The reference runner's decode metadata for every step of the scenario:
+    ``ModelRunner._build_decode`` (with ``_finalize``) called on a stand-in
+    runner whose device is the CPU, with request stand-ins carrying the fields
+    it reads (model_runner.py:169-230)."""
+    from types import SimpleNamespace
+
+    runner = SimpleNamespace(device="cpu")
+    runner._finalize = lambda *args: ModelRunner._finalize(runner, *args)
+    runner._last_input_token = ModelRunner._last_input_token
+    out = {}
+    for step, (_, committed, block_map) in enumerate(cases.step_scenario()):
+        requests = [SimpleNamespace(request_id=rid, num_computed_tokens=n, output_token_ids=[7],
+                                    prompt_token_ids=[1]) for rid, n in committed.items()]
+        mi = ModelRunner._build_decode(runner, requests, block_map)
+        out[f"{step}.seq_ids"] = np.array(mi.seq_ids)
+        out[f"{step}.positions"] = mi.positions.numpy()
+        out[f"{step}.block_ids"] = mi.block_ids.numpy()
+        out[f"{step}.context_lens"] = mi.context_lens.numpy()
+        out[f"{step}.token_offsets"] = mi.token_offsets.numpy()
+    return out
+
+
 def make_fixture(PagedAttention, PagedAttentionConfig, PagedKVCache, BlockPool) -> dict:
     """The reference's ``tests/test_paged_attention.py`` fixture and its four checks,
     with ``pool.append`` run before the chain is read (the shipped order raises)."""
@@ -274,6 +299,14 @@ def main(ref_src: str, only: str | None = None) -> None:
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     meta = {"torch": torch.__version__, "numpy": np.__version__}
+    if only == "step":
+        from llmopt.engine.model_runner import ModelRunner
+
+        out = make_step(ModelRunner)
+        out["versions"] = np.array(str(meta))
+        np.savez_compressed(os.path.join(HERE, "step_metadata.npz"), **out)
+        print("wrote step_metadata")
+        return
     if only == "rope":
         from llmopt.model.rotary import RotaryEmbedding, apply_rotary_pos_emb
 

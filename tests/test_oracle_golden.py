@@ -98,6 +98,18 @@ def test_oracle_rope_rejects_position_past_table():
                        case["heads"], case["kv_heads"])
 
 
+def test_oracle_decode_step_metadata_matches_reference():
+    gold = load_golden("step_metadata")
+    for step, (_, committed, block_map) in enumerate(cases.step_scenario()):
+        ids, pos, table, ctx, offs = po.decode_step_metadata(committed, block_map)
+        assert ids == [str(x) for x in gold[f"{step}.seq_ids"]], step
+        np.testing.assert_array_equal(pos, gold[f"{step}.positions"])
+        np.testing.assert_array_equal(table, gold[f"{step}.block_ids"])
+        assert table.dtype == gold[f"{step}.block_ids"].dtype == np.int32
+        np.testing.assert_array_equal(ctx, gold[f"{step}.context_lens"])
+        np.testing.assert_array_equal(offs, gold[f"{step}.token_offsets"])
+
+
 def test_oracle_reference_fixture():
     """The reference's own test_paged_attention.py fixture and checks."""
     g = load_golden("ref_fixture")
