@@ -925,7 +925,8 @@ def run_step(args) -> None:
     qp = torch.randn((B, H * D), generator=g, device=dev).to(torch.bfloat16)
     kp = torch.randn((B, KVH * D), generator=g, device=dev).to(torch.bfloat16)
     vp = torch.randn((B, KVH * D), generator=g, device=dev).to(torch.bfloat16)
-    state = pkg.DecodeStepState(B, width, device=dev, capacity=256)
+    # capacity: the first step admits every sequence with all of its blocks
+    state = pkg.DecodeStepState(B, width, device=dev, capacity=B * (width + 1))
     for rid in committed:
         state.admit(rid, blocks[rid], committed[rid])
     table, ctx, offs, pos = state.step()

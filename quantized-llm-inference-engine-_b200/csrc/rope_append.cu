@@ -28,7 +28,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kTokPerCta = 4;
+constexpr int kTokPerCta = 8;
 
 __device__ __forceinline__ float load_any(const void* p, int dt, long long i) {
   if (dt == kF32) return static_cast<const float*>(p)[i];
@@ -147,20 +147,20 @@ __device__ __forceinline__ void copy_v_row(const RopeArgs& a, long long tok, int
 }
 
 // Up to kRowsPerItem rows [r0, r0 + 8) of one token on the paired path
-// (head_dim % 4 == 0, head_dim <= 256): lane l owns the element pairs
-// (2l + 64m, 2l + 64m + 1) of each half, m < 2.  The token's cos/sin pairs are
+// (head_dim % 4 == 0, head_dim <= 4 * 32 * M): lane l owns the element pairs
+// (2l + 64m, 2l + 64m + 1) of each half, m < M.  The token's cos/sin pairs are
 // loaded once; each row's two input pairs per m are loaded for all rows first.
-template <int IN_DT, int KV_DT>
+template <int IN_DT, int KV_DT, int M>
 __device__ __forceinline__ void rotate_rows_paired(const RopeArgs& a, long long s, int i,
                                                    long long tok, long long pos, long long dst,
                                                    int r0, int rows, int lane) {
   const int D = a.head_dim;
   const int half = D / 2;
   const long long trow = pos * D;
-  float2 c1[2], c2[2], s1[2], s2[2];
-  bool live[2];
+  float2 c1[M], c2[M], s1[M], s2[M];
+  bool live[M];
 #pragma unroll
-  for (int m = 0; m < 2; ++m) {
+  for (int m = 0; m < M; ++m) {
     const int e = 2 * lane + 64 * m;
     live[m] = e < half;
     if (live[m]) {
@@ -175,7 +175,7 @@ __device__ __forceinline__ void rotate_rows_paired(const RopeArgs& a, long long 
     }
   }
   // Loads of every rotated row of the item first.
-  float2 x1[kRowsPerItem][2], x2[kRowsPerItem][2];
+  float2 x1[kRowsPerItem][M], x2[kRowsPerItem][M];
 #pragma unroll
   for (int j = 0; j < kRowsPerItem; ++j) {
     const int r = r0 + j;
@@ -185,7 +185,7 @@ __device__ __forceinline__ void rotate_rows_paired(const RopeArgs& a, long long 
     const long long src = rq ? tok * a.q_row + (long long)r * D
                              : tok * a.k_row + (long long)(r - a.num_heads) * D;
 #pragma unroll
-    for (int m = 0; m < 2; ++m) {
+    for (int m = 0; m < M; ++m) {
       const int e = 2 * lane + 64 * m;
       if ((rq || rk) && r < rows && live[m]) {
         x1[j][m] = load2<IN_DT>(base, src + e);
@@ -201,7 +201,7 @@ __device__ __forceinline__ void rotate_rows_paired(const RopeArgs& a, long long 
       const bool rq = r < a.num_heads;
       if (!rq && dst < 0) continue;
 #pragma unroll
-      for (int m = 0; m < 2; ++m) {
+      for (int m = 0; m < M; ++m) {
         if (!live[m]) continue;
         const int e = 2 * lane + 64 * m;
         float o1x, o2x, o1y, o2y;
@@ -225,8 +225,11 @@ __device__ __forceinline__ void rotate_rows_paired(const RopeArgs& a, long long 
   }
 }
 
-template <int IN_DT, int KV_DT>
-__global__ void __launch_bounds__(kThreads) rope_append_kernel(const RopeArgs a) {
+// M: element pairs per lane of the paired path (1: head_dim <= 128, 2: <= 256),
+// 0: the element-wise path.  Separate kernels, so the common M = 1 carries no
+// registers of the others.
+template <int IN_DT, int KV_DT, int M>
+__global__ void __launch_bounds__(kThreads, 3) rope_append_kernel(const RopeArgs a) {
   griddep_wait();
   griddep_launch_dependents();
   const long long s = blockIdx.x;
@@ -322,8 +325,8 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(const RopeArgs a)
         }
       }
     }
-    if (a.pairs && half <= 128) {
-      rotate_rows_paired<IN_DT, KV_DT>(a, s, i, tok, pos, dst, r0, rows, lane);
+    if constexpr (M > 0) {
+      rotate_rows_paired<IN_DT, KV_DT, M>(a, s, i, tok, pos, dst, r0, rows, lane);
     } else {
       for (int r = r0; r < r0 + kRowsPerItem && r < rows; ++r) {
         if (r >= a.num_heads && dst < 0) continue;
@@ -344,13 +347,15 @@ __global__ void __launch_bounds__(kThreads) rope_append_kernel(const RopeArgs a)
 }
 
 template <int IN_DT, int KV_DT>
-const void* rope_ptr() {
-  return reinterpret_cast<const void*>(&rope_append_kernel<IN_DT, KV_DT>);
+const void* rope_ptr(int m) {
+  if (m == 1) return reinterpret_cast<const void*>(&rope_append_kernel<IN_DT, KV_DT, 1>);
+  if (m == 2) return reinterpret_cast<const void*>(&rope_append_kernel<IN_DT, KV_DT, 2>);
+  return reinterpret_cast<const void*>(&rope_append_kernel<IN_DT, KV_DT, 0>);
 }
 
-const void* select_rope(int in_dt, int kv_dt) {
+const void* select_rope(int in_dt, int kv_dt, int m) {
 #define LLMOPT_ROPE_CASE(I, K) \
-  if (in_dt == I && kv_dt == K) return rope_ptr<I, K>();
+  if (in_dt == I && kv_dt == K) return rope_ptr<I, K>(m);
   LLMOPT_ROPE_CASE(kF32, kF32)
   LLMOPT_ROPE_CASE(kF32, kF16)
   LLMOPT_ROPE_CASE(kF32, kBF16)
@@ -368,7 +373,9 @@ const void* select_rope(int in_dt, int kv_dt) {
 
 cudaError_t rope_append_launch(const RopeArgs& a, cudaStream_t stream) {
   if (a.batch <= 0 || a.q_len <= 0) return cudaSuccess;
-  const void* fn = select_rope(a.in_dtype, a.kv_dtype);
+  const int half = a.head_dim / 2;
+  const int m = !a.pairs ? 0 : half <= 64 ? 1 : half <= 128 ? 2 : 0;
+  const void* fn = select_rope(a.in_dtype, a.kv_dtype, m);
   if (fn == nullptr) return cudaErrorInvalidValue;
   const long long gy = (a.q_len + kTokPerCta - 1) / kTokPerCta;
   if (a.batch > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidConfiguration;
