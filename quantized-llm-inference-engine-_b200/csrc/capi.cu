@@ -218,7 +218,7 @@ bool query_tensor_map(const AttnArgs& a, CUtensorMap* out, std::string* why) {
 
 // ---- split planning and workspace layout ------------------------------------------
 constexpr long long kAlign = 256;
-constexpr int kMaxBalancedCtasPerSm = 8;
+constexpr int kMaxBalancedCtasPerSm = 16;
 constexpr long long kMaxBalancedBatch = 4096;
 
 long long round_up(long long x, long long a) { return (x + a - 1) / a * a; }

@@ -18,6 +18,11 @@
 // is -1 (or out of range) are not loaded at all.  A ring of `stages` buffers
 // with full/empty mbarriers keeps several blocks in flight per SM.
 //
+// Self-issuing mode (SP, used when a CTA holds one KV head): the CTA is one
+// warp that issues its own K/V copies a ring's depth ahead of the block it is
+// consuming, into stages it has already consumed - no producer warp, so about
+// twice as many CTAs (and copy issuers, what limits this kernel) fit per SM.
+//
 // Math.  Consumer warp w handles KV head (first + w).  Its query rows (the
 // group's heads x q_len, padded to 16) are the A operand of m16n8k16 MMAs:
 // S = Q K^T over the 16 tokens (two n-tiles), online softmax in fp32 registers
@@ -86,13 +91,20 @@ __device__ __forceinline__ void load_q_frags(const AttnArgs& a, long long s, int
   }
 }
 
-template <int D, int Q_DT, int KV_DT>
-__global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
+// SP: 12 one-warp CTAs per SM by registers (168 a thread at head_dim 128).
+template <int D, int Q_DT, int KV_DT, bool SP>
+__global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1)
     decode_tma_kernel(const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const AttnArgs a, const int hpc,
                       const int nstages) {
+  // When the dependent kernel (the combine, or the next decode) may start
+  // launching, measured on B200: with a producer warp, right away - the next
+  // grid's CTAs then fill SMs as this grid's tail CTAs exit; with self-issuing
+  // one-warp CTAs, only as each CTA finishes - released at the start, the
+  // combine after it ran 40% slower (298 vs 213 us for decode + combine at the
+  // 8-GPU shard shape).
   griddep_wait();
-  griddep_launch_dependents();
+  if (!SP) griddep_launch_dependents();
   constexpr int kSubs = D / kSub;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -180,38 +192,64 @@ __global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
   const int kh0 = blockIdx.y * hpc;
   const long long total = hi - lo;
 
+  // Block `idx` of this CTA's range (0-based): its table entry and valid-token
+  // count (0: not loaded).  Called by each lane for its own block.
+  auto resolve = [&](long long idx, int* id, int* ntok) {
+    *id = 0;
+    *ntok = 0;
+    if (idx >= total) return;
+    const long long f = lo + idx;
+    long long s, j;
+    if (balanced) {
+      s = find_seq(sm.prefix, batch, f);
+      j = f - sm.prefix[s];
+    } else {
+      s = fixed_seq;
+      j = f;
+    }
+    const long long c = load_index(a.ctx, a.ctx_i64, s);
+    const long long raw = load_index(a.table, a.table_i64, s * a.table_stride + j);
+    const long long left = c - j * kBS;
+    const int nt = left < kBS ? (int)left : kBS;
+    if (raw < 0) {
+      return;
+    } else if (raw >= a.num_blocks) {
+      record_error(a.err, kErrBlockId);
+      return;
+    }
+    *id = (int)raw;
+    *ntok = nt;
+  };
+  // Fill stage st with block id (ntok > 0) or mark it empty; one thread.
+  auto fill_stage = [&](int st, int id_i, int nt_i) {
+    sm.meta[st] = nt_i;
+    if (nt_i > 0) {
+      unsigned char* kdst = sm.stages + (size_t)st * stage_bytes;
+      unsigned char* vdst = kdst + half_bytes;
+      mbar_arrive_expect_tx(&sm.full[st], (unsigned)stage_bytes);
+#pragma unroll
+      for (int sub = 0; sub < kSubs; ++sub) {
+        for (int hh = 0; hh < hpc; ++hh) {
+          const int off = sub * sub_bytes + hh * kBS * kSubRowBytes;
+          tma_load_5d(kdst + off, &tmk, &sm.full[st], sub * kSub, kh0 + hh, 0, id_i, a.layer);
+          tma_load_5d(vdst + off, &tmv, &sm.full[st], sub * kSub, kh0 + hh, 0, id_i, a.layer);
+        }
+      }
+    } else {
+      mbar_arrive(&sm.full[st]);
+    }
+  };
+
   // ---- producer warp -----------------------------------------------------------
-  if (warp == hpc) {
+  if (!SP && warp == hpc) {
     if (lane == 0) {
       prefetch_tensormap(&tmk);
       prefetch_tensormap(&tmv);
     }
     for (long long base = 0; base < total; base += 32) {
       // Each lane resolves one block: its table entry and valid-token count.
-      int id = 0, ntok = 0;
-      if (base + lane < total) {
-        const long long f = lo + base + lane;
-        long long s, j;
-        if (balanced) {
-          s = find_seq(sm.prefix, batch, f);
-          j = f - sm.prefix[s];
-        } else {
-          s = fixed_seq;
-          j = f;
-        }
-        const long long c = load_index(a.ctx, a.ctx_i64, s);
-        const long long raw = load_index(a.table, a.table_i64, s * a.table_stride + j);
-        const long long left = c - j * kBS;
-        ntok = left < kBS ? (int)left : kBS;
-        if (raw < 0) {
-          ntok = 0;
-        } else if (raw >= a.num_blocks) {
-          ntok = 0;
-          record_error(a.err, kErrBlockId);
-        } else {
-          id = (int)raw;
-        }
-      }
+      int id, ntok;
+      resolve(base + lane, &id, &ntok);
       const int cnt = total - base < 32 ? (int)(total - base) : 32;
       for (int i = 0; i < cnt; ++i) {
         const int id_i = __shfl_sync(0xffffffffu, id, i);
@@ -223,24 +261,7 @@ __global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
           if (round > 0 && !mbar_wait(&sm.empty[st], (unsigned)((round - 1) & 1))) {
             record_error(a.err, kErrWaitTimeout | kErrWaitSlot);
           }
-          sm.meta[st] = nt_i;
-          if (nt_i > 0) {
-            unsigned char* kdst = sm.stages + (size_t)st * stage_bytes;
-            unsigned char* vdst = kdst + half_bytes;
-            mbar_arrive_expect_tx(&sm.full[st], (unsigned)stage_bytes);
-#pragma unroll
-            for (int sub = 0; sub < kSubs; ++sub) {
-              for (int hh = 0; hh < hpc; ++hh) {
-                const int off = sub * sub_bytes + hh * kBS * kSubRowBytes;
-                tma_load_5d(kdst + off, &tmk, &sm.full[st], sub * kSub, kh0 + hh, 0, id_i,
-                            a.layer);
-                tma_load_5d(vdst + off, &tmv, &sm.full[st], sub * kSub, kh0 + hh, 0, id_i,
-                            a.layer);
-              }
-            }
-          } else {
-            mbar_arrive(&sm.full[st]);
-          }
+          fill_stage(st, id_i, nt_i);
         }
         __syncwarp();
       }
@@ -266,6 +287,37 @@ __global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
   const float scale_log2 = a.scale * kLog2e;
   const bool capped = a.softcap > 0.f;
   const int head_row0 = warp * kBS;  // first smem row of this head inside a slice
+
+  // Self-issuing: blocks [0, issued) have been issued; lane l caches the
+  // table entry of block cache_base + l.
+  long long issued = 0;
+  long long cache_base = -32;
+  int c_id = 0, c_nt = 0;
+  auto issue_upto = [&](long long limit) {
+    if (limit > total) limit = total;
+    while (issued < limit) {
+      if (issued >= cache_base + 32) {
+        cache_base = issued;
+        resolve(cache_base + lane, &c_id, &c_nt);
+      }
+      const int k = (int)(issued - cache_base);
+      const int id_i = __shfl_sync(0xffffffffu, c_id, k);
+      const int nt_i = __shfl_sync(0xffffffffu, c_nt, k);
+      // This stage's previous block was consumed by this warp: order its reads
+      // (and any zeroing) before the copy that overwrites it.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (lane == 0) fill_stage((int)(issued % nstages), id_i, nt_i);
+      __syncwarp();
+      ++issued;
+    }
+  };
+  if (SP) {
+    if (lane == 0) {
+      prefetch_tensormap(&tmk);
+      prefetch_tensormap(&tmv);
+    }
+    issue_upto(nstages);
+  }
 
   long long it = 0;
   long long cur = lo;
@@ -293,6 +345,8 @@ __global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
     for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
 
     for (long long f = cur; f < seg_end; ++f, ++it) {
+      // Self-issuing: keep nstages - 1 blocks in flight beyond this one.
+      if (SP) issue_upto(it + nstages);
       const int st = (int)(it % nstages);
       if (!mbar_wait(&sm.full[st], (unsigned)((it / nstages) & 1))) {
         record_error(a.err, kErrWaitTimeout | kErrWaitData);
@@ -396,7 +450,7 @@ __global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.empty[st]);
+      if (!SP && lane == 0) mbar_arrive(&sm.empty[st]);
     }
 
     // ---- finalize this (sequence, head) partial ------------------------------------
@@ -427,6 +481,7 @@ __global__ void __launch_bounds__((kMaxBoxHeads + 1) * 32, 1)
     }
     cur = seg_end;
   }
+  if (SP) griddep_launch_dependents();
 }
 
 // Two KV heads per CTA (one if the head count is odd).  Measured on B200 for
@@ -444,13 +499,14 @@ int choose_heads_per_cta(int kv_heads, int head_dim) {
 }
 
 template <int D, int Q_DT, int KV_DT>
-const void* kernel_ptr() {
-  return reinterpret_cast<const void*>(&decode_tma_kernel<D, Q_DT, KV_DT>);
+const void* kernel_ptr(bool sp) {
+  return sp ? reinterpret_cast<const void*>(&decode_tma_kernel<D, Q_DT, KV_DT, true>)
+            : reinterpret_cast<const void*>(&decode_tma_kernel<D, Q_DT, KV_DT, false>);
 }
 
-const void* select_kernel(const AttnArgs& a) {
+const void* select_kernel(const AttnArgs& a, bool sp = false) {
 #define LLMOPT_DECODE_CASE(DV, QT, KT) \
-  if (a.head_dim == DV && a.q_dtype == QT && a.kv_dtype == KT) return kernel_ptr<DV, QT, KT>();
+  if (a.head_dim == DV && a.q_dtype == QT && a.kv_dtype == KT) return kernel_ptr<DV, QT, KT>(sp);
 #define LLMOPT_DECODE_Q(DV, KT)     \
   LLMOPT_DECODE_CASE(DV, kF32, KT)  \
   LLMOPT_DECODE_CASE(DV, kF16, KT)  \
@@ -486,6 +542,7 @@ bool decode_tma_supported(const AttnArgs& a) {
 }
 
 // Optional tuning overrides (LLMOPT_B200_DECODE_HPC: KV heads per CTA,
+// LLMOPT_B200_DECODE_SP: 0/1 self-issuing single-head CTAs,
 // LLMOPT_B200_DECODE_STAGES: ring depth); invalid values are ignored.
 int env_int(const char* name, int dflt) {
   const char* v = std::getenv(name);
@@ -493,14 +550,19 @@ int env_int(const char* name, int dflt) {
 }
 
 bool decode_tma_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch) {
-  const void* fn = select_kernel(a);
-  if (fn == nullptr) return false;
   int hpc = choose_heads_per_cta(a.kv_heads, a.head_dim);
   const int hpc_env = env_int("LLMOPT_B200_DECODE_HPC", 0);
   if (hpc_env >= 1 && hpc_env <= kMaxBoxHeads && a.kv_heads % hpc_env == 0 &&
       2ull * hpc_env * kBS * a.head_dim * 2 <= 64 * 1024) {
     hpc = hpc_env;
   }
+  // A single-head CTA issues its own copies (one warp, no producer warp).
+  bool sp = hpc == 1;
+  const int sp_env = env_int("LLMOPT_B200_DECODE_SP", -1);
+  if (sp_env == 0 || sp_env == 1) sp = sp_env == 1;
+  if (hpc != 1 || a.head_dim > 128) sp = false;   // head_dim 256 would spill at its bound
+  const void* fn = select_kernel(a, sp);
+  if (fn == nullptr) return false;
   const long long prefix_entries = a.plan.mode == kModeBalanced ? a.batch + 1 : 0;
   // Double buffering per CTA; parallelism comes from several CTAs per SM.
   int stages = env_int("LLMOPT_B200_DECODE_STAGES", 2);
@@ -518,12 +580,13 @@ bool decode_tma_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch)
     return false;
   }
   int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, (hpc + 1) * 32, smem) !=
-          cudaSuccess ||
+  const int threads = sp ? 32 : (hpc + 1) * 32;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem) != cudaSuccess ||
       occ < 1) {
     return false;
   }
   launch->heads_per_cta = hpc;
+  launch->self_issue = sp ? 1 : 0;
   launch->stages = stages;
   launch->ctas_per_sm = occ;
   launch->smem_bytes = smem;
@@ -534,7 +597,7 @@ bool decode_tma_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch)
 cudaError_t decode_tma_launch(const AttnArgs& a, const DecodeLaunch& launch,
                               const CUtensorMap& tmk, const CUtensorMap& tmv,
                               cudaStream_t stream) {
-  const void* fn = select_kernel(a);
+  const void* fn = select_kernel(a, launch.self_issue != 0);
   if (fn == nullptr) return cudaErrorInvalidValue;
   const int head_groups = a.kv_heads / launch.heads_per_cta;
   const long long gx =
@@ -542,7 +605,7 @@ cudaError_t decode_tma_launch(const AttnArgs& a, const DecodeLaunch& launch,
   if (gx <= 0) return cudaSuccess;
   if (gx > 0x7fffffffLL || head_groups > 65535) return cudaErrorInvalidConfiguration;
   dim3 grid((unsigned)gx, (unsigned)head_groups);
-  dim3 block((launch.heads_per_cta + 1) * 32);
+  dim3 block(launch.self_issue ? 32 : (launch.heads_per_cta + 1) * 32);
   int hpc = launch.heads_per_cta;
   int stages = launch.stages;
   void* args[] = {const_cast<CUtensorMap*>(&tmk), const_cast<CUtensorMap*>(&tmv),

@@ -54,6 +54,7 @@ struct AttnArgs {
 // Fast decode path: TMA-staged blocks + m16n8k16 tensor-core tiles.
 struct DecodeLaunch {
   int heads_per_cta;  // KV heads one CTA stages per block (box height)
+  int self_issue;     // 1: one-warp CTAs that issue their own copies (heads_per_cta == 1)
   int stages;         // shared-memory ring depth
   int ctas_per_sm;
   size_t smem_bytes;

@@ -61,6 +61,24 @@ def test_decode_shapes(cuda, head_dim, heads, kv_heads):
     check_case(cuda, case)
 
 
+@pytest.mark.parametrize("self_issue", [0, 1])
+def test_single_head_ctas(cuda, monkeypatch, self_issue):
+    """One KV head per CTA (the 8-GPU shard shape), with a separate producer
+    warp or with one warp issuing its own copies: ragged and one-block
+    sequences, long ones over many CTAs, -1 holes, partial last blocks (stale V
+    rows zeroed before the stage is refilled), q_len > 1 rows, both plans."""
+    monkeypatch.setenv("LLMOPT_B200_DECODE_SP", str(self_issue))
+    ctx = [1, 16, 17, 33, 47, 300, 2049, 5000, 64, 31]
+    holes = [(3, 1), (5, 7), (6, 0), (7, 100), (7, 101)]
+    for heads, kv_heads, head_dim, q_len in ((4, 1, 128, 1), (3, 3, 128, 1), (8, 1, 64, 2),
+                                             (4, 1, 128, 4)):
+        case = build_paged_case(950 + heads + head_dim + q_len + self_issue, batch=len(ctx),
+                                heads=heads, kv_heads=kv_heads, head_dim=head_dim,
+                                block_size=16, ctx=ctx, kv_kind="bf16", q_kind="bf16",
+                                q_len=q_len, value_scale=0.5, holes=holes)
+        check_case(cuda, case, modes=("auto", "fixed"))
+
+
 @pytest.mark.parametrize("q_len,heads", [(2, 32), (4, 32), (16, 8), (3, 16)])
 def test_short_chunks_on_tensor_core_path(cuda, q_len, heads):
     """q_len * group <= 16: speculative-decode sized chunks, causal inside the chunk."""
