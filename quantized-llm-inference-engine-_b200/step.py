@@ -21,6 +21,61 @@ from . import _lib
 from . import _runtime as rt
 
 
+class StepLedger:
+    """Host bookkeeping of the device step state (no device memory): which
+    sequence holds which row, how many blocks each row has, and the update
+    records (op, row, a, b) the next step must apply, in order."""
+
+    def __init__(self, max_seqs: int, max_blocks: int) -> None:
+        self.max_seqs = max_seqs
+        self.max_blocks = max_blocks
+        self.pending: list[tuple[int, int, int, int]] = []
+        self.order: list = []                  # row -> sequence id
+        self.rows: dict = {}                   # sequence id -> row
+        self.nblocks: dict = {}                # sequence id -> blocks in its row
+
+    def admit(self, seq_id, blocks, committed: int) -> int:
+        if seq_id in self.rows:
+            raise ValueError(f"sequence {seq_id!r} is already running")
+        if len(self.order) >= self.max_seqs:
+            raise ValueError("no free row")
+        blocks = [int(b) for b in blocks]
+        if len(blocks) > self.max_blocks:
+            raise ValueError(f"{len(blocks)} blocks exceed the table width {self.max_blocks}")
+        row = len(self.order)
+        self.order.append(seq_id)
+        self.rows[seq_id] = row
+        self.nblocks[seq_id] = len(blocks)
+        self.pending.append((_lib.STEP_ADMIT, row, int(committed), 0))
+        for c, b in enumerate(blocks):
+            self.pending.append((_lib.STEP_SET_BLOCK, row, c, b))
+        return row
+
+    def append_block(self, seq_id, block_id: int) -> None:
+        row = self.rows[seq_id]
+        col = self.nblocks[seq_id]
+        if col >= self.max_blocks:
+            raise ValueError(f"sequence {seq_id!r} exceeds the table width {self.max_blocks}")
+        self.nblocks[seq_id] = col + 1
+        self.pending.append((_lib.STEP_SET_BLOCK, row, col, int(block_id)))
+
+    def release(self, seq_id) -> None:
+        row = self.rows.pop(seq_id)
+        self.nblocks.pop(seq_id)
+        last = len(self.order) - 1
+        if row != last:
+            moved = self.order[last]
+            self.pending.append((_lib.STEP_MOVE, row, last, 0))
+            self.order[row] = moved
+            self.rows[moved] = row
+        self.order.pop()
+
+    def take(self) -> list:
+        """The records of the next step (and forget them)."""
+        out, self.pending = self.pending, []
+        return out
+
+
 class DecodeStepState:
     """Device-resident ``block_ids`` / ``context_lens`` / ``token_offsets`` /
     ``positions`` for up to ``max_seqs`` decoding sequences.
@@ -51,53 +106,36 @@ class DecodeStepState:
         self._copied = [None, None]
         self._turn = 0
         self._dev = torch.zeros(1 + 4 * capacity, dtype=torch.int64, device=self.device)
-        self._pending: list[tuple[int, int, int, int]] = []
-        self.order: list = []                  # row -> sequence id
-        self._row: dict = {}                   # sequence id -> row
-        self._nblocks: dict = {}               # sequence id -> blocks in its row
+        self.ledger = StepLedger(max_seqs, max_blocks)
 
     # -- scheduling decisions (host) ---------------------------------------------
+    @property
+    def order(self) -> list:
+        """Sequence id of every running row."""
+        return self.ledger.order
+
+    @property
+    def _pending(self) -> list:
+        return self.ledger.pending
+
+    @property
+    def _nblocks(self) -> dict:
+        return self.ledger.nblocks
+
     def admit(self, seq_id, blocks, committed: int) -> int:
         """A sequence joins with ``committed`` tokens already in its ``blocks``."""
-        if seq_id in self._row:
-            raise ValueError(f"sequence {seq_id!r} is already running")
-        if len(self.order) >= self.max_seqs:
-            raise ValueError("no free row")
-        blocks = [int(b) for b in blocks]
-        if len(blocks) > self.max_blocks:
-            raise ValueError(f"{len(blocks)} blocks exceed the table width {self.max_blocks}")
-        row = len(self.order)
-        self.order.append(seq_id)
-        self._row[seq_id] = row
-        self._nblocks[seq_id] = len(blocks)
-        self._pending.append((_lib.STEP_ADMIT, row, int(committed), 0))
-        for c, b in enumerate(blocks):
-            self._pending.append((_lib.STEP_SET_BLOCK, row, c, b))
-        return row
+        return self.ledger.admit(seq_id, blocks, committed)
 
     def append_block(self, seq_id, block_id: int) -> None:
         """The sequence's next token needs one more block."""
-        row = self._row[seq_id]
-        col = self._nblocks[seq_id]
-        if col >= self.max_blocks:
-            raise ValueError(f"sequence {seq_id!r} exceeds the table width {self.max_blocks}")
-        self._nblocks[seq_id] = col + 1
-        self._pending.append((_lib.STEP_SET_BLOCK, row, col, int(block_id)))
+        self.ledger.append_block(seq_id, block_id)
 
     def release(self, seq_id) -> None:
         """The sequence finished; the last row moves into its place."""
-        row = self._row.pop(seq_id)
-        self._nblocks.pop(seq_id)
-        last = len(self.order) - 1
-        if row != last:
-            moved = self.order[last]
-            self._pending.append((_lib.STEP_MOVE, row, last, 0))
-            self.order[row] = moved
-            self._row[moved] = row
-        self.order.pop()
+        self.ledger.release(seq_id)
 
     def row_of(self, seq_id) -> int:
-        return self._row[seq_id]
+        return self.ledger.rows[seq_id]
 
     # -- the step (device) ---------------------------------------------------------
     def step(self):
@@ -116,7 +154,8 @@ class DecodeStepState:
         """Copy the recorded changes into the device update buffer (stream
         ordered, no host sync unless the staging buffer in turn is still being
         copied from two steps ago); ``launch`` or a graph replay applies them."""
-        n = len(self._pending)
+        records = self.ledger.take()
+        n = len(records)
         if n > self.capacity:
             raise ValueError(f"{n} updates exceed the capacity {self.capacity}")
         k = self._turn
@@ -126,8 +165,7 @@ class DecodeStepState:
         host = self._hosts[k]
         host[0] = n
         if n:
-            host[1:1 + 4 * n] = torch.tensor(self._pending, dtype=torch.int64).reshape(-1)
-        self._pending.clear()
+            host[1:1 + 4 * n] = torch.tensor(records, dtype=torch.int64).reshape(-1)
         self._dev[:1 + 4 * n].copy_(host[:1 + 4 * n], non_blocking=True)
         ev = torch.cuda.Event()
         ev.record(torch.cuda.current_stream(self.device))
