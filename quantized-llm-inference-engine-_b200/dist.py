@@ -276,7 +276,7 @@ class ShardedPagedAttention:
             self.peers = PeerGroup(self.group, device)
         dtype = query_local.dtype if query_local.dtype in (
             torch.float32, torch.float16, torch.bfloat16) else torch.float32
-        elem = torch.empty((), dtype=dtype).element_size()
+        elem = torch.finfo(dtype).bits // 8
         nbytes = self.num_heads * seq * q_len * self.head_dim * elem
         if phases & _lib.PHASE_COMBINE:
             epoch, which, bufs, flags = self.peers.next_call(nbytes)
