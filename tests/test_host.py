@@ -171,3 +171,73 @@ def test_package_alias_import():
     import llmopt_b200
 
     assert llmopt_b200.PagedAttention is load_package().PagedAttention
+
+
+def _rope(lib, **kw):
+    """llmopt_rope_kv_append with valid defaults (null data pointers: only
+    argument checks that come before any launch are exercised)."""
+    a = dict(q=None, k=None, v=None, in_dt=2, q_row=512, k_row=128, v_row=128, pos=None, p64=1,
+             cos=None, sin=None, tab_dt=0, max_pos=4096, q_out=None, qo_s=0, qo_h=0, qo_t=0,
+             kc=None, vc=None, kv_dt=2, L=2, NB=8, BS=16, KVH=2, D=64, layer=1, table=None,
+             t64=0, width=4, stride=4, offs=None, o64=1, batch=1, H=8, q_len=1)
+    a.update(kw)
+    return lib.llmopt_rope_kv_append(
+        a["q"], a["k"], a["v"], a["in_dt"], a["q_row"], a["k_row"], a["v_row"], a["pos"],
+        a["p64"], a["cos"], a["sin"], a["tab_dt"], a["max_pos"], a["q_out"], a["qo_s"],
+        a["qo_h"], a["qo_t"], a["kc"], a["vc"], a["kv_dt"], a["L"], a["NB"], a["BS"], a["KVH"],
+        a["D"], a["layer"], a["table"], a["t64"], a["width"], a["stride"], a["offs"], a["o64"],
+        a["batch"], a["H"], a["q_len"], None, None)
+
+
+def test_rope_entry_rejects_bad_arguments_before_any_launch(pkg):
+    lib = pkg.lib()
+    assert _rope(lib, D=63) == 1                 # odd head_dim
+    assert _rope(lib, in_dt=7) == 2              # unsupported model dtype
+    assert _rope(lib, tab_dt=5) == 2             # unsupported table dtype
+    assert _rope(lib, kv_dt=4) == 2              # unsupported cache dtype
+    assert _rope(lib, H=7) == 1                  # heads not a multiple of kv heads
+    assert _rope(lib, layer=2) == 5              # layer out of range -> IndexError
+    with pytest.raises(IndexError):
+        pkg.check(_rope(lib, layer=-1), "rope")
+    assert _rope(lib, max_pos=0) == 1
+    assert _rope(lib, batch=0) == 0              # empty batch: nothing to do
+    assert _rope(lib, q_len=0) == 0
+    assert _rope(lib) == 1                       # null pointers with work to do
+    assert _rope(lib, width=0) == 5              # empty block table
+
+
+def test_step_advance_rejects_bad_arguments_before_any_launch(pkg):
+    lib = pkg.lib()
+    fake = ctypes.c_void_p(256)
+    st = lib.llmopt_decode_step_advance(fake, -1, fake, 4, 4, fake, fake, fake, 8, 2, None, None)
+    assert st == 1                               # negative capacity
+    st = lib.llmopt_decode_step_advance(fake, 8, fake, 4, 3, fake, fake, fake, 8, 2, None, None)
+    assert st == 1                               # row stride shorter than the width
+    st = lib.llmopt_decode_step_advance(fake, 8, fake, 4, 4, fake, fake, fake, 8, 9, None, None)
+    assert st == 1                               # more active rows than rows
+    st = lib.llmopt_decode_step_advance(None, 8, fake, 4, 4, fake, fake, fake, 8, 2, None, None)
+    assert st == 1                               # null update buffer
+
+
+def test_gather_and_peer_entries_reject_bad_arguments(pkg):
+    lib = pkg.lib()
+    arr = (ctypes.c_void_p * 2)(256, 512)
+    misaligned = (ctypes.c_void_p * 2)(256, 520)
+
+    def gather(bufs, flags, world, rank, batch=1):
+        return lib.llmopt_paged_attention_gather(
+            None, 2, 0, 0, 0, None, None, 2, 1, 1, 16, 2, 64, 0, None, 0, 1, 1, None, 0,
+            bufs, flags, world, rank, 1, 2, None, batch, 8, 1, 0.125, 0.0, 0, None, 0, None,
+            None, 3)
+
+    assert gather(arr, arr, 9, 0) == 1           # more ranks than a group holds
+    assert gather(arr, arr, 2, 2) == 1           # rank outside the group
+    assert gather(None, arr, 2, 0) == 1          # null peer array
+    assert gather(arr, misaligned, 2, 0) == 1    # peer flags not 16-byte aligned
+    assert gather(arr, arr, 2, 1, batch=0) == 0  # valid group, nothing to do
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    assert lib.llmopt_peer_alloc(0, 0, ctypes.byref(ptr), handle) == 1      # zero bytes
+    assert lib.llmopt_peer_alloc(0, 64, None, handle) == 1                  # no output slot
+    assert lib.llmopt_peer_open(0, None, ctypes.byref(ptr)) == 1            # no handle
+    assert lib.llmopt_peer_close(0, None) == 0 and lib.llmopt_peer_free(0, None) == 0
