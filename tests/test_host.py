@@ -11,6 +11,8 @@ import re
 import sys
 
 import pytest
+
+REPO_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 import torch
 
 from conftest import REPO, load_package
@@ -127,7 +129,10 @@ def test_missing_library_fails_loudly(monkeypatch):
         _lib.lib()
 
 
-REFERENCE_SRC = "/root/reference/src"
+# The reference's source tree: LLMOPT_REFERENCE_SRC, else a "reference" checkout
+# next to this repository.  The test is skipped where neither exists.
+REFERENCE_SRC = os.environ.get("LLMOPT_REFERENCE_SRC") or os.path.join(
+    os.path.dirname(REPO_ROOT), "reference", "src")
 
 
 @pytest.mark.skipif(not os.path.isdir(REFERENCE_SRC), reason="reference source not present")
