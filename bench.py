@@ -63,7 +63,8 @@ def parse_args(argv=None):
                         "peer memory, or NCCL all_gather_into_tensor after it")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--config", choices=("c2", "c3", "c4", "c5", "rope", "step"), default="c2",
+    p.add_argument("--config", choices=("c2", "c3", "c4", "c5", "rope", "step", "fp8"),
+                   default="c2",
                    help="c2 (default, the headline line): Llama-3-8B decode; c3: chunked "
                         "prefill; c4: 128k-context decode sharded by KV head (strong "
                         "scaling); c5: shared-prefix decode (strong scaling); rope: the "
@@ -71,7 +72,8 @@ def parse_args(argv=None):
                         "a 64-sequence decode step (weak scaling by KV head); step: a whole "
                         "decode step (device-side metadata advance, rotary append, "
                         "attention) replayed from a CUDA graph vs launched eagerly, beside "
-                        "the reference runner's host-side metadata build")
+                        "the reference runner's host-side metadata build; fp8: the config-2 "
+                        "decode step over an e4m3 KV cache beside the bf16 one (1 GPU)")
     return p.parse_args(argv)
 
 
@@ -1022,6 +1024,115 @@ def run_step(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_fp8(args) -> None:
+    """Config-2 decode step over an FP8 (e4m3 + per-row scale) KV cache, one GPU,
+    beside the same step over the bf16 cache: append (quantizing) + split-K
+    decode + combine.  Bytes are the fp8 step's algorithmic bytes (codes, row
+    scales, q, out, block table)."""
+    import torch
+
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        print(json.dumps({"config": "fp8", "skipped": "single-GPU line"}), flush=True)
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pkg = importlib.import_module(PACKAGE)
+    _lib = importlib.import_module(f"{PACKAGE}._lib")
+    from oracle.paged_oracle import decode_bytes
+
+    wl = make_workload(args, 1)
+    B = wl["batch"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(3000)
+    table = torch.from_numpy(wl["table"]).to(dev)
+    ctx = torch.from_numpy(wl["ctx"]).to(dev)
+    offs = torch.from_numpy(wl["offsets"]).to(dev)
+    q = (torch.randn((B, HEADS, 1, HEAD_DIM), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    knew = (torch.randn((B, KV_HEADS, HEAD_DIM), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    vnew = (torch.randn((B, KV_HEADS, HEAD_DIM), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    out = torch.empty((B, HEADS, 1, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    attn = pkg.PagedAttention(HEADS, KV_HEADS, HEAD_DIM)
+    ctx_np = wl["ctx"]
+    lines = {}
+    for name, dt in (("bf16", torch.bfloat16), ("fp8", torch.float8_e4m3fn)):
+        cache = pkg.PagedKVCache(1, wl["num_blocks"], BLOCK, KV_HEADS, HEAD_DIM, dtype=dt,
+                                 device=dev)
+        for t in (cache.key_cache, cache.value_cache):
+            for i in range(0, t.shape[1], 4096):
+                sl = t[:, i:i + 4096]
+                if dt == torch.bfloat16:
+                    sl.copy_(torch.randn(sl.shape, generator=g, device=dev) * 0.5)
+                else:   # finite codes (no NaN pattern), either sign
+                    codes = torch.randint(0, 0x7E, sl.shape, generator=g, device=dev,
+                                          dtype=torch.int32)
+                    sign = torch.randint(0, 2, sl.shape, generator=g, device=dev,
+                                         dtype=torch.int32) << 7
+                    sl.view(torch.uint8).copy_((codes | sign).to(torch.uint8))
+        if cache.is_fp8:
+            for s in (cache.key_scale, cache.value_scale):
+                s.copy_(torch.rand(s.shape, generator=g, device=dev) * (1.0 / 448) + 1e-4)
+
+        def step(ev=None):
+            if ev is not None:
+                ev[0].record()
+            cache.write_decode(0, table, offs, knew, vnew)
+            if ev is not None:
+                ev[1].record()
+            attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out,
+                                  phases=_lib.PHASE_SPLIT)
+            if ev is not None:
+                ev[2].record()
+            attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out,
+                                  phases=_lib.PHASE_COMBINE)
+            if ev is not None:
+                ev[3].record()
+
+        for _ in range(max(args.warmup, 3)):
+            step()
+        every = 10
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)]
+               for _ in range((args.steps + every - 1) // every)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        sampler = ClockSampler(0)
+        sampler.start()
+        start.record()
+        for i in range(args.steps):
+            step(evs[i // every] if i % every == 0 else None)
+        end.record()
+        torch.cuda.synchronize(dev)
+        clocks = sampler.stop()
+        ms_step = start.elapsed_time(end) / args.steps
+        kv_bytes = 1 if cache.is_fp8 else 2
+        dec = decode_bytes(ctx_np, KV_HEADS, HEAD_DIM, kv_bytes, B, HEADS, 2, 2, BLOCK)
+        if cache.is_fp8:
+            dec += int(ctx_np.sum()) * KV_HEADS * 2 * 4        # K and V row scales
+        decode_ms = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
+        lines[name] = dict(
+            ms_per_step=round(ms_step, 5), decode_tok_s=round(B / (ms_step * 1e-3), 1),
+            bytes_per_step=int(dec), step_GBps=round(dec / (ms_step * 1e-3) / 1e9, 1),
+            kernel_ms={"append": round(statistics.fmean(e[0].elapsed_time(e[1]) for e in evs), 5),
+                       "decode_split": round(decode_ms, 5),
+                       "combine": round(statistics.fmean(e[2].elapsed_time(e[3]) for e in evs), 5)},
+            decode_kernel_GBps=round(dec / (decode_ms * 1e-3) / 1e9, 1), clocks=clocks)
+        del cache
+        torch.cuda.empty_cache()
+    peak, peak_kind = measured_hbm_peak()
+    f8 = lines["fp8"]
+    print(json.dumps({
+        "config": "fp8",
+        "metric": "paged-decode step, e4m3 KV cache (codes + fp32 row scales), HBM GB/s",
+        "unit": "GB/s", "value": f8["step_GBps"], "n_gpus": 1, "steps": args.steps,
+        "workload": "config2 shape (B64, H32/KVH8, D128, ctx U[1024,8192]) decode step: "
+                    "quantizing append + split-K decode + combine",
+        "fp8": f8, "bf16": lines["bf16"],
+        "speedup_vs_bf16_step": round(lines["bf16"]["ms_per_step"] / f8["ms_per_step"], 3),
+        "roofline": {"bound": "hbm", "achieved": f8["decode_kernel_GBps"], "peak": peak,
+                     "unit": "GB/s", "frac": round(f8["decode_kernel_GBps"] / peak, 4),
+                     "kernel": "decode_fp8_kernel", "peak_kind": f"{peak_kind} hbm_gbs"},
+    }), flush=True)
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
@@ -1030,6 +1141,8 @@ def main(argv=None):
         run_step(args)
     elif args.config == "rope":
         run_rope(args)
+    elif args.config == "fp8":
+        run_fp8(args)
     elif args.config != "c2":
         run_extra(args)
     else:

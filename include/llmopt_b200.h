@@ -30,6 +30,10 @@
  *                              PagedAttentionLayer.forward  src/llmopt/model/layers.py:106-134
  *                              (RotaryEmbedding.forward, apply_rotary_pos_emb
  *                              src/llmopt/model/rotary.py:16-46, 103-121)
+ *   llmopt_*_scaled         <- the same operations on an FP8 (e4m3) cache; the
+ *                              reference only names the float8 dtypes
+ *                              (src/llmopt/utils/misc.py:33-34, 57) and has no
+ *                              fp8 attention of its own.
  */
 #ifndef LLMOPT_B200_H_
 #define LLMOPT_B200_H_
@@ -49,11 +53,13 @@ extern "C" {
 
 #define LLMOPT_B200_ABI_VERSION 1
 
-/* Element types (torch.float32 / float16 / bfloat16). */
+/* Element types (torch.float32 / float16 / bfloat16; float8_e4m3fn for
+ * caches through the *_scaled entry points only). */
 enum {
   LLMOPT_DTYPE_F32 = 0,
   LLMOPT_DTYPE_F16 = 1,
-  LLMOPT_DTYPE_BF16 = 2
+  LLMOPT_DTYPE_BF16 = 2,
+  LLMOPT_DTYPE_E4M3 = 3
 };
 
 /* Return codes. The Python layer maps them to the reference's exception types. */
@@ -351,6 +357,63 @@ LLMOPT_API int llmopt_decode_step_advance(const int64_t* updates, int64_t capaci
                                           int64_t* token_offsets, int64_t* positions,
                                           int64_t max_rows, int64_t batch, uint32_t* err,
                                           void* stream);
+
+/*
+ * FP8 KV storage.  An e4m3 cache is key_cache / value_cache in the usual
+ * [num_layers, num_blocks, block_size, num_kv_heads, head_dim] layout holding
+ * float8_e4m3fn codes, plus key_scale / value_scale: contiguous fp32
+ * [num_layers, num_blocks, num_kv_heads, block_size] (head-major within a
+ * block, so one head's scales for a block are 64 contiguous bytes).  Element
+ * value = code * scale of its (token, head) row.  The appends quantize each
+ * (token, head) row on its own: scale = amax(|row|) / 448 (NaN ignored; 1 when
+ * not positive), code = e4m3(x / scale), both rounded to nearest even (the
+ * code rounding is torch's .to(torch.float8_e4m3fn)).  Attention reads the
+ * cache as those values with the query rounded to f16; outputs, LSE, splits,
+ * workspace and errors as llmopt_paged_attention_phase.  Gather returns the
+ * dequantized values as fp32.  Caches and scales 16-byte aligned, head_dim
+ * <= 256; the tensor-core decode covers block_size 16, head_dim 128 or 256
+ * and q_len * group <= 16, everything else runs on CUDA cores.
+ */
+LLMOPT_API int llmopt_kv_write_scaled(const void* keys, const void* values, int32_t in_dtype,
+                    int64_t k_s, int64_t k_t, int64_t k_h, int64_t v_s, int64_t v_t, int64_t v_h,
+                    void* key_cache, void* value_cache, int32_t kv_dtype,
+                    float* key_scale, float* value_scale,
+                    int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                    const void* block_table, int32_t table_is_i64, int64_t table_width,
+                    int64_t table_stride, const void* token_offsets, int32_t off_is_i64,
+                    int64_t batch, int32_t q_len, uint32_t* err, void* stream);
+
+LLMOPT_API int llmopt_kv_write_decode_scaled(const void* keys, const void* values,
+                    int32_t in_dtype, int64_t k_s, int64_t k_h, int64_t v_s, int64_t v_h,
+                    void* key_cache, void* value_cache, int32_t kv_dtype,
+                    float* key_scale, float* value_scale,
+                    int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                    const void* block_table, int32_t table_is_i64, int64_t table_width,
+                    int64_t table_stride, const void* token_offsets, int32_t off_is_i64,
+                    int64_t batch, uint32_t* err, void* stream);
+
+LLMOPT_API int llmopt_paged_attention_scaled(const void* query, int32_t q_dtype, int64_t q_s,
+                    int64_t q_h, int64_t q_t, const void* key_cache, const void* value_cache,
+                    int32_t kv_dtype, const float* key_scale, const float* value_scale,
+                    int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                    const void* block_table, int32_t table_is_i64, int64_t table_width,
+                    int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
+                    void* out, int32_t out_dtype, int64_t o_s, int64_t o_h, int64_t o_t,
+                    float* lse, int64_t batch, int32_t num_heads, int32_t q_len, float scale,
+                    float softcap, int64_t split_tokens, void* workspace,
+                    size_t workspace_bytes, uint32_t* err, void* stream, int32_t phases);
+
+LLMOPT_API int llmopt_paged_gather_scaled(const void* key_cache, const void* value_cache,
+                    int32_t kv_dtype, const float* key_scale, const float* value_scale,
+                    int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                    const void* block_table, int32_t table_is_i64, int64_t table_width,
+                    int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
+                    int64_t batch, int64_t max_len, float* out_keys, float* out_values,
+                    uint8_t* valid, uint32_t* err, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -63,6 +63,14 @@ __all__ = [
     "attention_lse",
     "decode_bytes",
     "prefill_flops",
+    "E4M3_MAX",
+    "e4m3_to_f32",
+    "f32_to_e4m3",
+    "quantize_rows_e4m3",
+    "dequantize_e4m3",
+    "write_e4m3",
+    "write_decode_e4m3",
+    "paged_attention_e4m3",
 ]
 
 KINDS = ("f32", "f16", "bf16")
@@ -241,6 +249,167 @@ def write_decode(key_cache: np.ndarray, value_cache: np.ndarray, kind: str, laye
     for s in range(B):
         key_cache[layer, blocks[s], slot[s]] = convert(keys[s], in_kind, kind)
         value_cache[layer, blocks[s], slot[s]] = convert(values[s], in_kind, kind)
+
+
+# ---------------------------------------------------------------------------
+# FP8 (e4m3) KV storage.  Beyond the reference: it only names the dtypes
+# (src/llmopt/utils/misc.py:33-34, 57); its attention would call a matmul in
+# float8, which torch has no kernel for, so there is no reference behaviour to
+# match.  The storage defined here: float8_e4m3fn codes in the reference's
+# [L, num_blocks, block_size, kv_heads, head_dim] layout plus one float32 scale
+# per (token, head) row in a [L, num_blocks, kv_heads, block_size] array; the
+# row's value is code * scale, scale = amax(|row|) / 448.  The code rounding is
+# torch's ``.to(torch.float8_e4m3fn)`` (pinned against it by the CPU tests).
+# ---------------------------------------------------------------------------
+
+E4M3_MAX = np.float32(448.0)
+
+
+def _e4m3_table() -> np.ndarray:
+    """float32 value of every e4m3fn code (bias 7, 3 mantissa bits, no
+    infinities, S.1111.111 = NaN)."""
+    codes = np.arange(256, dtype=np.int64)
+    sign = np.where(codes & 0x80, -1.0, 1.0)
+    exp = (codes >> 3) & 0xF
+    man = codes & 0x7
+    mag = np.where(exp == 0, man / 8.0 * 2.0 ** -6, (1.0 + man / 8.0) * 2.0 ** (exp - 7))
+    val = (sign * mag).astype(np.float32)
+    val[(codes & 0x7F) == 0x7F] = np.nan
+    return val
+
+
+_E4M3 = _e4m3_table()
+_E4M3_POS = _E4M3[:0x7F].astype(np.float64)     # codes 0..126, increasing
+
+
+def e4m3_to_f32(codes: np.ndarray) -> np.ndarray:
+    """Exact float32 value of e4m3fn codes (uint8)."""
+    return _E4M3[np.asarray(codes, dtype=np.uint8)]
+
+
+def f32_to_e4m3(x: np.ndarray) -> np.ndarray:
+    """float32 -> e4m3fn codes with round-to-nearest-even, as torch's cast:
+    magnitudes that round past 448 (above 464) and NaN become NaN (0x7F with
+    the sign bit), -0.0 keeps its sign."""
+    x = np.asarray(x, dtype=np.float32)
+    mag = np.abs(x).astype(np.float64)
+    idx = np.clip(np.searchsorted(_E4M3_POS, mag), 1, 0x7E)
+    lo, hi = idx - 1, idx
+    dlo = mag - _E4M3_POS[lo]
+    dhi = _E4M3_POS[hi] - mag
+    # nearest code; a tie goes to the even code (the even mantissa)
+    code = np.where((dhi < dlo) | ((dhi == dlo) & (hi % 2 == 0)), hi, lo)
+    code = np.where(mag >= _E4M3_POS[0x7E], 0x7E, code)
+    code = np.where((mag > 464.0) | np.isnan(x), 0x7F, code)
+    sign = np.signbit(x).astype(np.int64) << 7
+    return (code | sign).astype(np.uint8)
+
+
+def quantize_rows_e4m3(x: np.ndarray):
+    """Quantize the last axis of float32 ``x`` row by row: returns (codes,
+    scales) with scale = amax / 448 (amax over |x|, NaN ignored; 1 when that
+    is not a positive number) and codes = e4m3(x / scale), both steps in
+    float32 with round-to-nearest."""
+    x = np.asarray(x, dtype=np.float32)
+    with np.errstate(invalid="ignore"):
+        amax = np.fmax.reduce(np.abs(x), axis=-1) if x.shape[-1] else np.zeros(x.shape[:-1])
+    amax = np.asarray(amax, dtype=np.float32)
+    scale = (amax / E4M3_MAX).astype(np.float32)
+    with np.errstate(invalid="ignore"):
+        scale = np.where(scale > 0, scale, np.float32(1.0)).astype(np.float32)
+    with np.errstate(invalid="ignore", over="ignore"):
+        q = (x / scale[..., None]).astype(np.float32)
+    return f32_to_e4m3(q), scale
+
+
+def dequantize_e4m3(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """[L, nb, bs, kvh, D] codes and [L, nb, kvh, bs] scales -> float32 values
+    (code value * scale, one float32 product)."""
+    s = np.asarray(scales, dtype=np.float32).transpose(0, 1, 3, 2)[..., None]
+    with np.errstate(invalid="ignore", over="ignore"):
+        return (e4m3_to_f32(codes) * s).astype(np.float32)
+
+
+def _store_e4m3(codes, scales, layer, block, lo, rows_f32):
+    """Quantize rows [take, kvh, D] into slots lo.. of a block."""
+    q, s = quantize_rows_e4m3(rows_f32)
+    take = rows_f32.shape[0]
+    codes[layer, block, lo:lo + take] = q
+    scales[layer, block, :, lo:lo + take] = s.T
+
+
+def write_e4m3(key_codes, value_codes, key_scales, value_scales, layer, block_ids,
+               token_offsets, keys, values, in_kind: str) -> None:
+    """``write`` (paged_cache.py:175-232: same walk, same stops) into an e4m3
+    cache: each appended (token, head) row is quantized with its own scale."""
+    B, q_len = keys.shape[0], keys.shape[1]
+    if q_len == 0 or B == 0:
+        return
+    block_ids = np.asarray(block_ids).astype(np.int64)
+    bs = key_codes.shape[2]
+    num_blocks = key_codes.shape[1]
+    for s in range(B):
+        start = int(token_offsets[s])
+        blocks = block_ids[s]
+        written = 0
+        cursor = start
+        block_index = start // bs
+        while written < q_len and block_index < blocks.shape[0]:
+            block = _block_at(blocks, block_index)
+            if block < 0:
+                break
+            if block >= num_blocks:
+                raise IndexError(f"block id {block} out of range")
+            lo = cursor % bs
+            take = min(bs - lo, q_len - written)
+            _store_e4m3(key_codes, key_scales, layer, block, lo,
+                        to_f32(keys[s, written:written + take], in_kind))
+            _store_e4m3(value_codes, value_scales, layer, block, lo,
+                        to_f32(values[s, written:written + take], in_kind))
+            written += take
+            cursor += take
+            if cursor % bs == 0:
+                block_index += 1
+
+
+def write_decode_e4m3(key_codes, value_codes, key_scales, value_scales, layer, block_ids,
+                      token_offsets, keys, values, in_kind: str) -> None:
+    """``write_decode`` (paged_cache.py:234-261: same slot, same block-0
+    redirect) into an e4m3 cache."""
+    B = keys.shape[0]
+    if B == 0:
+        return
+    block_ids = np.asarray(block_ids).astype(np.int64)
+    bs = key_codes.shape[2]
+    num_blocks = key_codes.shape[1]
+    offsets = np.asarray(token_offsets).astype(np.int64)
+    col = np.floor_divide(offsets, bs)
+    slot = np.mod(offsets, bs)
+    width = block_ids.shape[1]
+    if np.any(col < -width) or np.any(col >= width):
+        raise IndexError("decode offset outside the block table")
+    blocks = block_ids[np.arange(B), col]
+    valid = (blocks >= 0) & (blocks < num_blocks)
+    blocks = np.where(valid, blocks, 0)
+    for s in range(B):
+        _store_e4m3(key_codes, key_scales, layer, blocks[s], slot[s],
+                    to_f32(keys[s], in_kind)[None])
+        _store_e4m3(value_codes, value_scales, layer, blocks[s], slot[s],
+                    to_f32(values[s], in_kind)[None])
+
+
+def paged_attention_e4m3(query, q_kind, key_codes, value_codes, key_scales, value_scales,
+                         layer, block_ids, context_lens, num_heads, num_kv_heads,
+                         q_len=None, scale=None, config=None, acc=np.float64):
+    """Attention over an e4m3 cache: ``paged_attention`` on the dequantized
+    values, with the query rounded to float16 (the precision the kernels feed
+    the tensor cores; an e4m3 query would lose too much)."""
+    k = dequantize_e4m3(key_codes, key_scales)
+    v = dequantize_e4m3(value_codes, value_scales)
+    q16 = convert(query, q_kind, "f16")
+    return paged_attention(q16, "f16", k, v, "f32", layer, block_ids, context_lens,
+                           num_heads, num_kv_heads, q_len=q_len, scale=scale, config=config,
+                           acc=acc)
 
 
 # ---------------------------------------------------------------------------

@@ -117,7 +117,25 @@ SIGNATURES = {
         _p, _i32, _i64, _i64, _p, _i32,               # table, is64, width, stride, offsets, is64
         _i64, _i32, _i32, _p, _p],                    # batch, heads, q_len, err, stream
     "llmopt_decode_step_advance": [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p],
+    # e4m3 caches: the same arguments plus the two scale arrays after the cache dtype
+    "llmopt_kv_write_scaled": [
+        _p, _p, _i32, _i64, _i64, _i64, _i64, _i64, _i64,
+        _p, _p, _i32, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32,
+        _p, _i32, _i64, _i64, _p, _i32, _i64, _i32, _p, _p],
+    "llmopt_kv_write_decode_scaled": [
+        _p, _p, _i32, _i64, _i64, _i64, _i64,
+        _p, _p, _i32, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32,
+        _p, _i32, _i64, _i64, _p, _i32, _i64, _p, _p],
+    "llmopt_paged_attention_scaled": [
+        _p, _i32, _i64, _i64, _i64, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32,
+        _p, _i32, _i64, _i64, _p, _i32, _p, _i32, _i64, _i64, _i64, _p,
+        _i64, _i32, _i32, _f32, _f32, _i64, _p, ctypes.c_size_t, _p, _p, _i32],
+    "llmopt_paged_gather_scaled": [
+        _p, _p, _i32, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32,
+        _p, _i32, _i64, _i64, _p, _i32, _i64, _i64, _p, _p, _p, _p, _p],
 }
+
+DTYPE_E4M3 = 3
 
 _RESTYPES = {
     "llmopt_b200_version": ctypes.c_char_p,

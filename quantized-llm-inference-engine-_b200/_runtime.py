@@ -16,6 +16,8 @@ import torch
 from . import _lib
 
 DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+#: Cache dtypes: the activation dtypes plus float8_e4m3fn (scaled FP8 storage).
+KV_DTYPE_CODE = {**DTYPE_CODE, torch.float8_e4m3fn: 3}
 
 #: Set LLMOPT_B200_CHECK=1 to synchronise after each op and raise IndexError on
 #: any device-side index error (the reference raises at those points too).

@@ -210,7 +210,13 @@ class PagedAttention:
             raise ValueError("out must be [seq, num_heads, q_len, head_dim] with unit inner stride")
         lse = (torch.empty((seq_len, self.num_heads, q_len), dtype=torch.float32, device=device)
                if want_lse else None)
-        kv_code = rt.dtype_code(cache.key_cache.dtype, "cache")
+        fp8 = cache.key_cache.dtype == torch.float8_e4m3fn
+        if fp8 and gather is not None:
+            raise ValueError("the peer-transport gather takes 16-bit or fp32 caches; shard an "
+                             "e4m3 cache with transport='nccl'")
+        kv_code = rt.KV_DTYPE_CODE.get(cache.key_cache.dtype)
+        if kv_code is None:
+            raise ValueError(f"cache: unsupported dtype {cache.key_cache.dtype}")
         split = self._split_tokens()
         L = _lib.lib()
         nbytes = _ctypes_size_t()
@@ -221,9 +227,13 @@ class PagedAttention:
         err = rt.err_word(device)
         if rt.CHECK and seq_len and int(ctx[:seq_len].max().item()) > table.shape[1] * cache.block_size:
             raise IndexError("context_lens exceed the block table width")
+        scales = ()
+        if fp8:
+            # e4m3 codes + per-row scales (cache.py); the scaled entry point
+            scales = (cache.key_scale.data_ptr(), cache.value_scale.data_ptr())
         common = (query.data_ptr(), rt.DTYPE_CODE[query.dtype], query.stride(0),
                   query.stride(1), query.stride(2),
-                  cache.key_cache.data_ptr(), cache.value_cache.data_ptr(), kv_code,
+                  cache.key_cache.data_ptr(), cache.value_cache.data_ptr(), kv_code, *scales,
                   cache.num_layers, cache.num_blocks, cache.block_size, cache.num_kv_heads,
                   cache.head_dim, layer,
                   table.data_ptr(), t64, table.shape[1], table.stride(0),
@@ -233,7 +243,8 @@ class PagedAttention:
                 int(phases))
         lse_ptr = lse.data_ptr() if lse is not None else None
         if gather is None:
-            st = L.llmopt_paged_attention_phase(
+            entry = L.llmopt_paged_attention_scaled if fp8 else L.llmopt_paged_attention_phase
+            st = entry(
                 *common, out.data_ptr(), rt.dtype_code(out.dtype, "out"), out.stride(0),
                 out.stride(1), out.stride(2), lse_ptr, *tail)
         else:

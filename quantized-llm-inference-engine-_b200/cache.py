@@ -15,6 +15,14 @@ Differences from the reference, all deliberate:
 * a block id >= ``num_blocks`` reached by ``write`` / ``gather`` is skipped and
   flagged on the device instead of raising (``LLMOPT_B200_CHECK=1`` restores
   the ``IndexError`` at the cost of a sync).
+
+FP8 storage (``dtype=torch.float8_e4m3fn``), beyond the reference (which only
+names the dtype, src/llmopt/utils/misc.py:33-34): ``key_cache`` /
+``value_cache`` hold e4m3 codes in the same layout, and ``key_scale`` /
+``value_scale`` hold one fp32 scale per (token, head) row,
+``[num_layers, num_blocks, num_kv_heads, block_size]``; a value is code *
+scale.  ``write`` / ``write_decode`` quantize each appended row with its own
+scale (amax / 448), and ``gather`` returns the dequantized values in fp32.
 """
 
 from __future__ import annotations
@@ -44,7 +52,8 @@ class PagedKVCache:
             raise ValueError("num_blocks and block_size must be >= 1")
         if num_kv_heads < 1 or head_dim < 1:
             raise ValueError("num_kv_heads and head_dim must be >= 1")
-        rt.dtype_code(dtype, "PagedKVCache")
+        if dtype not in rt.KV_DTYPE_CODE:
+            raise ValueError(f"PagedKVCache: unsupported dtype {dtype}")
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         if dev.type != "cuda":
             raise RuntimeError("PagedKVCache (llmopt_b200) lives in GPU memory: pass a CUDA device")
@@ -60,6 +69,18 @@ class PagedKVCache:
         shape = (num_layers, num_blocks, block_size, num_kv_heads, head_dim)
         self.key_cache = torch.zeros(shape, dtype=dtype, device=dev)
         self.value_cache = torch.zeros_like(self.key_cache)
+        self.key_scale = self.value_scale = None
+        if self.is_fp8:
+            if head_dim > 256:
+                raise ValueError("float8 caches support head_dim <= 256")
+            sshape = (num_layers, num_blocks, num_kv_heads, block_size)
+            self.key_scale = torch.zeros(sshape, dtype=torch.float32, device=dev)
+            self.value_scale = torch.zeros_like(self.key_scale)
+
+    @property
+    def is_fp8(self) -> bool:
+        """e4m3 codes with per-row fp32 scales (``key_scale`` / ``value_scale``)."""
+        return self.dtype == torch.float8_e4m3fn
 
     # -- helpers -----------------------------------------------------------------
     def _layer(self, layer_idx: int) -> int:
@@ -69,8 +90,13 @@ class PagedKVCache:
 
     def _pool_args(self, layer: int):
         return (self.key_cache.data_ptr(), self.value_cache.data_ptr(),
-                rt.DTYPE_CODE[self.dtype], self.num_layers, self.num_blocks, self.block_size,
+                rt.KV_DTYPE_CODE[self.dtype], self.num_layers, self.num_blocks, self.block_size,
                 self.num_kv_heads, self.head_dim, layer)
+
+    def _scaled_pool_args(self, layer: int):
+        """The caches, their dtype and the two scale arrays, then the shape."""
+        base = self._pool_args(layer)
+        return base[:3] + (self.key_scale.data_ptr(), self.value_scale.data_ptr()) + base[3:]
 
     def _check_storage(self) -> None:
         # The public attributes may be reassigned by callers (benchmarks do); the
@@ -78,6 +104,12 @@ class PagedKVCache:
         for t in (self.key_cache, self.value_cache):
             if not t.is_contiguous() or t.dtype != self.dtype or t.device != self.device:
                 raise ValueError("key_cache/value_cache must stay contiguous, with the cache dtype/device")
+        if self.is_fp8:
+            shape = (self.num_layers, self.num_blocks, self.num_kv_heads, self.block_size)
+            for t in (self.key_scale, self.value_scale):
+                if (t is None or not t.is_contiguous() or t.dtype != torch.float32
+                        or t.device != self.device or tuple(t.shape) != shape):
+                    raise ValueError(f"key_scale/value_scale must stay contiguous fp32 {shape}")
 
     def _rows(self, x: torch.Tensor, what: str) -> torch.Tensor:
         """Activations may come from anywhere; the kernels read them on our device."""
@@ -107,11 +139,14 @@ class PagedKVCache:
         table, t64 = rt.index_tensor(block_ids, self.device, "block_ids")
         offs, o64 = rt.index_tensor(token_offsets, self.device, "token_offsets")
         err = rt.err_word(self.device)
-        st = _lib.lib().llmopt_kv_write(
+        L = _lib.lib()
+        fn, pool = ((L.llmopt_kv_write_scaled, self._scaled_pool_args(layer)) if self.is_fp8
+                    else (L.llmopt_kv_write, self._pool_args(layer)))
+        st = fn(
             keys.data_ptr(), values.data_ptr(), rt.DTYPE_CODE[keys.dtype],
             keys.stride(0), keys.stride(1), keys.stride(2),
             values.stride(0), values.stride(1), values.stride(2),
-            *self._pool_args(layer),
+            *pool,
             table.data_ptr(), t64, table.shape[1], table.stride(0),
             offs.data_ptr(), o64, seq_len, q_len, err.data_ptr(), rt.stream_handle(self.device))
         _lib.check(st, "PagedKVCache.write")
@@ -137,10 +172,13 @@ class PagedKVCache:
         if table.shape[0] < seq_len or offs.shape[0] < seq_len:
             raise IndexError("block_ids/token_offsets have fewer rows than keys")
         err = rt.err_word(self.device)
-        st = _lib.lib().llmopt_kv_write_decode(
+        L = _lib.lib()
+        fn, pool = ((L.llmopt_kv_write_decode_scaled, self._scaled_pool_args(layer))
+                    if self.is_fp8 else (L.llmopt_kv_write_decode, self._pool_args(layer)))
+        st = fn(
             keys.data_ptr(), values.data_ptr(), rt.DTYPE_CODE[keys.dtype],
             keys.stride(0), keys.stride(1), values.stride(0), values.stride(1),
-            *self._pool_args(layer),
+            *pool,
             table.data_ptr(), t64, table.shape[1], table.stride(0),
             offs.data_ptr(), o64, seq_len, err.data_ptr(), rt.stream_handle(self.device))
         _lib.check(st, "PagedKVCache.write_decode")
@@ -155,19 +193,23 @@ class PagedKVCache:
         ctx, c64 = rt.index_tensor(context_lens, self.device, "context_lens")
         max_len = int(ctx.max().item()) if seq_len else 0
         head = (self.num_kv_heads, self.head_dim)
+        out_dtype = torch.float32 if self.is_fp8 else self.dtype
         if max_len <= 0:
-            empty = torch.zeros((seq_len, 0, *head), dtype=self.dtype, device=self.device)
+            empty = torch.zeros((seq_len, 0, *head), dtype=out_dtype, device=self.device)
             return empty, empty.clone(), torch.zeros((seq_len, 0), dtype=torch.bool,
                                                      device=self.device)
         table, t64 = rt.index_tensor(block_ids, self.device, "block_ids")
         if max_len > table.shape[1] * self.block_size:
             raise IndexError("context_lens exceed the block table width")
-        keys = torch.empty((seq_len, max_len, *head), dtype=self.dtype, device=self.device)
+        keys = torch.empty((seq_len, max_len, *head), dtype=out_dtype, device=self.device)
         values = torch.empty_like(keys)
         valid = torch.empty((seq_len, max_len), dtype=torch.uint8, device=self.device)
         err = rt.err_word(self.device)
-        st = _lib.lib().llmopt_paged_gather(
-            *self._pool_args(layer), table.data_ptr(), t64, table.shape[1], table.stride(0),
+        L = _lib.lib()
+        fn, pool = ((L.llmopt_paged_gather_scaled, self._scaled_pool_args(layer)) if self.is_fp8
+                    else (L.llmopt_paged_gather, self._pool_args(layer)))
+        st = fn(
+            *pool, table.data_ptr(), t64, table.shape[1], table.stride(0),
             ctx.data_ptr(), c64, seq_len, max_len, keys.data_ptr(), values.data_ptr(),
             valid.data_ptr(), err.data_ptr(), rt.stream_handle(self.device))
         _lib.check(st, "PagedKVCache.gather")
@@ -176,12 +218,18 @@ class PagedKVCache:
         return keys, values, valid.bool()
 
     def memory_bytes(self) -> int:
-        return (self.key_cache.numel() * self.key_cache.element_size()
-                + self.value_cache.numel() * self.value_cache.element_size())
+        n = (self.key_cache.numel() * self.key_cache.element_size()
+             + self.value_cache.numel() * self.value_cache.element_size())
+        if self.is_fp8:
+            n += 4 * (self.key_scale.numel() + self.value_scale.numel())
+        return n
 
     def reset(self) -> None:
         self.key_cache.zero_()
         self.value_cache.zero_()
+        if self.is_fp8:
+            self.key_scale.zero_()
+            self.value_scale.zero_()
 
     def __repr__(self) -> str:
         gib = self.memory_bytes() / float(1 << 30)

@@ -14,6 +14,10 @@
 // z = tile of 16 query rows (the group's heads x q_len).  Each CTA walks its
 // split's keys in tiles of 32 tokens through shared memory, keeps an online
 // softmax per row, and writes a normalised partial + LSE for combine.cu.
+//
+// e4m3 caches: a K/V element is its code's value times the row's fp32 scale
+// (one float product, as the gather's dequantisation), and the query is
+// rounded to f16, the operand precision of the fp8 tensor-core decode.
 #include <float.h>
 
 #include "common.cuh"
@@ -29,7 +33,7 @@ constexpr int KT = kGenericKeyTile;
 size_t generic_smem(int d) {
   return sizeof(float) * ((size_t)RT * d + (size_t)KT * (d + 1) + (size_t)KT * d +
                           (size_t)RT * (KT + 1) + (size_t)RT * d + 3 * RT) +
-         sizeof(long long) * KT + 16;
+         2 * sizeof(long long) * KT + 16;
 }
 
 template <int KV_DT, int Q_DT>
@@ -49,6 +53,9 @@ __global__ void __launch_bounds__(kThreads) attn_generic_kernel(const AttnArgs a
   float* arow = lrow + RT;              // [RT]
   long long* tok_off = reinterpret_cast<long long*>(
       (reinterpret_cast<uintptr_t>(arow + RT) + 7) & ~uintptr_t(7));  // [KT]
+  long long* tok_sidx = tok_off + KT;   // [KT] scale index (e4m3 caches)
+  // The query's rounding: the cache dtype (q.to(k.dtype)), f16 for e4m3.
+  constexpr int QR = KV_DT == kE4M3 ? kF16 : KV_DT;
 
   const long long s = blockIdx.x / a.plan.splits;
   const int j = blockIdx.x - (int)(s * a.plan.splits);
@@ -77,7 +84,7 @@ __global__ void __launch_bounds__(kThreads) attn_generic_kernel(const AttnArgs a
       const int r = r0 + rr;
       const int qi = r / a.group;
       const int qh = kh * a.group + (r - qi * a.group);
-      v = round_through<KV_DT>(
+      v = round_through<QR>(
           load_f32<Q_DT>(a.q, s * a.q_s + (long long)qh * a.q_h + (long long)qi * a.q_t + d));
     }
     Qs[idx] = v;
@@ -94,18 +101,21 @@ __global__ void __launch_bounds__(kThreads) attn_generic_kernel(const AttnArgs a
   for (long long kp0 = tok_lo; kp0 < tok_hi; kp0 += KT) {
     if (tid < KT) {
       const long long pos = kp0 + tid;
-      long long off = -1;
+      long long off = -1, sidx = 0;
       if (pos < tok_hi) {
         const long long col = pos / a.block_size;
         const long long id = load_index(a.table, a.table_i64, s * a.table_stride + col);
         if (id >= 0 && id < a.num_blocks) {
-          off = layer_base + (id * a.block_size + (pos - col * a.block_size)) * row_elems +
-                (long long)kh * D;
+          const long long slot = pos - col * a.block_size;
+          off = layer_base + (id * a.block_size + slot) * row_elems + (long long)kh * D;
+          sidx = (((long long)a.layer * a.num_blocks + id) * a.kv_heads + kh) * a.block_size +
+                 slot;
         } else if (id >= a.num_blocks) {
           record_error(a.err, kErrBlockId);
         }
       }
       tok_off[tid] = off;
+      tok_sidx[tid] = sidx;
     }
     __syncthreads();
     for (int idx = tid; idx < KT * D; idx += kThreads) {
@@ -114,8 +124,14 @@ __global__ void __launch_bounds__(kThreads) attn_generic_kernel(const AttnArgs a
       const long long off = tok_off[t];
       float kv = 0.f, vv = 0.f;
       if (off >= 0) {
-        kv = load_f32<KV_DT>(a.k_cache, off + d);
-        vv = load_f32<KV_DT>(a.v_cache, off + d);
+        if constexpr (KV_DT == kE4M3) {
+          const long long si = tok_sidx[t];
+          kv = e4m3_to_f32(static_cast<const uint8_t*>(a.k_cache)[off + d]) * a.k_scale[si];
+          vv = e4m3_to_f32(static_cast<const uint8_t*>(a.v_cache)[off + d]) * a.v_scale[si];
+        } else {
+          kv = load_f32<KV_DT>(a.k_cache, off + d);
+          vv = load_f32<KV_DT>(a.v_cache, off + d);
+        }
       }
       Ks[t * (D + 1) + d] = kv;
       Vs[t * D + d] = vv;
@@ -205,6 +221,9 @@ const void* select_generic(const AttnArgs& a) {
   LLMOPT_GENERIC_CASE(kBF16, kF32)
   LLMOPT_GENERIC_CASE(kBF16, kF16)
   LLMOPT_GENERIC_CASE(kBF16, kBF16)
+  LLMOPT_GENERIC_CASE(kE4M3, kF32)
+  LLMOPT_GENERIC_CASE(kE4M3, kF16)
+  LLMOPT_GENERIC_CASE(kE4M3, kBF16)
 #undef LLMOPT_GENERIC_CASE
   return nullptr;
 }

@@ -156,19 +156,22 @@ bool kv_tensor_map(const void* base, int dtype, int layers, int num_blocks, int 
     *why = "cuTensorMapEncodeTiled unavailable";
     return false;
   }
-  const cuuint64_t es = 2;
+  // e4m3 codes: one byte per element, boxes of 128 dims (the swizzle span).
+  const bool e4m3 = dtype == kE4M3;
+  const cuuint64_t es = e4m3 ? 1 : 2;
   cuuint64_t dims[5] = {(cuuint64_t)head_dim, (cuuint64_t)kv_heads, (cuuint64_t)block_size,
                         (cuuint64_t)num_blocks, (cuuint64_t)layers};
   cuuint64_t strides[4] = {es * head_dim, es * head_dim * kv_heads,
                            es * head_dim * kv_heads * block_size,
                            es * head_dim * kv_heads * block_size * (cuuint64_t)num_blocks};
-  cuuint32_t box[5] = {64, 1, (cuuint32_t)block_size, 1, 1};
+  cuuint32_t box[5] = {e4m3 ? 128u : 64u, 1, (cuuint32_t)block_size, 1, 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUtensorMap map;
   std::memset(&map, 0, sizeof(map));
   CUresult r = encode(&map,
-                      dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                      e4m3            ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                      : dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                       5, const_cast<void*>(base), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -277,8 +280,9 @@ struct Choice {
 // Pick the kernel and split plan.  Returns LLMOPT_OK or an error code.
 int choose(AttnArgs& a, long long split_tokens, int device, bool encode_maps, Choice* c) {
   const int sms = sm_count_of(device);
+  const bool e4m3 = a.kv_dtype == kE4M3;
   // Dense chunked prefill: tensor-core tiles over whole sequences, no split-K.
-  if (prefill_tc_supported(a)) {
+  if (!e4m3 && prefill_tc_supported(a)) {
     bool maps = true;
     if (encode_maps) {
       std::string why;
@@ -305,7 +309,9 @@ int choose(AttnArgs& a, long long split_tokens, int device, bool encode_maps, Ch
   } else {
     probe.plan = explicit_plan(a.batch, a.table_width, a.block_size, split_tokens);
   }
-  if (decode_tma_supported(probe) && decode_tma_configure(probe, sms, &c->launch)) {
+  const bool fast = e4m3 ? decode_fp8_supported(probe) && decode_fp8_configure(probe, sms, &c->launch)
+                         : decode_tma_supported(probe) && decode_tma_configure(probe, sms, &c->launch);
+  if (fast) {
     bool maps = true;
     if (encode_maps) {
       std::string why;
@@ -438,13 +444,19 @@ int phase_impl(const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h, int
                int32_t out_dtype, int64_t o_s, int64_t o_h, int64_t o_t, float* lse,
                int64_t batch, int32_t num_heads, int32_t q_len, float scale, float softcap,
                int64_t split_tokens, void* workspace, size_t workspace_bytes, uint32_t* err,
-               void* stream, int32_t phases, const PeerArgs* peers) {
+               void* stream, int32_t phases, const PeerArgs* peers,
+               const float* k_scale = nullptr, const float* v_scale = nullptr) {
   if (phases < 1 || phases > LLMOPT_PHASE_ALL) {
     return fail(LLMOPT_ERR_INVALID_ARGUMENT, "phases must be 1, 2 or 3");
   }
-  if (!valid_dtype(q_dtype) || !valid_dtype(kv_dtype) || !valid_dtype(out_dtype)) {
+  // e4m3 caches come with their scales (llmopt_paged_attention_scaled only).
+  const bool kv_ok = k_scale != nullptr ? kv_dtype == kE4M3 : valid_dtype(kv_dtype);
+  if (!valid_dtype(q_dtype) || !kv_ok || !valid_dtype(out_dtype)) {
     return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype (q=%d kv=%d out=%d)", q_dtype,
                 kv_dtype, out_dtype);
+  }
+  if (kv_dtype == kE4M3 && (v_scale == nullptr || head_dim > 256)) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "e4m3 cache needs both scale arrays, head_dim <= 256");
   }
   if (num_heads < 1 || num_kv_heads < 1 || num_heads % num_kv_heads != 0) {
     return fail(LLMOPT_ERR_INVALID_ARGUMENT, "num_heads must be divisible by num_kv_heads");
@@ -482,6 +494,8 @@ int phase_impl(const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h, int
   a.kv_heads = num_kv_heads;
   a.head_dim = head_dim;
   a.layer = layer_idx;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
   a.table = block_table;
   a.table_i64 = table_is_i64 ? 1 : 0;
   a.table_width = table_width;
@@ -524,7 +538,8 @@ int phase_impl(const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (phases & LLMOPT_PHASE_SPLIT) {
     cudaError_t e = c.prefill ? prefill_tc_launch(a, c.tmq, c.tmk, c.tmv, s)
-                    : c.tma   ? decode_tma_launch(a, c.launch, c.tmk, c.tmv, s)
+                    : c.tma   ? (kv_dtype == kE4M3 ? decode_fp8_launch(a, c.launch, c.tmk, c.tmv, s)
+                                                   : decode_tma_launch(a, c.launch, c.tmk, c.tmv, s))
                               : generic_launch(a, s);
     if (e != cudaSuccess) {
       return cuda_fail(e, c.prefill ? "prefill_tc launch"
@@ -563,6 +578,28 @@ int llmopt_paged_attention_phase(const void* query, int32_t q_dtype, int64_t q_s
                     table_is_i64, table_width, table_stride, context_lens, ctx_is_i64, out,
                     out_dtype, o_s, o_h, o_t, lse, batch, num_heads, q_len, scale, softcap,
                     split_tokens, workspace, workspace_bytes, err, stream, phases, nullptr);
+}
+
+int llmopt_paged_attention_scaled(
+    const void* query, int32_t q_dtype, int64_t q_s, int64_t q_h, int64_t q_t,
+    const void* key_cache, const void* value_cache, int32_t kv_dtype, const float* key_scale,
+    const float* value_scale, int32_t num_layers, int32_t num_blocks, int32_t block_size,
+    int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx, const void* block_table,
+    int32_t table_is_i64, int64_t table_width, int64_t table_stride, const void* context_lens,
+    int32_t ctx_is_i64, void* out, int32_t out_dtype, int64_t o_s, int64_t o_h, int64_t o_t,
+    float* lse, int64_t batch, int32_t num_heads, int32_t q_len, float scale, float softcap,
+    int64_t split_tokens, void* workspace, size_t workspace_bytes, uint32_t* err, void* stream,
+    int32_t phases) {
+  if (kv_dtype != kE4M3 || key_scale == nullptr || value_scale == nullptr) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT,
+                "llmopt_paged_attention_scaled takes an e4m3 cache and both scale arrays");
+  }
+  return phase_impl(query, q_dtype, q_s, q_h, q_t, key_cache, value_cache, kv_dtype, num_layers,
+                    num_blocks, block_size, num_kv_heads, head_dim, layer_idx, block_table,
+                    table_is_i64, table_width, table_stride, context_lens, ctx_is_i64, out,
+                    out_dtype, o_s, o_h, o_t, lse, batch, num_heads, q_len, scale, softcap,
+                    split_tokens, workspace, workspace_bytes, err, stream, phases, nullptr,
+                    key_scale, value_scale);
 }
 
 // ---- head-sharded groups: peer memory and the gathered entry -----------------
@@ -737,17 +774,19 @@ static int vector_width(const void* src_k, const void* src_v, int in_dtype, cons
   return 8;
 }
 
-int llmopt_kv_write(const void* keys, const void* values, int32_t in_dtype, int64_t k_s,
-                    int64_t k_t, int64_t k_h, int64_t v_s, int64_t v_t, int64_t v_h,
-                    void* key_cache, void* value_cache, int32_t kv_dtype, int32_t num_layers,
-                    int32_t num_blocks, int32_t block_size, int32_t num_kv_heads,
-                    int32_t head_dim, int32_t layer_idx, const void* block_table,
-                    int32_t table_is_i64, int64_t table_width, int64_t table_stride,
-                    const void* token_offsets, int32_t off_is_i64, int64_t batch, int32_t q_len,
-                    uint32_t* err, void* stream) {
+static int kv_write_impl(const void* keys, const void* values, int32_t in_dtype, int64_t k_s,
+                         int64_t k_t, int64_t k_h, int64_t v_s, int64_t v_t, int64_t v_h,
+                         void* key_cache, void* value_cache, int32_t kv_dtype, float* key_scale,
+                         float* value_scale, int32_t num_layers, int32_t num_blocks,
+                         int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                         int32_t layer_idx, const void* block_table, int32_t table_is_i64,
+                         int64_t table_width, int64_t table_stride, const void* token_offsets,
+                         int32_t off_is_i64, int64_t batch, int32_t q_len, uint32_t* err,
+                         void* stream) {
   if (!valid_dtype(in_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported input dtype");
-  int st = check_cache_args(kv_dtype, num_layers, num_blocks, block_size, num_kv_heads, head_dim,
-                            layer_idx, table_width, table_stride);
+  int st = check_cache_args(kv_dtype == kE4M3 ? kF32 : kv_dtype, num_layers, num_blocks,
+                            block_size, num_kv_heads, head_dim, layer_idx, table_width,
+                            table_stride);
   if (st != LLMOPT_OK) return st;
   if (batch < 0 || q_len < 0) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
   if (batch == 0 || q_len == 0) return ok();
@@ -783,6 +822,8 @@ int llmopt_kv_write(const void* keys, const void* values, int32_t in_dtype, int6
   a.batch = batch;
   a.q_len = q_len;
   a.err = err;
+  a.k_scale = key_scale;
+  a.v_scale = value_scale;
   a.vec = vector_width(keys, values, in_dtype, key_cache, value_cache, head_dim,
                        {k_s, k_t, k_h, v_s, v_t, v_h});
   if (table_width == 0) return ok();  // every walk ends before its first column
@@ -791,17 +832,64 @@ int llmopt_kv_write(const void* keys, const void* values, int32_t in_dtype, int6
   return ok();
 }
 
-int llmopt_kv_write_decode(const void* keys, const void* values, int32_t in_dtype, int64_t k_s,
-                           int64_t k_h, int64_t v_s, int64_t v_h, void* key_cache,
-                           void* value_cache, int32_t kv_dtype, int32_t num_layers,
+// Arguments every e4m3 entry point checks.
+static int check_e4m3(int32_t kv_dtype, const void* key_scale, const void* value_scale,
+                      int32_t head_dim) {
+  if (kv_dtype != kE4M3) return fail(LLMOPT_ERR_UNSUPPORTED, "scaled entry points take e4m3 caches");
+  if (key_scale == nullptr || value_scale == nullptr) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null scale array");
+  }
+  if (head_dim > 256) return fail(LLMOPT_ERR_UNSUPPORTED, "e4m3 caches need head_dim <= 256");
+  return LLMOPT_OK;
+}
+
+int llmopt_kv_write(const void* keys, const void* values, int32_t in_dtype, int64_t k_s,
+                    int64_t k_t, int64_t k_h, int64_t v_s, int64_t v_t, int64_t v_h,
+                    void* key_cache, void* value_cache, int32_t kv_dtype, int32_t num_layers,
+                    int32_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                    int32_t head_dim, int32_t layer_idx, const void* block_table,
+                    int32_t table_is_i64, int64_t table_width, int64_t table_stride,
+                    const void* token_offsets, int32_t off_is_i64, int64_t batch, int32_t q_len,
+                    uint32_t* err, void* stream) {
+  if (!valid_dtype(kv_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported cache dtype");
+  return kv_write_impl(keys, values, in_dtype, k_s, k_t, k_h, v_s, v_t, v_h, key_cache,
+                       value_cache, kv_dtype, nullptr, nullptr, num_layers, num_blocks,
+                       block_size, num_kv_heads, head_dim, layer_idx, block_table, table_is_i64,
+                       table_width, table_stride, token_offsets, off_is_i64, batch, q_len, err,
+                       stream);
+}
+
+int llmopt_kv_write_scaled(const void* keys, const void* values, int32_t in_dtype, int64_t k_s,
+                           int64_t k_t, int64_t k_h, int64_t v_s, int64_t v_t, int64_t v_h,
+                           void* key_cache, void* value_cache, int32_t kv_dtype,
+                           float* key_scale, float* value_scale, int32_t num_layers,
                            int32_t num_blocks, int32_t block_size, int32_t num_kv_heads,
                            int32_t head_dim, int32_t layer_idx, const void* block_table,
                            int32_t table_is_i64, int64_t table_width, int64_t table_stride,
                            const void* token_offsets, int32_t off_is_i64, int64_t batch,
-                           uint32_t* err, void* stream) {
+                           int32_t q_len, uint32_t* err, void* stream) {
+  const int st = check_e4m3(kv_dtype, key_scale, value_scale, head_dim);
+  if (st != LLMOPT_OK) return st;
+  return kv_write_impl(keys, values, in_dtype, k_s, k_t, k_h, v_s, v_t, v_h, key_cache,
+                       value_cache, kv_dtype, key_scale, value_scale, num_layers, num_blocks,
+                       block_size, num_kv_heads, head_dim, layer_idx, block_table, table_is_i64,
+                       table_width, table_stride, token_offsets, off_is_i64, batch, q_len, err,
+                       stream);
+}
+
+static int kv_write_decode_impl(const void* keys, const void* values, int32_t in_dtype,
+                                int64_t k_s, int64_t k_h, int64_t v_s, int64_t v_h,
+                                void* key_cache, void* value_cache, int32_t kv_dtype,
+                                float* key_scale, float* value_scale, int32_t num_layers,
+                                int32_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                                int32_t head_dim, int32_t layer_idx, const void* block_table,
+                                int32_t table_is_i64, int64_t table_width, int64_t table_stride,
+                                const void* token_offsets, int32_t off_is_i64, int64_t batch,
+                                uint32_t* err, void* stream) {
   if (!valid_dtype(in_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported input dtype");
-  int st = check_cache_args(kv_dtype, num_layers, num_blocks, block_size, num_kv_heads, head_dim,
-                            layer_idx, table_width, table_stride);
+  int st = check_cache_args(kv_dtype == kE4M3 ? kF32 : kv_dtype, num_layers, num_blocks,
+                            block_size, num_kv_heads, head_dim, layer_idx, table_width,
+                            table_stride);
   if (st != LLMOPT_OK) return st;
   if (batch < 0) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
   if (batch == 0) return ok();
@@ -837,6 +925,8 @@ int llmopt_kv_write_decode(const void* keys, const void* values, int32_t in_dtyp
   a.batch = batch;
   a.q_len = 1;
   a.err = err;
+  a.k_scale = key_scale;
+  a.v_scale = value_scale;
   a.vec = vector_width(keys, values, in_dtype, key_cache, value_cache, head_dim,
                        {k_s, k_h, v_s, v_h});
   cudaError_t e = kv_write_decode_launch(a, static_cast<cudaStream_t>(stream));
@@ -844,15 +934,52 @@ int llmopt_kv_write_decode(const void* keys, const void* values, int32_t in_dtyp
   return ok();
 }
 
-int llmopt_paged_gather(const void* key_cache, const void* value_cache, int32_t kv_dtype,
-                        int32_t num_layers, int32_t num_blocks, int32_t block_size,
-                        int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
-                        const void* block_table, int32_t table_is_i64, int64_t table_width,
-                        int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
-                        int64_t batch, int64_t max_len, void* out_keys, void* out_values,
-                        uint8_t* valid, uint32_t* err, void* stream) {
-  int st = check_cache_args(kv_dtype, num_layers, num_blocks, block_size, num_kv_heads, head_dim,
-                            layer_idx, table_width, table_stride);
+int llmopt_kv_write_decode(const void* keys, const void* values, int32_t in_dtype, int64_t k_s,
+                           int64_t k_h, int64_t v_s, int64_t v_h, void* key_cache,
+                           void* value_cache, int32_t kv_dtype, int32_t num_layers,
+                           int32_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                           int32_t head_dim, int32_t layer_idx, const void* block_table,
+                           int32_t table_is_i64, int64_t table_width, int64_t table_stride,
+                           const void* token_offsets, int32_t off_is_i64, int64_t batch,
+                           uint32_t* err, void* stream) {
+  if (!valid_dtype(kv_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported cache dtype");
+  return kv_write_decode_impl(keys, values, in_dtype, k_s, k_h, v_s, v_h, key_cache, value_cache,
+                              kv_dtype, nullptr, nullptr, num_layers, num_blocks, block_size,
+                              num_kv_heads, head_dim, layer_idx, block_table, table_is_i64,
+                              table_width, table_stride, token_offsets, off_is_i64, batch, err,
+                              stream);
+}
+
+int llmopt_kv_write_decode_scaled(const void* keys, const void* values, int32_t in_dtype,
+                                  int64_t k_s, int64_t k_h, int64_t v_s, int64_t v_h,
+                                  void* key_cache, void* value_cache, int32_t kv_dtype,
+                                  float* key_scale, float* value_scale, int32_t num_layers,
+                                  int32_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                                  int32_t head_dim, int32_t layer_idx, const void* block_table,
+                                  int32_t table_is_i64, int64_t table_width,
+                                  int64_t table_stride, const void* token_offsets,
+                                  int32_t off_is_i64, int64_t batch, uint32_t* err,
+                                  void* stream) {
+  const int st = check_e4m3(kv_dtype, key_scale, value_scale, head_dim);
+  if (st != LLMOPT_OK) return st;
+  return kv_write_decode_impl(keys, values, in_dtype, k_s, k_h, v_s, v_h, key_cache, value_cache,
+                              kv_dtype, key_scale, value_scale, num_layers, num_blocks,
+                              block_size, num_kv_heads, head_dim, layer_idx, block_table,
+                              table_is_i64, table_width, table_stride, token_offsets, off_is_i64,
+                              batch, err, stream);
+}
+
+static int gather_impl(const void* key_cache, const void* value_cache, int32_t kv_dtype,
+                       const float* key_scale, const float* value_scale, int32_t num_layers,
+                       int32_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                       int32_t head_dim, int32_t layer_idx, const void* block_table,
+                       int32_t table_is_i64, int64_t table_width, int64_t table_stride,
+                       const void* context_lens, int32_t ctx_is_i64, int64_t batch,
+                       int64_t max_len, void* out_keys, void* out_values, uint8_t* valid,
+                       uint32_t* err, void* stream) {
+  int st = check_cache_args(kv_dtype == kE4M3 ? kF32 : kv_dtype, num_layers, num_blocks,
+                            block_size, num_kv_heads, head_dim, layer_idx, table_width,
+                            table_stride);
   if (st != LLMOPT_OK) return st;
   if (batch < 0 || max_len < 0) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape");
   if (batch == 0 || max_len == 0) return ok();
@@ -886,9 +1013,42 @@ int llmopt_paged_gather(const void* key_cache, const void* value_cache, int32_t 
   a.out_v = out_values;
   a.valid = valid;
   a.err = err;
+  a.k_scale = key_scale;
+  a.v_scale = value_scale;
   cudaError_t e = gather_launch(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "gather launch");
   return ok();
+}
+
+int llmopt_paged_gather(const void* key_cache, const void* value_cache, int32_t kv_dtype,
+                        int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                        int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                        const void* block_table, int32_t table_is_i64, int64_t table_width,
+                        int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
+                        int64_t batch, int64_t max_len, void* out_keys, void* out_values,
+                        uint8_t* valid, uint32_t* err, void* stream) {
+  if (!valid_dtype(kv_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported cache dtype");
+  return gather_impl(key_cache, value_cache, kv_dtype, nullptr, nullptr, num_layers, num_blocks,
+                     block_size, num_kv_heads, head_dim, layer_idx, block_table, table_is_i64,
+                     table_width, table_stride, context_lens, ctx_is_i64, batch, max_len,
+                     out_keys, out_values, valid, err, stream);
+}
+
+int llmopt_paged_gather_scaled(const void* key_cache, const void* value_cache, int32_t kv_dtype,
+                               const float* key_scale, const float* value_scale,
+                               int32_t num_layers, int32_t num_blocks, int32_t block_size,
+                               int32_t num_kv_heads, int32_t head_dim, int32_t layer_idx,
+                               const void* block_table, int32_t table_is_i64,
+                               int64_t table_width, int64_t table_stride,
+                               const void* context_lens, int32_t ctx_is_i64, int64_t batch,
+                               int64_t max_len, float* out_keys, float* out_values,
+                               uint8_t* valid, uint32_t* err, void* stream) {
+  const int st = check_e4m3(kv_dtype, key_scale, value_scale, head_dim);
+  if (st != LLMOPT_OK) return st;
+  return gather_impl(key_cache, value_cache, kv_dtype, key_scale, value_scale, num_layers,
+                     num_blocks, block_size, num_kv_heads, head_dim, layer_idx, block_table,
+                     table_is_i64, table_width, table_stride, context_lens, ctx_is_i64, batch,
+                     max_len, out_keys, out_values, valid, err, stream);
 }
 
 }  // extern "C"

@@ -10,12 +10,18 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace llmopt {
 
-enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
+// kE4M3: float8_e4m3fn KV storage with one fp32 scale per (token, head) row
+// (value = e4m3 * scale); caches only.
+enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2, kE4M3 = 3 };
+
+// Largest finite e4m3 magnitude: a row's scale maps its amax onto it.
+constexpr float kE4M3Max = 448.f;
 
 constexpr unsigned kErrBlockId = 1u;
 constexpr unsigned kErrTableWidth = 2u;
@@ -96,6 +102,33 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+}
+
+// ---- float8 e4m3 (cuda_fp8.h conversions, hardware cvt on sm_100a) --------
+// Two e4m3 bytes (low byte first) -> two f16 in one register; exact, since every
+// e4m3 value is an f16 value.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)pair, __NV_E4M3);
+  return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// Round-to-nearest-even to e4m3, saturating to +-448 (NaN stays NaN).  The
+// inputs here are already scaled into [-448, 448] (up to one rounding step),
+// where this equals torch's non-saturating .to(torch.float8_e4m3fn).
+__device__ __forceinline__ uint8_t f32_to_e4m3(float x) {
+  return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+
+// Scale of a row with largest magnitude amax: amax / 448, or 1 when that is
+// not a positive number (an all-zero row, underflow, NaN).
+__device__ __forceinline__ float e4m3_row_scale(float amax) {
+  const float s = __fdiv_rn(amax, kE4M3Max);
+  return s > 0.f ? s : 1.f;
 }
 
 __device__ __forceinline__ long long load_index(const void* p, int is64, long long i) {

@@ -28,6 +28,9 @@ struct AttnArgs {
   const void* v_cache;
   int kv_dtype;
   int num_layers, num_blocks, block_size, kv_heads, head_dim, layer;
+  // kE4M3 caches: fp32 scale per (token, head) row, [layers, num_blocks, kv_heads, block_size]
+  const float* k_scale;
+  const float* v_scale;
   // block table / context
   const void* table;
   int table_i64;
@@ -64,6 +67,14 @@ bool decode_tma_supported(const AttnArgs& a);
 // Fills `launch` (occupancy, smem) for this shape; false if it cannot run here.
 bool decode_tma_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch);
 cudaError_t decode_tma_launch(const AttnArgs& a, const DecodeLaunch& launch,
+                              const CUtensorMap& tmk, const CUtensorMap& tmv,
+                              cudaStream_t stream);
+
+// The same split-K decode over an e4m3 cache (decode_fp8.cu): TMA-staged code
+// blocks and scales, dequantised in registers into f16 m16n8k16 tiles.
+bool decode_fp8_supported(const AttnArgs& a);
+bool decode_fp8_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch);
+cudaError_t decode_fp8_launch(const AttnArgs& a, const DecodeLaunch& launch,
                               const CUtensorMap& tmk, const CUtensorMap& tmv,
                               cudaStream_t stream);
 
@@ -119,6 +130,8 @@ struct KvWriteArgs {
   void* v_cache;
   int kv_dtype;
   int num_layers, num_blocks, block_size, kv_heads, head_dim, layer;
+  float* k_scale;  // kE4M3: [layers, num_blocks, kv_heads, block_size]
+  float* v_scale;
   const void* table;
   int table_i64;
   long long table_width, table_stride;
@@ -187,6 +200,8 @@ struct GatherArgs {
   const void* v_cache;
   int kv_dtype;
   int num_layers, num_blocks, block_size, kv_heads, head_dim, layer;
+  const float* k_scale;  // kE4M3: outputs are dequantised fp32
+  const float* v_scale;
   const void* table;
   int table_i64;
   long long table_width, table_stride;

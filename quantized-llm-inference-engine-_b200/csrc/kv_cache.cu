@@ -91,6 +91,53 @@ __device__ __forceinline__ void copy_row(const void* src, long long sbase, long 
   }
 }
 
+// Quantize one token row [kv_heads, head_dim] (head_dim <= 256) to e4m3 by one
+// warp: per head, amax over the row (NaN ignored), scale = amax / 448 (1 if
+// that is not positive), code = e4m3(x / scale) with both steps rounded to
+// nearest.  `scale_idx` is head 0's scale; heads are block_size apart.
+template <int IN_DT>
+__device__ __forceinline__ void quantize_row(const void* src, long long sbase, long long sh,
+                                             uint8_t* dst, long long dbase, float* scales,
+                                             long long scale_idx, long long scale_step, int kvh,
+                                             int d, int lane) {
+  for (int h = 0; h < kvh; ++h) {
+    float x[8];
+    float amax = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int e = lane + 32 * k;
+      x[k] = e < d ? load_f32<IN_DT>(src, sbase + (long long)h * sh + e) : 0.f;
+      amax = fmaxf(amax, fabsf(x[k]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = e4m3_row_scale(amax);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int e = lane + 32 * k;
+      if (e < d) dst[dbase + (long long)h * d + e] = f32_to_e4m3(__fdiv_rn(x[k], scale));
+    }
+    if (lane == 0) scales[scale_idx + (long long)h * scale_step] = scale;
+  }
+}
+
+// Append one token row of K or V: cast copy, or e4m3 quantization with scales.
+template <int IN_DT, int OUT_DT>
+__device__ __forceinline__ void append_row(const KvWriteArgs& a, const void* src, long long sbase,
+                                           long long sh, void* cache, float* scales,
+                                           long long id, long long slot, int lane) {
+  const long long row_elems = (long long)a.kv_heads * a.head_dim;
+  const long long bs = a.block_size;
+  const long long blk = (long long)a.layer * a.num_blocks + id;
+  if constexpr (OUT_DT == kE4M3) {
+    quantize_row<IN_DT>(src, sbase, sh, static_cast<uint8_t*>(cache), (blk * bs + slot) * row_elems,
+                        scales, blk * a.kv_heads * bs + slot, bs, a.kv_heads, a.head_dim, lane);
+  } else {
+    copy_row<IN_DT, OUT_DT>(src, sbase, sh, cache, (blk * bs + slot) * row_elems, a.kv_heads,
+                            a.head_dim, a.vec, lane);
+  }
+}
+
 // write(): grid (batch, ceil(q_len / kWriteRowsPerCta)).
 template <int IN_DT, int OUT_DT>
 __global__ void __launch_bounds__(kThreads) kv_write_kernel(const KvWriteArgs a) {
@@ -139,7 +186,6 @@ __global__ void __launch_bounds__(kThreads) kv_write_kernel(const KvWriteArgs a)
     if (reason == 2) record_error(a.err, kErrTableWidth);
   }
 
-  const long long row_elems = (long long)a.kv_heads * a.head_dim;
   const int t0 = blockIdx.y * kWriteRowsPerCta;
   const int t1 = t0 + kWriteRowsPerCta < a.q_len ? t0 + kWriteRowsPerCta : a.q_len;
   for (int i = t0 + warp; i < t1; i += kWarps) {
@@ -148,11 +194,10 @@ __global__ void __launch_bounds__(kThreads) kv_write_kernel(const KvWriteArgs a)
     if (c >= stop_col) continue;
     const long long id = load_index(a.table, a.table_i64, s * a.table_stride + (c < 0 ? c + W : c));
     const long long slot = floormod(pos, bs);
-    const long long dst = (((long long)a.layer * a.num_blocks + id) * bs + slot) * row_elems;
-    copy_row<IN_DT, OUT_DT>(a.keys, s * a.k_s + (long long)i * a.k_t, a.k_h, a.k_cache, dst,
-                            a.kv_heads, a.head_dim, a.vec, lane);
-    copy_row<IN_DT, OUT_DT>(a.values, s * a.v_s + (long long)i * a.v_t, a.v_h, a.v_cache, dst,
-                            a.kv_heads, a.head_dim, a.vec, lane);
+    append_row<IN_DT, OUT_DT>(a, a.keys, s * a.k_s + (long long)i * a.k_t, a.k_h, a.k_cache,
+                              a.k_scale, id, slot, lane);
+    append_row<IN_DT, OUT_DT>(a, a.values, s * a.v_s + (long long)i * a.v_t, a.v_h, a.v_cache,
+                              a.v_scale, id, slot, lane);
   }
 }
 
@@ -175,14 +220,11 @@ __global__ void __launch_bounds__(64) kv_write_decode_kernel(const KvWriteArgs a
   long long id = load_index(a.table, a.table_i64, s * a.table_stride + (col < 0 ? col + W : col));
   if (id < 0 || id >= a.num_blocks) id = 0;         // paged_cache.py:257-259
   const long long slot = floormod(off, bs);         // paged_cache.py:253
-  const long long row_elems = (long long)a.kv_heads * a.head_dim;
-  const long long dst = (((long long)a.layer * a.num_blocks + id) * bs + slot) * row_elems;
   if (warp == 0) {
-    copy_row<IN_DT, OUT_DT>(a.keys, s * a.k_s, a.k_h, a.k_cache, dst, a.kv_heads, a.head_dim,
-                            a.vec, lane);
+    append_row<IN_DT, OUT_DT>(a, a.keys, s * a.k_s, a.k_h, a.k_cache, a.k_scale, id, slot, lane);
   } else {
-    copy_row<IN_DT, OUT_DT>(a.values, s * a.v_s, a.v_h, a.v_cache, dst, a.kv_heads, a.head_dim,
-                            a.vec, lane);
+    append_row<IN_DT, OUT_DT>(a, a.values, s * a.v_s, a.v_h, a.v_cache, a.v_scale, id, slot,
+                              lane);
   }
 }
 
@@ -240,6 +282,49 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(const GatherArgs a, in
   }
 }
 
+// gather() of an e4m3 cache: the padded rows come out dequantised to fp32
+// (code value * row scale, one rounding), zero where invalid.
+__global__ void __launch_bounds__(kThreads) gather_e4m3_kernel(const GatherArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const long long s = blockIdx.x;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long bs = a.block_size;
+  const long long ctx_s = load_index(a.ctx, a.ctx_i64, s);
+  const long long row_elems = (long long)a.kv_heads * a.head_dim;
+  const long long t0 = (long long)blockIdx.y * kRowsPerCta;
+  const long long t1 = t0 + kRowsPerCta < a.max_len ? t0 + kRowsPerCta : a.max_len;
+  const uint8_t* kc = static_cast<const uint8_t*>(a.k_cache);
+  const uint8_t* vc = static_cast<const uint8_t*>(a.v_cache);
+  float* ok_ = static_cast<float*>(a.out_k);
+  float* ov = static_cast<float*>(a.out_v);
+  for (long long t = t0 + warp; t < t1; t += kWarps) {
+    const long long col = t / bs;                   // paged_cache.py:289 (< width, host-checked)
+    const long long id = load_index(a.table, a.table_i64, s * a.table_stride + col);
+    bool ok = id >= 0 && t < ctx_s;                 // paged_cache.py:293-295
+    if (id >= a.num_blocks) {
+      if (lane == 0) record_error(a.err, kErrBlockId);
+      ok = false;
+    }
+    const long long slot = t - col * bs;
+    const long long blk = ok ? (long long)a.layer * a.num_blocks + id : 0;
+    const long long src = (blk * bs + slot) * row_elems;
+    const long long dst = (s * a.max_len + t) * row_elems;
+    if (lane == 0) a.valid[s * a.max_len + t] = ok ? 1 : 0;
+    for (long long e = lane; e < row_elems; e += 32) {
+      float kx = 0.f, vx = 0.f;
+      if (ok) {
+        const long long sidx = (blk * a.kv_heads + e / a.head_dim) * bs + slot;
+        kx = e4m3_to_f32(kc[src + e]) * a.k_scale[sidx];
+        vx = e4m3_to_f32(vc[src + e]) * a.v_scale[sidx];
+      }
+      ok_[dst + e] = kx;
+      ov[dst + e] = vx;
+    }
+  }
+}
+
 template <int IN_DT, int OUT_DT>
 const void* write_ptr(bool decode) {
   return decode ? reinterpret_cast<const void*>(&kv_write_decode_kernel<IN_DT, OUT_DT>)
@@ -258,6 +343,9 @@ const void* select_write(int in_dt, int out_dt, bool decode) {
   LLMOPT_WRITE_CASE(kBF16, kF32)
   LLMOPT_WRITE_CASE(kBF16, kF16)
   LLMOPT_WRITE_CASE(kBF16, kBF16)
+  LLMOPT_WRITE_CASE(kF32, kE4M3)
+  LLMOPT_WRITE_CASE(kF16, kE4M3)
+  LLMOPT_WRITE_CASE(kBF16, kE4M3)
 #undef LLMOPT_WRITE_CASE
   return nullptr;
 }
@@ -288,6 +376,11 @@ cudaError_t gather_launch(const GatherArgs& a, cudaStream_t stream) {
   if (a.batch <= 0 || a.max_len <= 0) return cudaSuccess;
   const long long gy = (a.max_len + kRowsPerCta - 1) / kRowsPerCta;
   if (a.batch > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidConfiguration;
+  if (a.kv_dtype == kE4M3) {
+    void* args[] = {const_cast<GatherArgs*>(&a)};
+    return launch_pdl(reinterpret_cast<const void*>(&gather_e4m3_kernel),
+                      dim3((unsigned)a.batch, (unsigned)gy), dim3(kThreads), args, 0, stream);
+  }
   const int esize = a.kv_dtype == kF32 ? 4 : 2;
   const long long row_bytes = (long long)a.kv_heads * a.head_dim * esize;
   int vec = (row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(a.k_cache) & 15) == 0 &&

@@ -75,6 +75,9 @@ def rope_kv_append(q_proj: torch.Tensor, k_proj: torch.Tensor, v_proj: torch.Ten
     if q_len < 1:
         raise ValueError("q_len must be >= 1")
     rt.require_cuda(cache.key_cache, "cache")
+    if getattr(cache, "is_fp8", False):
+        raise ValueError("rope_kv_append writes 16-bit or fp32 caches; for an e4m3 cache rotate "
+                         "q/k and append with cache.write / cache.write_decode")
     device = cache.device
     total = q_proj.shape[0]
     if total % q_len:
