@@ -112,6 +112,18 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
   return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 
+// Four e4m3 bytes -> two f16 pairs: bytes (0, 1) into lo, (2, 3) into hi.  The
+// word is split into its 16-bit halves in PTX so each conversion reads a half
+// register directly.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\t"
+      "mov.b32 {l, h}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+
 __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
   const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
   return __half2float(__half(h));

@@ -18,21 +18,26 @@
 // bulk copy each for the K and V scales of the CTA's heads (contiguous in the
 // [.., kv_heads, block_size] scale layout).
 //
-// Math: m16n8k16 f16 MMAs with fp32 accumulation.  e4m3 -> f16 is exact, so the
-// only roundings beyond the fp32 reference are the query's (to f16) and the
-// probabilities' (to f16).  Fragments are read from shared memory with 16-byte
+// Math: m16n8k16 f16 MMAs with fp32 accumulation, transposed against the
+// bf16 kernel: the 16 tokens of a block are the M dimension and the query
+// rows of the KV head (q_len * group, 4 for Llama-3 decode) the N dimension,
+// 8 per n-tile, so a block costs D/16 MMAs for S and D/16 for O instead of
+// twice that with rows padded to 16.  e4m3 -> f16 is exact, so the only
+// roundings beyond the fp32 reference are the query's (to f16) and the
+// probabilities' (to f16).  Fragments come from shared memory in 16-byte
 // loads that hit eight different bank groups per quarter warp:
-// * S = Q K^T: lane (g, t) of n-tile n reads token 8n + g, dims 32t..32t+31
-//   of each slice; k-step (slice u, word w) uses dims 128u + 32t + 4w .. +3,
+// * S^T = K Q^T: lane (g, t) reads tokens g and g + 8, dims 32t..32t+31 of
+//   each 128-dim slice; k-step (slice u, word w) uses dims 128u + 32t + 4w .. +3
 //   and the query fragments follow the same dim order (a dot product does not
-//   care which k-slot holds which dim).  The row's K scale multiplies the
+//   care which k-slot holds which dim).  The token's K scale multiplies the
 //   fp32 scores.
-// * O += P V: lane (g, t) reads tokens 2t, 2t+1, 2t+8, 2t+9, dims 16g..16g+15
-//   of each slice, and byte-permutes token pairs of one dim into the B
-//   fragment; n-tile 16u + j of slice u is dim 128u + 16n' + j for n-slot n',
-//   so each lane's output dims are 32 contiguous values per slice.  The V
-//   scales are folded into the probabilities before the f16 cast; the row sums
-//   use the unscaled probabilities.
+// * O^T += V^T P^T: lane (g, t) reads tokens 2t, 2t+1, 2t+8, 2t+9, dims
+//   16g..16g+15 of each slice, and byte-permutes token pairs of one dim into
+//   the A fragment: m-slots g and g + 8 of m-tile j of slice u are dims
+//   128u + 16g + 2j and + 1, so each lane ends with 16 contiguous output dims
+//   of its two query rows per slice.  The V scales multiply the probabilities
+//   before the f16 cast (the row sums use the unscaled ones), and
+//   movmatrix.trans turns the S^T accumulator layout into the B fragments.
 // Partials (normalised O, natural-log LSE) go to the split workspace in the
 // bf16 kernel's format; combine.cu merges them.
 #include <float.h>
@@ -90,14 +95,15 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
-// Query fragments for S = Q K^T in the kernel's dim order: k-step ks = 8u + w
-// covers dims 128u + 32t + 4w + {0,1} (a0/a1) and {2,3} (a2/a3).
-template <int D, int Q_DT>
-__device__ __forceinline__ void load_q_frags(const AttnArgs& a, long long s, int kh, int gid,
-                                             int tid4, uint32_t (&qa)[D / 16][4]) {
+// Query fragments (the B operand of S^T = K Q^T) in the kernel's dim order:
+// n-tile nt holds query rows 8nt..8nt+7 (row 8nt + g in lane g); k-step
+// ks = 8u + w covers dims 128u + 32t + 4w + {0,1} (b0) and {2,3} (b1).
+template <int D, int Q_DT, int NT>
+__device__ __forceinline__ void load_qt_frags(const AttnArgs& a, long long s, int kh, int gid,
+                                              int tid4, uint32_t (&qb)[NT][D / 16][2]) {
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const int r = gid + 8 * half;
+  for (int nt = 0; nt < NT; ++nt) {
+    const int r = 8 * nt + gid;
     const bool ok = r < a.rows;
     long long base = 0;
     if (ok) {
@@ -115,19 +121,36 @@ __device__ __forceinline__ void load_q_frags(const AttnArgs& a, long long s, int
           x0 = load_f32<Q_DT>(a.q, base + d + 2 * pr);
           x1 = load_f32<Q_DT>(a.q, base + d + 2 * pr + 1);
         }
-        qa[ks][half + 2 * pr] = pack2<kF16>(x0, x1);
+        qb[nt][ks][pr] = pack2<kF16>(x0, x1);
       }
     }
   }
 }
 
-template <int D, int Q_DT>
-__global__ void __launch_bounds__((max_heads(D) + 1) * 32, 1)
+// Transpose an 8x8 matrix of 16-bit pairs held in the MMA fragment layout
+// (lane holds row lane/4, columns 2(lane%4) and +1) across the warp.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// Register cap per thread.  One n-tile at head_dim 128 fits 112 registers
+// without spilling (128 with the self-issue state): 16 one-warp CTAs, or
+// three of the default 5-warp CTAs, per SM.
+constexpr int reg_cap(int d, int nt, bool sp) {
+  return d == 256 ? 255 : (nt == 1 ? (sp ? 128 : 112) : 168);
+}
+
+template <int D, int Q_DT, int NT, bool SP>
+__global__ void __launch_bounds__(SP ? 32 : (max_heads(D) + 1) * 32) __maxnreg__(reg_cap(D, NT, SP))
     decode_fp8_kernel(const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const AttnArgs a, const int hpc,
                       const int nstages) {
+  // Dependent-launch trigger as the bf16 kernel: at the start with a producer
+  // warp, at the end for self-issuing one-warp CTAs.
   griddep_wait();
-  griddep_launch_dependents();
+  if (!SP) griddep_launch_dependents();
   constexpr int kSlices = D / kSlice;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -214,36 +237,67 @@ __global__ void __launch_bounds__((max_heads(D) + 1) * 32, 1)
   const int kh0 = blockIdx.y * hpc;
   const long long total = hi - lo;
 
+  // Block `idx` of this CTA's range: its table entry and valid-token count
+  // (ntok 0: not loaded).
+  auto resolve = [&](long long idx, int* id, int* ntok) {
+    *id = 0;
+    *ntok = 0;
+    if (idx >= total) return;
+    const long long f = lo + idx;
+    long long s, j;
+    if (balanced) {
+      s = find_seq(sm.prefix, batch, f);
+      j = f - sm.prefix[s];
+    } else {
+      s = fixed_seq;
+      j = f;
+    }
+    const long long c = load_index(a.ctx, a.ctx_i64, s);
+    const long long raw = load_index(a.table, a.table_i64, s * a.table_stride + j);
+    const long long left = c - j * kBS;
+    if (raw >= a.num_blocks) {
+      record_error(a.err, kErrBlockId);
+    } else if (raw >= 0) {
+      *id = (int)raw;
+      *ntok = left < kBS ? (int)left : kBS;
+    }
+  };
+  // Stage st <- block id (codes of the CTA's heads and their scales); one thread.
+  auto fill_stage = [&](int st, int id_i, int nt_i) {
+    sm.meta[st] = nt_i;
+    if (nt_i > 0) {
+      unsigned char* kdst = sm.stages + (size_t)st * stage_bytes;
+      unsigned char* vdst = kdst + half_bytes;
+      float* sdst = sm.scales + (size_t)st * 2 * scale_floats;
+      mbar_arrive_expect_tx(&sm.full[st],
+                            (unsigned)(stage_bytes + 2 * scale_floats * sizeof(float)));
+#pragma unroll
+      for (int sl = 0; sl < kSlices; ++sl) {
+        for (int h = 0; h < hpc; ++h) {
+          const int off = sl * slice_bytes + h * kBS * kSlice;
+          tma_load_5d(kdst + off, &tmk, &sm.full[st], sl * kSlice, kh0 + h, 0, id_i, a.layer);
+          tma_load_5d(vdst + off, &tmv, &sm.full[st], sl * kSlice, kh0 + h, 0, id_i, a.layer);
+        }
+      }
+      const long long sidx = (((long long)a.layer * a.num_blocks + id_i) * a.kv_heads + kh0) * kBS;
+      bulk_load(sdst, a.k_scale + sidx, (unsigned)(scale_floats * sizeof(float)), &sm.full[st]);
+      bulk_load(sdst + scale_floats, a.v_scale + sidx, (unsigned)(scale_floats * sizeof(float)),
+                &sm.full[st]);
+    } else {
+      mbar_arrive(&sm.full[st]);
+    }
+  };
+
   // ---- producer warp ------------------------------------------------------------
-  if (warp == hpc) {
+  if (!SP && warp == hpc) {
     if (lane == 0) {
       prefetch_tensormap(&tmk);
       prefetch_tensormap(&tmv);
     }
     for (long long base = 0; base < total; base += 32) {
       // Each lane resolves one block: its table entry and valid-token count.
-      int id = 0, ntok = 0;
-      const long long idx = base + lane;
-      if (idx < total) {
-        const long long f = lo + idx;
-        long long s, j;
-        if (balanced) {
-          s = find_seq(sm.prefix, batch, f);
-          j = f - sm.prefix[s];
-        } else {
-          s = fixed_seq;
-          j = f;
-        }
-        const long long c = load_index(a.ctx, a.ctx_i64, s);
-        const long long raw = load_index(a.table, a.table_i64, s * a.table_stride + j);
-        const long long left = c - j * kBS;
-        if (raw >= a.num_blocks) {
-          record_error(a.err, kErrBlockId);
-        } else if (raw >= 0) {
-          id = (int)raw;
-          ntok = left < kBS ? (int)left : kBS;
-        }
-      }
+      int id, ntok;
+      resolve(base + lane, &id, &ntok);
       const int cnt = total - base < 32 ? (int)(total - base) : 32;
       for (int i = 0; i < cnt; ++i) {
         const int id_i = __shfl_sync(0xffffffffu, id, i);
@@ -255,32 +309,7 @@ __global__ void __launch_bounds__((max_heads(D) + 1) * 32, 1)
           if (round > 0 && !mbar_wait(&sm.empty[st], (unsigned)((round - 1) & 1))) {
             record_error(a.err, kErrWaitTimeout | kErrWaitSlot);
           }
-          sm.meta[st] = nt_i;
-          if (nt_i > 0) {
-            unsigned char* kdst = sm.stages + (size_t)st * stage_bytes;
-            unsigned char* vdst = kdst + half_bytes;
-            float* sdst = sm.scales + (size_t)st * 2 * scale_floats;
-            mbar_arrive_expect_tx(&sm.full[st],
-                                  (unsigned)(stage_bytes + 2 * scale_floats * sizeof(float)));
-#pragma unroll
-            for (int sl = 0; sl < kSlices; ++sl) {
-              for (int hh = 0; hh < hpc; ++hh) {
-                const int off = sl * slice_bytes + hh * kBS * kSlice;
-                tma_load_5d(kdst + off, &tmk, &sm.full[st], sl * kSlice, kh0 + hh, 0, id_i,
-                            a.layer);
-                tma_load_5d(vdst + off, &tmv, &sm.full[st], sl * kSlice, kh0 + hh, 0, id_i,
-                            a.layer);
-              }
-            }
-            const long long sidx =
-                (((long long)a.layer * a.num_blocks + id_i) * a.kv_heads + kh0) * kBS;
-            bulk_load(sdst, a.k_scale + sidx, (unsigned)(scale_floats * sizeof(float)),
-                      &sm.full[st]);
-            bulk_load(sdst + scale_floats, a.v_scale + sidx,
-                      (unsigned)(scale_floats * sizeof(float)), &sm.full[st]);
-          } else {
-            mbar_arrive(&sm.full[st]);
-          }
+          fill_stage(st, id_i, nt_i);
         }
         __syncwarp();
       }
@@ -298,12 +327,45 @@ __global__ void __launch_bounds__((max_heads(D) + 1) * 32, 1)
   }
 
   // ---- consumer warps: one KV head each ----------------------------------------
+  constexpr int KS = D / 16;   // k-steps of S^T = m-tiles of O^T
   const int hh = warp;
   const int kh = kh0 + hh;
   const int gid = lane >> 2;
   const int tid4 = lane & 3;
   const float scale_log2 = a.scale * kLog2e;
   const bool capped = a.softcap > 0.f;
+
+  // Self-issuing: blocks [0, issued) have been issued; lane l caches the table
+  // entry of block cache_base + l.  Every issued block is consumed (waited on)
+  // before the warp exits, so no copy is in flight when it returns.
+  long long issued = 0;
+  long long cache_base = -32;
+  int c_id = 0, c_nt = 0;
+  auto issue_upto = [&](long long limit) {
+    if (limit > total) limit = total;
+    while (issued < limit) {
+      if (issued >= cache_base + 32) {
+        cache_base = issued;
+        resolve(cache_base + lane, &c_id, &c_nt);
+      }
+      const int k = (int)(issued - cache_base);
+      const int id_i = __shfl_sync(0xffffffffu, c_id, k);
+      const int nt_i = __shfl_sync(0xffffffffu, c_nt, k);
+      // The stage's previous block has been read (and its V rows maybe zeroed)
+      // by this warp: order those accesses before the copies that overwrite it.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (lane == 0) fill_stage((int)(issued % nstages), id_i, nt_i);
+      __syncwarp();
+      ++issued;
+    }
+  };
+  if (SP) {
+    if (lane == 0) {
+      prefetch_tensormap(&tmk);
+      prefetch_tensormap(&tmv);
+    }
+    issue_upto(nstages);
+  }
 
   long long it = 0;
   long long cur = lo;
@@ -319,17 +381,31 @@ __global__ void __launch_bounds__((max_heads(D) + 1) * 32, 1)
       seg_end = hi;
     }
     const long long ctx_s = load_index(a.ctx, a.ctx_i64, s);
-    uint32_t qa[D / 16][4];
-    load_q_frags<D, Q_DT>(a, s, kh, gid, tid4, qa);
-    const long long qpos0 = ctx_s - a.q_len + (gid / a.group);
-    const long long qpos1 = ctx_s - a.q_len + ((gid + 8) / a.group);
-
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float o[D / 8][4];
+    uint32_t qb[NT][KS][2];
+    load_qt_frags<D, Q_DT, NT>(a, s, kh, gid, tid4, qb);
+    // Causal limit of this lane's rows 8nt + 2t + j (only used when q_len > 1).
+    long long qpos[NT][2];
 #pragma unroll
-    for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        qpos[nt][j] = ctx_s - a.q_len + (8 * nt + 2 * tid4 + j) / a.group;
+      }
+    }
+
+    float m[NT][2], l[NT][2];
+    float o[NT][KS][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      m[nt][0] = m[nt][1] = -INFINITY;
+      l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
+    }
 
     for (long long f = cur; f < seg_end; ++f, ++it) {
+      // Self-issuing: keep nstages - 1 blocks in flight beyond this one.
+      if (SP) issue_upto(it + nstages);
       const int st = (int)(it % nstages);
       if (!mbar_wait(&sm.full[st], (unsigned)((it / nstages) & 1))) {
         record_error(a.err, kErrWaitTimeout | kErrWaitData);
@@ -354,91 +430,78 @@ __global__ void __launch_bounds__((max_heads(D) + 1) * 32, 1)
           __syncwarp();
         }
 
-        // S = Q K^T: two n-tiles of 8 tokens
-        float sacc[2][4];
+        // S^T = K Q^T: tokens g and g + 8 (A) against the query rows (B)
+        float sacc[NT][4];
 #pragma unroll
-        for (int n = 0; n < 2; ++n) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+        for (int nt = 0; nt < NT; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
 #pragma unroll
         for (int sl = 0; sl < kSlices; ++sl) {
           uint4 kv[2][2];
 #pragma unroll
-          for (int n = 0; n < 2; ++n) {
-            const int t = n * 8 + gid;
+          for (int hl = 0; hl < 2; ++hl) {
+            const int t = gid + 8 * hl;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-              kv[n][c] = lds128(kst + sl * slice_bytes + t * kSlice +
-                                (((2 * tid4 + c) ^ (t & 7)) << 4));
+              kv[hl][c] = lds128(kst + sl * slice_bytes + t * kSlice +
+                                 (((2 * tid4 + c) ^ (t & 7)) << 4));
             }
           }
 #pragma unroll
           for (int w = 0; w < 8; ++w) {
+            uint32_t af[4];   // token g dims +0,+1 | token g+8 | token g dims +2,+3 | token g+8
+            e4m3x4_to_f16x2x2(word_of(kv[0][w >> 2], w & 3), af[0], af[2]);
+            e4m3x4_to_f16x2x2(word_of(kv[1][w >> 2], w & 3), af[1], af[3]);
 #pragma unroll
-            for (int n = 0; n < 2; ++n) {
-              const uint32_t word = word_of(kv[n][w >> 2], w & 3);
-              mma_16816<kF16>(sacc[n], qa[sl * 8 + w], e4m3x2_to_f16x2(word & 0xFFFFu),
-                              e4m3x2_to_f16x2(word >> 16));
+            for (int nt = 0; nt < NT; ++nt) {
+              mma_16816<kF16>(sacc[nt], af, qb[nt][sl * 8 + w][0], qb[nt][sl * 8 + w][1]);
             }
           }
         }
 
-        // K scale, softmax scale / softcap, mask (log2 units)
+        // K scale, softmax scale / softcap, mask (log2 units); element e of
+        // n-tile nt: token g + 8 (e >> 1), query row 8nt + 2t + (e & 1)
         const long long kbase = (f - seg_begin) * kBS;
-        float sc[2][4];
+        const float ksc[2] = {kscale[gid], kscale[gid + 8]};
+        const float vsc[2] = {vscale[gid], vscale[gid + 8]};
+        uint32_t pb[NT][2];
 #pragma unroll
-        for (int n = 0; n < 2; ++n) {
-          const float2 ksc = *reinterpret_cast<const float2*>(kscale + n * 8 + 2 * tid4);
+        for (int nt = 0; nt < NT; ++nt) {
+          float p[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int tok = n * 8 + 2 * tid4 + (e & 1);
-            float x = sacc[n][e] * ((e & 1) ? ksc.y : ksc.x);
+            const int tok = gid + 8 * (e >> 1);
+            float x = sacc[nt][e] * ksc[e >> 1];
             x = capped ? tanhf(x * a.scale / a.softcap) * (a.softcap * kLog2e) : x * scale_log2;
             bool ok = tok < ntok;
-            if (a.q_len > 1) ok = ok && (kbase + tok <= ((e >> 1) ? qpos1 : qpos0));
-            sc[n][e] = ok ? x : -INFINITY;
+            if (a.q_len > 1) ok = ok && (kbase + tok <= qpos[nt][e & 1]);
+            p[e] = ok ? x : -INFINITY;
           }
-        }
-        float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-        float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-        mx0 = warp_max_xor(warp_max_xor(mx0, 1), 2);
-        mx1 = warp_max_xor(warp_max_xor(mx1, 1), 2);
-        const float mn0 = fmaxf(m0, mx0);
-        const float mn1 = fmaxf(m1, mx1);
-        const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
-        const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
-        const float al0 = fast_exp2(m0 - mu0);
-        const float al1 = fast_exp2(m1 - mu1);
-        float p[2][4];
 #pragma unroll
-        for (int n = 0; n < 2; ++n) {
-          p[n][0] = fast_exp2(sc[n][0] - mu0);
-          p[n][1] = fast_exp2(sc[n][1] - mu0);
-          p[n][2] = fast_exp2(sc[n][2] - mu1);
-          p[n][3] = fast_exp2(sc[n][3] - mu1);
-        }
-        l0 = l0 * al0 + (p[0][0] + p[0][1]) + (p[1][0] + p[1][1]);
-        l1 = l1 * al1 + (p[0][2] + p[0][3]) + (p[1][2] + p[1][3]);
-        m0 = mn0;
-        m1 = mn1;
+          for (int j = 0; j < 2; ++j) {
+            float mx = fmaxf(p[j], p[2 + j]);
+            mx = warp_max_xor(warp_max_xor(warp_max_xor(mx, 4), 8), 16);
+            const float mn = fmaxf(m[nt][j], mx);
+            const float mu = mn == -INFINITY ? 0.f : mn;
+            const float al = fast_exp2(m[nt][j] - mu);
+            p[j] = fast_exp2(p[j] - mu);
+            p[2 + j] = fast_exp2(p[2 + j] - mu);
+            l[nt][j] = l[nt][j] * al + (p[j] + p[2 + j]);
+            m[nt][j] = mn;
 #pragma unroll
-        for (int n = 0; n < D / 8; ++n) {
-          o[n][0] *= al0;
-          o[n][1] *= al0;
-          o[n][2] *= al1;
-          o[n][3] *= al1;
-        }
-        // V scales folded into the probabilities (masked tokens stay exactly 0)
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
-          const float2 vsc = *reinterpret_cast<const float2*>(vscale + n * 8 + 2 * tid4);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            p[n][e] = p[n][e] > 0.f ? p[n][e] * ((e & 1) ? vsc.y : vsc.x) : 0.f;
+            for (int mt = 0; mt < KS; ++mt) {
+              o[nt][mt][j] *= al;
+              o[nt][mt][2 + j] *= al;
+            }
           }
+          // V scales into the probabilities (masked tokens stay exactly 0), then
+          // the [token][row] 8x8 halves transposed into [row][token] B fragments.
+#pragma unroll
+          for (int e = 0; e < 4; ++e) p[e] = p[e] > 0.f ? p[e] * vsc[e >> 1] : 0.f;
+          pb[nt][0] = movmatrix_trans(pack2<kF16>(p[0], p[1]));   // tokens 2t, 2t+1
+          pb[nt][1] = movmatrix_trans(pack2<kF16>(p[2], p[3]));   // tokens 2t+8, 2t+9
         }
-        const uint32_t pa[4] = {pack2<kF16>(p[0][0], p[0][1]), pack2<kF16>(p[0][2], p[0][3]),
-                                pack2<kF16>(p[1][0], p[1][1]), pack2<kF16>(p[1][2], p[1][3])};
 
-        // O += P V: per slice, tokens (2t, 2t+1 | 2t+8, 2t+9) x dims 16g..16g+15
+        // O^T += V^T P^T: per slice, tokens (2t, 2t+1 | 2t+8, 2t+9) x dims 16g..16g+15
 #pragma unroll
         for (int sl = 0; sl < kSlices; ++sl) {
           uint4 rv[4];
@@ -453,69 +516,77 @@ __global__ void __launch_bounds__((max_heads(D) + 1) * 32, 1)
             const uint32_t lo23 = __byte_perm(word_of(rv[0], q), word_of(rv[1], q), 0x7362);
             const uint32_t hi01 = __byte_perm(word_of(rv[2], q), word_of(rv[3], q), 0x5140);
             const uint32_t hi23 = __byte_perm(word_of(rv[2], q), word_of(rv[3], q), 0x7362);
-            const int nt = sl * 16 + 4 * q;
-            mma_16816<kF16>(o[nt + 0], pa, e4m3x2_to_f16x2(lo01 & 0xFFFFu),
-                            e4m3x2_to_f16x2(hi01 & 0xFFFFu));
-            mma_16816<kF16>(o[nt + 1], pa, e4m3x2_to_f16x2(lo01 >> 16),
-                            e4m3x2_to_f16x2(hi01 >> 16));
-            mma_16816<kF16>(o[nt + 2], pa, e4m3x2_to_f16x2(lo23 & 0xFFFFu),
-                            e4m3x2_to_f16x2(hi23 & 0xFFFFu));
-            mma_16816<kF16>(o[nt + 3], pa, e4m3x2_to_f16x2(lo23 >> 16),
-                            e4m3x2_to_f16x2(hi23 >> 16));
+            // m-tile 2q: dims 16g + 4q (m-slot g) and + 1 (m-slot g + 8);
+            // m-tile 2q + 1: dims 16g + 4q + 2 and + 3
+            uint32_t a0[4], a1[4];
+            e4m3x4_to_f16x2x2(lo01, a0[0], a0[1]);
+            e4m3x4_to_f16x2x2(hi01, a0[2], a0[3]);
+            e4m3x4_to_f16x2x2(lo23, a1[0], a1[1]);
+            e4m3x4_to_f16x2x2(hi23, a1[2], a1[3]);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              mma_16816<kF16>(o[nt][sl * 8 + 2 * q], a0, pb[nt][0], pb[nt][1]);
+              mma_16816<kF16>(o[nt][sl * 8 + 2 * q + 1], a1, pb[nt][0], pb[nt][1]);
+            }
           }
         }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.empty[st]);
+      if (!SP && lane == 0) mbar_arrive(&sm.empty[st]);
     }
 
     // ---- finalize this (sequence, head) partial ------------------------------------
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
     const long long slot =
         balanced ? s + blockIdx.x : s * a.plan.splits + (blockIdx.x - s * a.plan.splits);
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = gid + 8 * half;
-      if (r < a.rows) {
-        const float l = half ? l1 : l0;
-        const float m = half ? m1 : m0;
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        const int qi = r / a.group;
-        const int qh = kh * a.group + (r - qi * a.group);
-        const long long row = (slot * a.num_heads + qh) * a.q_len + qi;
-        float* dst = a.part_o + row * D;
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-        for (int sl = 0; sl < kSlices; ++sl) {
+      for (int j = 0; j < 2; ++j) {
+        float lt = l[nt][j];
+        lt += __shfl_xor_sync(0xffffffffu, lt, 4);
+        lt += __shfl_xor_sync(0xffffffffu, lt, 8);
+        lt += __shfl_xor_sync(0xffffffffu, lt, 16);
+        const int r = 8 * nt + 2 * tid4 + j;
+        if (r < a.rows) {
+          const float inv = lt > 0.f ? 1.f / lt : 0.f;
+          const int qi = r / a.group;
+          const int qh = kh * a.group + (r - qi * a.group);
+          const long long row = (slot * a.num_heads + qh) * a.q_len + qi;
+          float* dst = a.part_o + row * D;
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {      // n-slot 2t + c: dims 128 sl + 16 (2t + c) + j
+          for (int sl = 0; sl < kSlices; ++sl) {
 #pragma unroll
-            for (int m4 = 0; m4 < 4; ++m4) {
-              const int nt = sl * 16 + 4 * m4;
-              const float4 v = make_float4(o[nt][2 * half + c] * inv, o[nt + 1][2 * half + c] * inv,
-                                           o[nt + 2][2 * half + c] * inv,
-                                           o[nt + 3][2 * half + c] * inv);
-              *reinterpret_cast<float4*>(dst + sl * kSlice + 16 * (2 * tid4 + c) + 4 * m4) = v;
+            for (int v4 = 0; v4 < 4; ++v4) {   // dims 16g + 4 v4 .. + 3 of the slice
+              const int mt = sl * 8 + 2 * v4;
+              const float4 v = make_float4(o[nt][mt][j] * inv, o[nt][mt][2 + j] * inv,
+                                           o[nt][mt + 1][j] * inv, o[nt][mt + 1][2 + j] * inv);
+              *reinterpret_cast<float4*>(dst + sl * kSlice + 16 * gid + 4 * v4) = v;
             }
           }
+          if (gid == 0) {
+            a.part_lse[row] = lt > 0.f ? (m[nt][j] + log2f(lt)) * kLn2 : -INFINITY;
+          }
         }
-        if (tid4 == 0) a.part_lse[row] = l > 0.f ? (m + log2f(l)) * kLn2 : -INFINITY;
       }
     }
     cur = seg_end;
   }
+  if (SP) griddep_launch_dependents();
 }
 
 template <int D, int Q_DT>
-const void* fp8_kernel_ptr() {
-  return reinterpret_cast<const void*>(&decode_fp8_kernel<D, Q_DT>);
+const void* fp8_kernel_ptr(int rows, bool sp) {
+  if (sp) {
+    return rows <= 8 ? reinterpret_cast<const void*>(&decode_fp8_kernel<D, Q_DT, 1, true>)
+                     : reinterpret_cast<const void*>(&decode_fp8_kernel<D, Q_DT, 2, true>);
+  }
+  return rows <= 8 ? reinterpret_cast<const void*>(&decode_fp8_kernel<D, Q_DT, 1, false>)
+                   : reinterpret_cast<const void*>(&decode_fp8_kernel<D, Q_DT, 2, false>);
 }
 
-const void* select_fp8_kernel(const AttnArgs& a) {
+const void* select_fp8_kernel(const AttnArgs& a, bool sp = false) {
 #define LLMOPT_FP8_CASE(DV, QT) \
-  if (a.head_dim == DV && a.q_dtype == QT) return fp8_kernel_ptr<DV, QT>();
+  if (a.head_dim == DV && a.q_dtype == QT) return fp8_kernel_ptr<DV, QT>(a.rows, sp);
   LLMOPT_FP8_CASE(128, kF32)
   LLMOPT_FP8_CASE(128, kF16)
   LLMOPT_FP8_CASE(128, kBF16)
@@ -553,18 +624,23 @@ bool decode_fp8_supported(const AttnArgs& a) {
   return select_fp8_kernel(a) != nullptr;
 }
 
-// KV heads per CTA and ring depth (LLMOPT_B200_FP8_HPC / LLMOPT_B200_FP8_STAGES
-// override them; invalid values are ignored).
+// KV heads per CTA, self-issuing one-warp CTAs, ring depth
+// (LLMOPT_B200_FP8_HPC / LLMOPT_B200_FP8_SP / LLMOPT_B200_FP8_STAGES override
+// them; invalid values are ignored).
 bool decode_fp8_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch) {
-  int hpc = a.kv_heads % 2 == 0 ? 2 : 1;
+  int hpc = a.kv_heads % 4 == 0 ? 4 : (a.kv_heads % 2 == 0 ? 2 : 1);
   const int hpc_env = env_int("LLMOPT_B200_FP8_HPC", 0);
   if (hpc_env >= 1 && hpc_env <= max_heads(a.head_dim) && a.kv_heads % hpc_env == 0) {
     hpc = hpc_env;
   }
-  const void* fn = select_fp8_kernel(a);
+  bool sp = hpc == 1;
+  const int sp_env = env_int("LLMOPT_B200_FP8_SP", -1);
+  if (sp_env == 0 || sp_env == 1) sp = sp_env == 1;
+  if (sp) hpc = 1;                      // one warp = one KV head
+  const void* fn = select_fp8_kernel(a, sp);
   if (fn == nullptr) return false;
   const long long prefix_entries = a.plan.mode == kModeBalanced ? a.batch + 1 : 0;
-  int stages = env_int("LLMOPT_B200_FP8_STAGES", 4);
+  int stages = env_int("LLMOPT_B200_FP8_STAGES", 3);
   if (stages < 2) stages = 2;
   if (stages > 16) stages = 16;
   size_t smem = fp8_smem_bytes(hpc, a.head_dim, stages, prefix_entries);
@@ -579,13 +655,13 @@ bool decode_fp8_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch)
     return false;
   }
   int occ = 0;
-  const int threads = (hpc + 1) * 32;
+  const int threads = sp ? 32 : (hpc + 1) * 32;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem) != cudaSuccess ||
       occ < 1) {
     return false;
   }
   launch->heads_per_cta = hpc;
-  launch->self_issue = 0;
+  launch->self_issue = sp ? 1 : 0;
   launch->stages = stages;
   launch->ctas_per_sm = occ;
   launch->smem_bytes = smem;
@@ -596,7 +672,7 @@ bool decode_fp8_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch)
 cudaError_t decode_fp8_launch(const AttnArgs& a, const DecodeLaunch& launch,
                               const CUtensorMap& tmk, const CUtensorMap& tmv,
                               cudaStream_t stream) {
-  const void* fn = select_fp8_kernel(a);
+  const void* fn = select_fp8_kernel(a, launch.self_issue != 0);
   if (fn == nullptr) return cudaErrorInvalidValue;
   const int head_groups = a.kv_heads / launch.heads_per_cta;
   const long long gx =
@@ -604,7 +680,7 @@ cudaError_t decode_fp8_launch(const AttnArgs& a, const DecodeLaunch& launch,
   if (gx <= 0) return cudaSuccess;
   if (gx > 0x7fffffffLL || head_groups > 65535) return cudaErrorInvalidConfiguration;
   dim3 grid((unsigned)gx, (unsigned)head_groups);
-  dim3 block((launch.heads_per_cta + 1) * 32);
+  dim3 block(launch.self_issue ? 32 : (launch.heads_per_cta + 1) * 32);
   int hpc = launch.heads_per_cta;
   int stages = launch.stages;
   void* args[] = {const_cast<CUtensorMap*>(&tmk), const_cast<CUtensorMap*>(&tmv),

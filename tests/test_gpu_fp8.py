@@ -101,10 +101,14 @@ def test_decode_tensor_core_path(cuda, head_dim, heads, kv_heads):
     _check(case, cuda)
 
 
-@pytest.mark.parametrize("hpc,stages", [(1, 2), (2, 4), (4, 3), (8, 6)])
-def test_heads_per_cta_and_ring_depth(cuda, monkeypatch, hpc, stages):
+@pytest.mark.parametrize("hpc,stages,sp", [(1, 2, 0), (2, 4, 0), (4, 3, 0), (8, 6, 0),
+                                           (1, 2, 1), (1, 3, 1), (1, 6, 1)])
+def test_heads_per_cta_and_ring_depth(cuda, monkeypatch, hpc, stages, sp):
+    """Producer-warp CTAs of 1-8 KV heads and self-issuing one-warp CTAs, each
+    over several ring depths."""
     monkeypatch.setenv("LLMOPT_B200_FP8_HPC", str(hpc))
     monkeypatch.setenv("LLMOPT_B200_FP8_STAGES", str(stages))
+    monkeypatch.setenv("LLMOPT_B200_FP8_SP", str(sp))
     case = _fp8_case(7100 + hpc, batch=6, heads=32, kv_heads=8, head_dim=128,
                      ctx=[5, 160, 2049, 17, 700, 3000])
     _check(case, cuda, modes=("auto", "fixed"))
