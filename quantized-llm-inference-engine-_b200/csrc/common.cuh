@@ -158,6 +158,46 @@ __device__ __forceinline__ long long floormod(long long a, long long b) {
   return (r != 0 && ((r < 0) != (b < 0))) ? r + b : r;
 }
 
+// write_decode's destination of sequence s (paged_cache.py:252-259): block
+// id (an id < 0 or >= num_blocks goes to block 0) and slot; false when the
+// table column is outside the row (nothing is written).
+__device__ __forceinline__ bool decode_target(const void* table, int table_i64,
+                                              long long table_stride, long long width,
+                                              const void* offsets, int off_i64, long long bs,
+                                              long long num_blocks, long long s,
+                                              long long* block, long long* slot) {
+  const long long off = load_index(offsets, off_i64, s);
+  const long long col = floordiv(off, bs);
+  if (col < -width || col >= width) return false;
+  long long id = load_index(table, table_i64, s * table_stride + (col < 0 ? col + width : col));
+  if (id < 0 || id >= num_blocks) id = 0;
+  *block = id;
+  *slot = floormod(off, bs);
+  return true;
+}
+
+// True when a later sequence of the batch writes the same row of block 0.
+// The reference's write_decode is one index_put, where the last of repeated
+// indices wins; repeats arise by design only at block 0 (the redirect of
+// invalid ids), so only rows of block 0 are checked.  Warp-collective.
+__device__ __forceinline__ bool block0_row_taken_later(const void* table, int table_i64,
+                                                       long long table_stride, long long width,
+                                                       const void* offsets, int off_i64,
+                                                       long long bs, long long num_blocks,
+                                                       long long s, long long batch,
+                                                       long long slot, int lane) {
+  bool hit = false;
+  for (long long s2 = s + 1 + lane; s2 < batch; s2 += 32) {
+    long long b2, t2;
+    if (decode_target(table, table_i64, table_stride, width, offsets, off_i64, bs, num_blocks,
+                      s2, &b2, &t2) &&
+        b2 == 0 && t2 == slot) {
+      hit = true;
+    }
+  }
+  return __any_sync(0xffffffffu, hit);
+}
+
 // ---------------------------------------------------------------------------
 // PTX wrappers
 // ---------------------------------------------------------------------------

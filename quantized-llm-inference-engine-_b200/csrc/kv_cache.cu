@@ -220,6 +220,10 @@ __global__ void __launch_bounds__(64) kv_write_decode_kernel(const KvWriteArgs a
   long long id = load_index(a.table, a.table_i64, s * a.table_stride + (col < 0 ? col + W : col));
   if (id < 0 || id >= a.num_blocks) id = 0;         // paged_cache.py:257-259
   const long long slot = floormod(off, bs);         // paged_cache.py:253
+  if (id == 0 && block0_row_taken_later(a.table, a.table_i64, a.table_stride, W, a.offsets,
+                                        a.off_i64, bs, a.num_blocks, s, a.batch, slot, lane)) {
+    return;                                         // a later sequence's row wins
+  }
   if (warp == 0) {
     append_row<IN_DT, OUT_DT>(a, a.keys, s * a.k_s, a.k_h, a.k_cache, a.k_scale, id, slot, lane);
   } else {

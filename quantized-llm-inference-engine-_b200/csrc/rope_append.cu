@@ -287,8 +287,13 @@ __global__ void __launch_bounds__(kThreads, 3) rope_append_kernel(const RopeArgs
       long long id =
           load_index(a.table, a.table_i64, s * a.table_stride + (col < 0 ? col + W : col));
       if (id < 0 || id >= a.num_blocks) id = 0;   // paged_cache.py:257-259
-      dec_dst = (((long long)a.layer * a.num_blocks + id) * bs + floormod(start, bs)) *
-                (long long)a.kv_heads * D;
+      // A later sequence writing the same row of block 0 wins (index_put).
+      if (id != 0 || !block0_row_taken_later(a.table, a.table_i64, a.table_stride, W,
+                                             a.offsets, a.off_i64, bs, a.num_blocks, s,
+                                             a.batch, floormod(start, bs), lane)) {
+        dec_dst = (((long long)a.layer * a.num_blocks + id) * bs + floormod(start, bs)) *
+                  (long long)a.kv_heads * D;
+      }
     }
   }
 

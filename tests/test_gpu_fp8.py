@@ -273,3 +273,34 @@ def test_memory_and_reset(cuda):
     cache.key_scale.fill_(3.0)
     cache.reset()
     assert torch.count_nonzero(cache.key_scale) == 0
+
+
+@pytest.mark.parametrize("kind", ["bf16", "fp8"])
+def test_write_decode_repeated_block0_rows_keep_the_last_writer(cuda, kind):
+    """write_decode is one index_put in the reference (paged_cache.py:260-261):
+    when invalid ids send several sequences to the same row of block 0, the
+    last sequence's values are the ones stored."""
+    pkg = load_package()
+    rng = np.random.default_rng(7650)
+    L, nb, bs, kvh, d = 1, 8, 16, 2, 128
+    table = np.array([[-1, 3], [5, -1], [99, 2], [-1, 4], [0, 6]], dtype=np.int64)
+    offs = np.array([4, 20, 4, 4, 5])   # rows 0, 1->(0, 4), 2 (id 99), 3 all land on (0, 4)
+    x = rng.standard_normal((5, kvh, d)).astype(np.float32)
+    keys, vals = po.from_f32(x, "bf16"), po.from_f32(x * 0.5, "bf16")
+    dt = torch.bfloat16 if kind == "bf16" else torch.float8_e4m3fn
+    cache = pkg.PagedKVCache(L, nb, bs, kvh, d, dtype=dt, device=cuda)
+    for _ in range(3):
+        cache.write_decode(0, torch.from_numpy(table).to(cuda), torch.from_numpy(offs).to(cuda),
+                           to_dev(keys, "bf16", cuda), to_dev(vals, "bf16", cuda))
+    torch.cuda.synchronize(cuda)
+    if kind == "bf16":
+        kc = np.zeros((L, nb, bs, kvh, d), np.uint16)
+        vc = kc.copy()
+        po.write_decode(kc, vc, "bf16", 0, table, offs, keys, vals, "bf16")
+        got = cache.key_cache.view(torch.int16).cpu().numpy().view(np.uint16)
+        assert np.array_equal(got, kc)
+        assert np.array_equal(got[0, 0, 4], keys[3])          # the last of rows 0-3
+    else:
+        kc, vc, ks, vs = _empty_pools(L, nb, bs, kvh, d)
+        po.write_decode_e4m3(kc, vc, ks, vs, 0, table, offs, keys, vals, "bf16")
+        _assert_pools(cache, kc, vc, ks, vs)
