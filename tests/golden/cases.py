@@ -354,3 +354,44 @@ def case_merge(seed: int = 20) -> dict:
     l1[1, 2, 4] = -np.inf
     l2[1, 2, 4] = -np.inf
     return dict(o1=o1, o2=o2, l1=l1, l2=l2)
+
+
+# ---------------------------------------------------------------------------
+# Weight-only quantized linear (QuantLinear over RTN / GPTQ packed weights)
+# ---------------------------------------------------------------------------
+
+def case_quant(seed: int, *, out_features: int, in_features: int, bits: int, group: int,
+               symmetric: bool, m: int, bias: bool = True, kind: str = "f32",
+               strategy: str = "rtn", calib: int = 0) -> dict:
+    """A linear layer's float weight, bias and input, plus (for GPTQ) the
+    calibration activations whose second moment drives the quantizer."""
+    rng = np.random.default_rng(seed)
+    w = _normal(rng, (out_features, in_features), 0.05)
+    w[0, :group] *= 8.0                         # one outlier group
+    b = _normal(rng, (out_features,), 0.1) if bias else None
+    x = _normal(rng, (m, in_features))
+    xc = _normal(rng, (calib, in_features)) if calib else None
+    return dict(weight=w, bias=b, x=from_f32(x, kind), x_kind=kind, bits=bits, group=group,
+                symmetric=symmetric, strategy=strategy, calib=xc,
+                shape=(out_features, in_features))
+
+
+QUANT_CASES = {
+    "quant_rtn4_sym_g64": lambda: case_quant(40, out_features=48, in_features=256, bits=4,
+                                             group=64, symmetric=True, m=5),
+    "quant_rtn4_asym_g128": lambda: case_quant(41, out_features=40, in_features=256, bits=4,
+                                               group=128, symmetric=False, m=3),
+    "quant_rtn8_sym_g64": lambda: case_quant(42, out_features=32, in_features=128, bits=8,
+                                             group=64, symmetric=True, m=4, bias=False),
+    "quant_rtn8_asym_g32": lambda: case_quant(43, out_features=24, in_features=128, bits=8,
+                                              group=32, symmetric=False, m=2),
+    "quant_rtn2_sym_g32": lambda: case_quant(44, out_features=16, in_features=128, bits=2,
+                                             group=32, symmetric=True, m=3),
+    "quant_gptq4_sym_g64": lambda: case_quant(45, out_features=32, in_features=128, bits=4,
+                                              group=64, symmetric=True, m=4, strategy="gptq",
+                                              calib=64),
+    "quant_rtn4_sym_g64_bf16": lambda: case_quant(46, out_features=64, in_features=256, bits=4,
+                                                  group=64, symmetric=True, m=6, kind="bf16"),
+    "quant_rtn4_asym_g64_f16": lambda: case_quant(47, out_features=64, in_features=192, bits=4,
+                                                  group=64, symmetric=False, m=3, kind="f16"),
+}

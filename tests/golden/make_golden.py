@@ -2,7 +2,7 @@
 
 Run once, in a container where the reference source is present::
 
-    python tests/golden/make_golden.py /path/to/reference/src [--only=rope|step]
+    python tests/golden/make_golden.py /path/to/reference/src [--only=rope|step|quant]
 
 It imports ``llmopt.attention`` / ``llmopt.cache`` from that path, runs them
 on CPU on the seeded inputs of ``cases.py`` (plus the reference's own
@@ -23,7 +23,9 @@ Recorded per attention run:
 Rotary + append cases (``rope_*.npz``) record the reference's cos/sin tables,
 the rotated query and the caches after the append, bit for bit;
 ``step_metadata.npz`` the reference runner's decode metadata for every step of
-the request scenario in ``cases.step_scenario``.
+the request scenario in ``cases.step_scenario``; ``quant_*.npz`` the reference
+quantizer's packed weights, the dense weight ``QuantLinear`` dequantizes them
+to and its forward output.
 """
 
 from __future__ import annotations
@@ -222,6 +224,44 @@ def make_step(ModelRunner) -> dict:
     return out
 
 
+def make_quant(build, build_quantizer, QuantLinear) -> dict:
+    """The reference quantizer's packed weight (qweight / scales / zeros), the
+    dense weight it dequantizes to in the compute dtype, and QuantLinear's
+    forward on the case's input, all run on CPU."""
+    import torch
+    from torch import nn
+
+    case = build()
+    kind = case["x_kind"]
+    dtype = _kind_dtype(kind)
+    out_f, in_f = case["shape"]
+    weight = torch.from_numpy(case["weight"])
+    quantizer = build_quantizer(case["strategy"], bits=case["bits"], group_size=case["group"],
+                                symmetric=case["symmetric"])
+    hessian = None
+    if case["calib"] is not None:
+        xc = torch.from_numpy(case["calib"]).to(torch.float32)
+        hessian = 2.0 / xc.shape[0] * xc.T @ xc
+    qt = quantizer.quantize(weight, hessian)
+    linear = nn.Linear(in_f, out_f, bias=case["bias"] is not None).to(dtype)
+    with torch.no_grad():
+        linear.weight.copy_(weight.to(dtype))
+        if case["bias"] is not None:
+            linear.bias.copy_(torch.from_numpy(case["bias"]).to(dtype))
+    layer = QuantLinear.from_float(linear, qt, compute_dtype=dtype)
+    x = _torch_from(case["x"], kind)
+    with torch.no_grad():
+        y = layer(x)
+    out = {"qweight": qt.qweight.numpy().copy(), "scales": qt.scales.numpy().copy(),
+           "zeros": qt.zeros.numpy().copy(),
+           "dense": _np_from(layer._dequantized_weight(), kind),
+           "out": _np_from(y, kind), "torch": torch.__version__,
+           "checksum": cases.checksum(case["weight"], case["x"])}
+    if case["bias"] is not None:
+        out["bias"] = _np_from(linear.bias.detach(), kind)
+    return out
+
+
 def make_fixture(PagedAttention, PagedAttentionConfig, PagedKVCache, BlockPool) -> dict:
     """The reference's ``tests/test_paged_attention.py`` fixture and its four checks,
     with ``pool.append`` run before the chain is read (the shipped order raises)."""
@@ -307,6 +347,16 @@ def main(ref_src: str, only: str | None = None) -> None:
         np.savez_compressed(os.path.join(HERE, "step_metadata.npz"), **out)
         print("wrote step_metadata")
         return
+    if only == "quant":
+        from llmopt.quantization.quant_linear import QuantLinear
+        from llmopt.quantization.quantizers import build_quantizer
+
+        for name, build in cases.QUANT_CASES.items():
+            out = make_quant(build, build_quantizer, QuantLinear)
+            out["versions"] = np.array(str(meta))
+            np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+            print("wrote", name)
+        return
     if only == "rope":
         from llmopt.model.rotary import RotaryEmbedding, apply_rotary_pos_emb
 
@@ -330,6 +380,14 @@ def main(ref_src: str, only: str | None = None) -> None:
 
     for name, build in cases.ROPE_CASES.items():
         out = make_rope(build, RotaryEmbedding, apply_rotary_pos_emb, PagedKVCache)
+        out["versions"] = np.array(str(meta))
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+        print("wrote", name)
+    from llmopt.quantization.quant_linear import QuantLinear
+    from llmopt.quantization.quantizers import build_quantizer
+
+    for name, build in cases.QUANT_CASES.items():
+        out = make_quant(build, build_quantizer, QuantLinear)
         out["versions"] = np.array(str(meta))
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
         print("wrote", name)
