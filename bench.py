@@ -63,7 +63,7 @@ def parse_args(argv=None):
                         "peer memory, or NCCL all_gather_into_tensor after it")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--config", choices=("c2", "c3", "c4", "c5", "rope", "step", "fp8"),
+    p.add_argument("--config", choices=("c2", "c3", "c4", "c5", "rope", "step", "fp8", "quant"),
                    default="c2",
                    help="c2 (default, the headline line): Llama-3-8B decode; c3: chunked "
                         "prefill; c4: 128k-context decode sharded by KV head (strong "
@@ -73,7 +73,9 @@ def parse_args(argv=None):
                         "decode step (device-side metadata advance, rotary append, "
                         "attention) replayed from a CUDA graph vs launched eagerly, beside "
                         "the reference runner's host-side metadata build; fp8: the config-2 "
-                        "decode step over an e4m3 KV cache beside the bf16 one (1 GPU)")
+                        "decode step over an e4m3 KV cache beside the bf16 one (1 GPU); "
+                        "quant: QuantLinear's fused int4 dequantize-GEMM on the Llama-3-8B "
+                        "MLP shapes beside the dense bf16 GEMM (1 GPU)")
     return p.parse_args(argv)
 
 
@@ -1133,6 +1135,93 @@ def run_fp8(args) -> None:
     }), flush=True)
 
 
+def run_quant(args) -> None:
+    """QuantLinear.forward (fused dequantize-GEMM over packed 4-bit codes) on the
+    Llama-3-8B MLP projections, beside what the reference's forward runs in the
+    steady state: F.linear over its cached dense bf16 copy (a cuBLAS GEMM)."""
+    import torch
+
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        print(json.dumps({"config": "quant", "skipped": "single-GPU line"}), flush=True)
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pkg = importlib.import_module(PACKAGE)
+    from types import SimpleNamespace
+
+    from oracle.quant_oracle import weight_bytes
+
+    group, bits = 128, 4
+    g = torch.Generator(device=dev)
+    g.manual_seed(4000)
+    peak, peak_kind = measured_hbm_peak()
+    rows = []
+    for (k, n) in ((4096, 14336), (14336, 4096)):
+        # random codes / scales of the reference's layout (values do not matter
+        # for timing; parity is the tests' job)
+        qweight = torch.randint(0, 256, (n, k // 2), generator=g, device=dev,
+                                dtype=torch.int32).to(torch.uint8)
+        scales = (torch.rand((n, k // group), generator=g, device=dev) * 0.01 + 1e-3)
+        zeros = torch.zeros_like(scales)
+        qt = SimpleNamespace(qweight=qweight, scales=scales, zeros=zeros, bits=bits,
+                             group_size=group, symmetric=True)
+        lin = torch.nn.Linear(k, n, bias=False, device=dev, dtype=torch.bfloat16)
+        layer = pkg.QuantLinear.from_float(lin, qt, compute_dtype=torch.bfloat16)
+        dense = layer.dequantized_weight(dev)            # the reference's cached copy
+        for m in (1, 16, 64):
+            x = (torch.randn((m, k), generator=g, device=dev)).to(torch.bfloat16)
+            # the packed weight (29 MB) fits in L2: flush it before every timed call
+            flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+            def timed(fn, iters):
+                # Replayed from a CUDA graph, so the events time the GPU work and
+                # not the host's launch path; L2 flushed before every replay.
+                for _ in range(max(args.warmup, 3)):
+                    fn()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    fn()
+                for _ in range(3):
+                    graph.replay()
+                evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                       for _ in range(iters)]
+                for a, b in evs:
+                    flush.zero_()
+                    a.record()
+                    graph.replay()
+                    b.record()
+                torch.cuda.synchronize(dev)
+                del graph
+                return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+            iters = max(10, min(args.steps, 50))
+            ms_q = timed(lambda: layer(x), iters)
+            ms_d = timed(lambda: torch.nn.functional.linear(x, dense), iters)
+            wb = weight_bytes(n, k, bits, group) + 2 * m * (k + n)
+            db = n * k * 2 + 2 * m * (k + n)
+            rows.append({"k": k, "n": n, "tokens": m,
+                         "quant_ms": round(ms_q, 5), "dense_bf16_ms": round(ms_d, 5),
+                         "speedup_vs_dense": round(ms_d / ms_q, 3),
+                         "quant_GBps": round(wb / (ms_q * 1e-3) / 1e9, 1),
+                         "quant_frac_of_hbm": round(wb / (ms_q * 1e-3) / 1e9 / peak, 4),
+                         "dense_GBps": round(db / (ms_d * 1e-3) / 1e9, 1),
+                         "quant_TFLOPs": round(2 * m * n * k / (ms_q * 1e-3) / 1e12, 2)})
+            del flush
+    top = max(rows, key=lambda r: r["quant_frac_of_hbm"])
+    print(json.dumps({
+        "config": "quant",
+        "metric": "QuantLinear.forward (int4, group 128, bf16) weight-stream GB/s",
+        "unit": "GB/s", "value": top["quant_GBps"], "n_gpus": 1,
+        "workload": "Llama-3-8B MLP projections (4096->14336, 14336->4096), 1/16/64 tokens; "
+                    "each call replayed from a CUDA graph, L2 flushed before every replay; "
+                    "median of CUDA-event times",
+        "rows": rows,
+        "roofline": {"bound": "hbm", "achieved": top["quant_GBps"], "peak": peak,
+                     "unit": "GB/s", "frac": top["quant_frac_of_hbm"],
+                     "kernel": "wq_gemm_kernel", "peak_kind": f"{peak_kind} hbm_gbs"},
+    }), flush=True)
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
@@ -1143,6 +1232,8 @@ def main(argv=None):
         run_rope(args)
     elif args.config == "fp8":
         run_fp8(args)
+    elif args.config == "quant":
+        run_quant(args)
     elif args.config != "c2":
         run_extra(args)
     else:

@@ -30,6 +30,9 @@
  *                              PagedAttentionLayer.forward  src/llmopt/model/layers.py:106-134
  *                              (RotaryEmbedding.forward, apply_rotary_pos_emb
  *                              src/llmopt/model/rotary.py:16-46, 103-121)
+ *   llmopt_quant_linear     <- QuantLinear.forward  src/llmopt/quantization/quant_linear.py:93-113
+ *   llmopt_dequantize       <- QuantizedTensor.dequantize / dequantize
+ *                              src/llmopt/quantization/quantizers.py:203-239
  *   llmopt_*_scaled         <- the same operations on an FP8 (e4m3) cache; the
  *                              reference only names the float8 dtypes
  *                              (src/llmopt/utils/misc.py:33-34, 57) and has no
@@ -414,6 +417,43 @@ LLMOPT_API int llmopt_paged_gather_scaled(const void* key_cache, const void* val
                     int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
                     int64_t batch, int64_t max_len, float* out_keys, float* out_values,
                     uint8_t* valid, uint32_t* err, void* stream);
+
+/*
+ * Weight-only quantized linear layer.  Replaces QuantLinear.forward
+ * (src/llmopt/quantization/quant_linear.py:93-113: dequantize the packed weight
+ * to the compute dtype, quantizers.py:203-239, then F.linear) by one fused
+ * kernel that reads the packed codes on every call (no dense copy is kept).
+ *
+ *   x       [m, k] compute dtype (f32 / f16 / bf16), row stride ldx
+ *   qweight the reference's QuantizedTensor.qweight: uint8 [n, k/2] for 2- and
+ *           4-bit codes (two per byte, even column in the low nibble, symmetric
+ *           codes biased by 2^(bits-1)); uint8 [n, k] (asymmetric) or int8 [n, k]
+ *           (symmetric) for 8-bit
+ *   scales, zeros  float32 [n, k / group_size] (zeros unused and may be null
+ *           when symmetric)
+ *   bias    [n] compute dtype, or null;  out [m, n] compute dtype, stride ldo
+ * The weight element is (q - offset) * s or (q - z) * s in float32 rounded to
+ * the compute dtype, as the reference's dequantize.  16-bit compute dtypes
+ * with k % 128 == 0, n % 64 == 0, group_size 32, 64, 128 or a multiple of
+ * 128, and 16-byte aligned x / qweight run on tensor cores (2- and 4-bit codes
+ * are scaled there in 16-bit arithmetic with the scale split into two 16-bit
+ * parts and one rounding, which matches the reference's float32 product
+ * rounded to the compute dtype up to the split's precision); everything else
+ * runs on CUDA cores.  The workspace (fp32 split-k partials)
+ * is sized by llmopt_quant_linear_workspace_size for the same m, n, k.
+ */
+LLMOPT_API int llmopt_quant_linear_workspace_size(int device, int64_t m, int64_t n, int64_t k,
+                    int32_t bits, int32_t group_size, int32_t x_dtype, size_t* bytes);
+LLMOPT_API int llmopt_quant_linear(const void* x, int32_t x_dtype, int64_t m, int64_t ldx,
+                    const void* qweight, int32_t bits, int32_t group_size, int32_t symmetric,
+                    const float* scales, const float* zeros, int64_t n, int64_t k,
+                    const void* bias, void* out, int64_t ldo, void* workspace,
+                    size_t workspace_bytes, void* stream);
+/* The dense weight [n, k] in out_dtype, bit-exact with the reference's
+ * dequantize (QuantizedTensor.dequantize().to(dtype), quantizers.py:231-239). */
+LLMOPT_API int llmopt_dequantize(const void* qweight, int32_t bits, int32_t group_size,
+                    int32_t symmetric, const float* scales, const float* zeros, int64_t n,
+                    int64_t k, void* out, int32_t out_dtype, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -6,7 +6,8 @@ backed by the C-ABI library ``libllmopt_b200.so`` (``include/llmopt_b200.h``):
 
 * paged decode attention with an exact log-sum-exp split-K combine;
 * chunked-prefill causal attention over block-table-addressed KV;
-* the KV append into the block pool, fused with the dtype cast.
+* the KV append into the block pool, fused with the dtype cast;
+* FP8 (e4m3) KV storage; the weight-only quantized linear layer (``QuantLinear``).
 
 ``install()`` rebinds the reference engine's names; ``dist`` shards the path by
 KV head over several GPUs.  The package directory name is not a Python
@@ -22,6 +23,7 @@ from ._lib import check, lib, version
 from .attention import AttentionBackend, PagedAttention, PagedAttentionConfig, merge_states
 from .cache import PagedKVCache
 from .install import install, uninstall
+from .quant import QuantLinear, QuantLinearConfig
 from .rope import RotaryEmbedding, rope_kv_append
 from .step import DecodeStepState
 
@@ -34,6 +36,8 @@ __all__ = [
     "RotaryEmbedding",
     "rope_kv_append",
     "DecodeStepState",
+    "QuantLinear",
+    "QuantLinearConfig",
     "install",
     "uninstall",
     "lib",

@@ -133,6 +133,12 @@ SIGNATURES = {
     "llmopt_paged_gather_scaled": [
         _p, _p, _i32, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32,
         _p, _i32, _i64, _i64, _p, _i32, _i64, _i64, _p, _p, _p, _p, _p],
+    "llmopt_quant_linear_workspace_size": [
+        ctypes.c_int, _i64, _i64, _i64, _i32, _i32, _i32, ctypes.POINTER(ctypes.c_size_t)],
+    "llmopt_quant_linear": [
+        _p, _i32, _i64, _i64, _p, _i32, _i32, _i32, _p, _p, _i64, _i64, _p, _p, _i64,
+        _p, ctypes.c_size_t, _p],
+    "llmopt_dequantize": [_p, _i32, _i32, _i32, _p, _p, _i64, _i64, _p, _i32, _p],
 }
 
 DTYPE_E4M3 = 3

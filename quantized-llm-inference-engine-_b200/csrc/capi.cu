@@ -722,6 +722,127 @@ int llmopt_paged_attention_gather(
                     split_tokens, workspace, workspace_bytes, err, stream, phases, &p);
 }
 
+// ---- weight-only quantized linear ---------------------------------------------
+namespace {
+
+// Checks shared by the quantized-linear entry points; fills the kernel args.
+int quant_args(const void* qweight, int32_t bits, int32_t group_size, int32_t symmetric,
+               const float* scales, const float* zeros, int64_t n, int64_t k,
+               QuantLinearArgs* a) {
+  if (bits != 2 && bits != 4 && bits != 8) {
+    return fail(LLMOPT_ERR_UNSUPPORTED, "bits must be 2, 4 or 8 (got %d)", bits);
+  }
+  if (n < 1 || k < 1 || group_size < 1 || k % group_size != 0 || (bits < 8 && k % 2 != 0)) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT,
+                "invalid shape: n=%lld k=%lld group_size=%d (k must be a multiple of the "
+                "group size, and even for 2/4-bit codes)",
+                (long long)n, (long long)k, group_size);
+  }
+  if (qweight == nullptr || scales == nullptr || (!symmetric && zeros == nullptr)) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null pointer argument");
+  }
+  *a = QuantLinearArgs{};
+  a->qweight = static_cast<const unsigned char*>(qweight);
+  a->bits = bits;
+  a->group = group_size;
+  a->symmetric = symmetric ? 1 : 0;
+  a->scales = scales;
+  a->zeros = zeros;
+  a->n = n;
+  a->k = k;
+  return LLMOPT_OK;
+}
+
+// Split of the k range (whole 128-column tiles) for the tensor-core path.
+void plan_quant_splits(QuantLinearArgs* a, int sms) {
+  a->splits = 1;
+  a->k_per_split = a->k;
+  if (!quant_linear_tc_supported(*a)) return;
+  const long long tiles = a->k / 128;
+  const int want = quant_linear_splits(*a, sms);
+  const long long per = (tiles + want - 1) / want;
+  a->k_per_split = per * 128;
+  a->splits = (int)((tiles + per - 1) / per);
+}
+
+}  // namespace
+
+int llmopt_quant_linear_workspace_size(int device, int64_t m, int64_t n, int64_t k,
+                                       int32_t bits, int32_t group_size, int32_t x_dtype,
+                                       size_t* bytes) {
+  if (bytes == nullptr) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "bytes is null");
+  *bytes = 0;
+  if (m < 0) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "m < 0");
+  if (!valid_dtype(x_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype %d", x_dtype);
+  QuantLinearArgs a{};
+  static const float kDummy[4] = {};
+  const int st = quant_args(kDummy, bits, group_size, 1, kDummy, kDummy, n, k, &a);
+  if (st != LLMOPT_OK) return st;
+  if (m == 0) return ok();
+  // Size for 16-byte aligned operands (an unaligned call runs without splits).
+  alignas(16) static const unsigned char kAligned[16] = {};
+  a.x = kAligned;
+  a.qweight = kAligned;
+  a.x_dtype = x_dtype;
+  a.m = m;
+  a.ldx = k;
+  plan_quant_splits(&a, sm_count_of(device));
+  if (a.splits > 1) *bytes = (size_t)a.splits * (size_t)m * (size_t)n * sizeof(float);
+  return ok();
+}
+
+int llmopt_quant_linear(const void* x, int32_t x_dtype, int64_t m, int64_t ldx,
+                        const void* qweight, int32_t bits, int32_t group_size,
+                        int32_t symmetric, const float* scales, const float* zeros, int64_t n,
+                        int64_t k, const void* bias, void* out, int64_t ldo, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!valid_dtype(x_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype %d", x_dtype);
+  QuantLinearArgs a{};
+  int st = quant_args(qweight, bits, group_size, symmetric, scales, zeros, n, k, &a);
+  if (st != LLMOPT_OK) return st;
+  if (m < 0 || ldx < k || ldo < n) {
+    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid shape: m=%lld ldx=%lld ldo=%lld",
+                (long long)m, (long long)ldx, (long long)ldo);
+  }
+  if (m == 0) return ok();
+  if (x == nullptr || out == nullptr) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null pointer argument");
+  a.x = x;
+  a.x_dtype = x_dtype;
+  a.m = m;
+  a.ldx = ldx;
+  a.bias = bias;
+  a.out = out;
+  a.ldo = ldo;
+  plan_quant_splits(&a, sm_count_of(current_device()));
+  if (a.splits > 1) {
+    const size_t need = (size_t)a.splits * (size_t)m * (size_t)n * sizeof(float);
+    if (workspace == nullptr || workspace_bytes < need) {
+      return fail(LLMOPT_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed", workspace_bytes,
+                  need);
+    }
+    if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0) {
+      return fail(LLMOPT_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+    }
+    a.partial = static_cast<float*>(workspace);
+  }
+  cudaError_t e = quant_linear_launch(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "quant_linear launch");
+  return ok();
+}
+
+int llmopt_dequantize(const void* qweight, int32_t bits, int32_t group_size, int32_t symmetric,
+                      const float* scales, const float* zeros, int64_t n, int64_t k, void* out,
+                      int32_t out_dtype, void* stream) {
+  if (!valid_dtype(out_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype %d", out_dtype);
+  QuantLinearArgs a{};
+  int st = quant_args(qweight, bits, group_size, symmetric, scales, zeros, n, k, &a);
+  if (st != LLMOPT_OK) return st;
+  if (out == nullptr) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "null pointer argument");
+  cudaError_t e = dequantize_launch(a, out, out_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dequantize launch");
+  return ok();
+}
+
 int llmopt_merge_states(const void* o1, const void* o2, const void* l1, const void* l2,
                         void* out, void* lse_out, int64_t rows, int32_t head_dim,
                         int32_t o_dtype, int32_t lse_dtype, void* stream) {

@@ -195,6 +195,30 @@ struct StepArgs {
 };
 cudaError_t step_advance_launch(const StepArgs& a, cudaStream_t stream);
 
+// Weight-only quantized linear (quant_linear.cu): out = x W^T + bias with W as
+// packed codes + per-group fp32 scales / zeros (the reference's QuantizedTensor).
+struct QuantLinearArgs {
+  const void* x;                   // [m, k] compute dtype, row stride ldx
+  int x_dtype;
+  long long m, ldx;
+  const unsigned char* qweight;    // [n, k/2] (2/4-bit, nibbles) or [n, k] (8-bit)
+  int bits, group, symmetric;
+  const float* scales;             // [n, k / group]
+  const float* zeros;
+  long long n, k;
+  const void* bias;                // [n] compute dtype, or null
+  void* out;                       // [m, n] compute dtype, row stride ldo
+  long long ldo;
+  float* partial;                  // [splits, m, n] when the k range is split, else null
+  int splits;
+  long long k_per_split;           // multiple of 128
+};
+bool quant_linear_tc_supported(const QuantLinearArgs& a);
+int quant_linear_splits(const QuantLinearArgs& a, int sm_count);
+cudaError_t quant_linear_launch(const QuantLinearArgs& a, cudaStream_t stream);
+cudaError_t dequantize_launch(const QuantLinearArgs& a, void* out, int out_dtype,
+                              cudaStream_t stream);
+
 struct GatherArgs {
   const void* k_cache;
   const void* v_cache;

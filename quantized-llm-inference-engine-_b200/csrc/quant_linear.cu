@@ -1,0 +1,503 @@
+// Weight-only quantized linear layer: y = x W^T + b with W held as packed
+// 2/4/8-bit codes plus per-group float32 scales and zero points.
+//
+// Replaces QuantLinear.forward (src/llmopt/quantization/quant_linear.py:93-113),
+// which dequantizes the whole weight to the compute dtype (quantizers.py:203-239),
+// caches that dense copy and calls F.linear.  Here the codes are read and
+// dequantized on the fly by every call, so a forward streams bits/16 of the
+// bytes of a 16-bit weight and no dense copy is kept.
+//
+// Storage (the reference's): qweight uint8 [n, k/2] for 2- and 4-bit codes
+// (two per byte, the even column in the low nibble; symmetric codes biased by
+// 2^(bits-1)), uint8 [n, k] for asymmetric 8-bit, int8 [n, k] for symmetric
+// 8-bit; scales / zeros float32 [n, k / group].  Dequantized value:
+// (q - 2^(bits-1)) * s (symmetric, sub-byte), q * s (symmetric 8-bit),
+// (q - z) * s (asymmetric), in float32, then cast to the compute dtype.
+//
+// Kernels:
+// * wq_dequant_kernel: the dense weight in the compute dtype, bit-exact with the
+//   reference's dequantize.
+// * wq_gemm_kernel (f16 / bf16, k % 128 == 0, n % 64 == 0, group 32, 64, 128 or
+//   a multiple of 128):
+//   tensor cores.  A CTA owns 64 output features (four warps of 16) and 32
+//   tokens (8 when a call has at most 8); a 4-stage cp.async ring brings each 128-column tile's codes,
+//   token rows and group constants into shared memory, and each warp
+//   dequantizes its 16 rows in registers into m16n8k16 A fragments (weight
+//   rows = M, tokens = N: decode batches need no padding to 16 rows).  2- and
+//   4-bit codes become 16-bit pairs by one LOP3 each (a nibble in the mantissa
+//   of 128.0 for bf16 / 1024.0 for f16, the magic-number trick), then an exact
+//   subtraction of (magic + zero) and a multiply by the scale split into two
+//   16-bit parts (one FMA, one rounding);
+//   8-bit codes go through float32 (exact), so their weights are bit-exact.
+//   The pairs come out as (code j, code j+4) of each 8-code chunk; the B
+//   fragments pair the token values the same way with byte permutes after a
+//   16-byte read of the chunk (token rows are stored swizzled, so the reads of
+//   a quarter warp hit eight bank groups).  The k range is split across CTAs
+//   when n and m alone do not fill the GPU; splits write fp32 partials that
+//   wq_reduce_kernel sums (with the bias) in a fixed order.
+// * wq_generic_kernel: CUDA cores, fp32 accumulation, any shape and dtype.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace llmopt {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kRows = 16 * kWarps;   // output features per CTA
+constexpr int kKT = 128;             // k per tile
+constexpr int kMT = 32;              // tokens per CTA, large batches (4 n-tiles of 8)
+constexpr int kMTSmall = 8;          // tokens per CTA up to 8 tokens (one n-tile)
+constexpr int kThreads = 32 * kWarps;
+constexpr int kChunks = kKT / 8;     // 8-element chunks per token row of a tile
+
+// Physical 16-byte chunk of logical chunk c in token row i of a staged tile.
+__device__ __forceinline__ int x_chunk(int i, int c) { return c ^ ((c >> 3) << 1) ^ (i & 1); }
+
+// code value of element e of a row (unpacked, before the offset)
+__device__ __forceinline__ float code_at(const QuantLinearArgs& a, long long row, long long e) {
+  if (a.bits == 8) {
+    const unsigned char b = a.qweight[row * a.k + e];
+    return a.symmetric ? (float)(signed char)b : (float)b;
+  }
+  const unsigned char b = a.qweight[row * (a.k / 2) + (e >> 1)];
+  return (float)((e & 1) ? (b >> 4) : (b & 0x0F));
+}
+
+// The reference's dequantized weight element in float32 (before the cast).
+__device__ __forceinline__ float dequant_at(const QuantLinearArgs& a, long long row, long long e) {
+  const long long gi = row * (a.k / a.group) + e / a.group;
+  const float q = code_at(a, row, e);
+  const float s = a.scales[gi];
+  if (a.symmetric) {
+    return __fmul_rn(a.bits < 8 ? q - (float)(1 << (a.bits - 1)) : q, s);
+  }
+  return __fmul_rn(q - a.zeros[gi], s);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256) wq_dequant_kernel(const QuantLinearArgs a, void* out) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const long long total = a.n * a.k;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    store_f32<DT>(out, i, dequant_at(a, i / a.k, i % a.k));
+  }
+}
+
+// CUDA cores: a CTA computes 16 tokens x 64 features; the weight tile is
+// dequantized (rounded to the compute dtype, as the reference's dense copy)
+// into shared memory once per 32-column step.
+template <int DT>
+__global__ void __launch_bounds__(256) wq_generic_kernel(const QuantLinearArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  constexpr int TM = 16, TN = 64, TK = 32;
+  __shared__ float ws[TN][TK + 1];
+  __shared__ float xs[TM][TK + 1];
+  const long long m0 = (long long)blockIdx.y * TM;
+  const long long n0 = (long long)blockIdx.x * TN;
+  const int tid = threadIdx.x;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};     // (token tid / 16, features 4 * (tid % 16) + j)
+  const int ti = tid >> 4;
+  const int fj = (tid & 15) * 4;
+  for (long long k0 = 0; k0 < a.k; k0 += TK) {
+    for (int idx = tid; idx < TN * TK; idx += 256) {
+      const int r = idx / TK, c = idx % TK;
+      float v = 0.f;
+      if (n0 + r < a.n && k0 + c < a.k) v = round_through<DT>(dequant_at(a, n0 + r, k0 + c));
+      ws[r][c] = v;
+    }
+    for (int idx = tid; idx < TM * TK; idx += 256) {
+      const int r = idx / TK, c = idx % TK;
+      float v = 0.f;
+      if (m0 + r < a.m && k0 + c < a.k) v = load_f32<DT>(a.x, (m0 + r) * a.ldx + k0 + c);
+      xs[r][c] = v;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int c = 0; c < TK; ++c) {
+      const float xv = xs[ti][c];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = fmaf(xv, ws[fj + j][c], acc[j]);
+    }
+    __syncthreads();
+  }
+  const long long tok = m0 + ti;
+  if (tok < a.m) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const long long f = n0 + fj + j;
+      if (f < a.n) {
+        float v = acc[j];
+        if (a.bias != nullptr) v += load_f32<DT>(a.bias, f);
+        store_f32<DT>(a.out, tok * a.ldo + f, v);
+      }
+    }
+  }
+}
+
+// 16-bit pair type of the compute dtype, and its magic-number constants.
+template <int DT> struct Pair;
+template <> struct Pair<kBF16> {
+  using T = __nv_bfloat162;
+  static constexpr uint32_t kMagic = 0x43004300u;   // 128.0 in both halves
+  static constexpr float kBase = 128.f;
+  __device__ static T splat(float v) { return __floats2bfloat162_rn(v, v); }
+  __device__ static T pack(float lo, float hi) { return __floats2bfloat162_rn(lo, hi); }
+  __device__ static float low_as_float(T v) { return __low2float(v); }
+};
+template <> struct Pair<kF16> {
+  using T = __half2;
+  static constexpr uint32_t kMagic = 0x64006400u;   // 1024.0 in both halves
+  static constexpr float kBase = 1024.f;
+  __device__ static T splat(float v) { return __floats2half2_rn(v, v); }
+  __device__ static T pack(float lo, float hi) { return __floats2half2_rn(lo, hi); }
+  __device__ static float low_as_float(T v) { return __low2float(v); }
+};
+
+template <class T>
+__device__ __forceinline__ uint32_t as_u32(const T& v) {
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <class T>
+__device__ __forceinline__ T from_u32(uint32_t u) {
+  return *reinterpret_cast<const T*>(&u);
+}
+
+// Dequantized pairs (code j, code j+4), j = 0..3, of the 8-code chunk `word`
+// (sub-byte codes: 8 nibbles).  d = (magic + q) - (magic + z) is exact; the
+// scale is split into a 16-bit head and a 16-bit residual (s = hi + lo to ~16
+// bits) and w = fma(d, hi, d * lo) rounds once, like the reference's float32
+// product rounded to the compute dtype, instead of carrying the scale's own
+// rounding error into every weight of the group.
+template <int DT>
+__device__ __forceinline__ void dequant_chunk4(uint32_t word, typename Pair<DT>::T off2,
+                                               typename Pair<DT>::T s_hi,
+                                               typename Pair<DT>::T s_lo, uint32_t (&p)[4]) {
+  using P = Pair<DT>;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t h = ((word >> (4 * j)) & 0x000F000Fu) | P::kMagic;
+    const typename P::T d = __hsub2(from_u32<typename P::T>(h), off2);
+    p[j] = as_u32(__hfma2(d, s_hi, __hmul2(d, s_lo)));
+  }
+}
+
+// The same for 8-bit codes (two words: codes 0-3 and 4-7), exact in float32.
+template <int DT>
+__device__ __forceinline__ void dequant_chunk8(uint32_t w0, uint32_t w1, uint32_t flip,
+                                               float zoff, float s, uint32_t (&p)[4]) {
+  using P = Pair<DT>;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t b0 = ((w0 >> (8 * j)) & 0xFFu) ^ flip;
+    const uint32_t b1 = ((w1 >> (8 * j)) & 0xFFu) ^ flip;
+    const float f0 = __fmul_rn(__int_as_float(0x4B000000 | b0) - zoff, s);
+    const float f1 = __fmul_rn(__int_as_float(0x4B000000 | b1) - zoff, s);
+    p[j] = as_u32(P::pack(f0, f1));
+  }
+}
+
+// 16-byte global -> shared copy, L2 only (cp.async.cg); `bytes` of the source
+// (0 or 16) are read, the rest of the 16 filled with zeros.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)),
+               "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+constexpr int kStages = 4;
+constexpr int kMaxGroupsPerTile = kKT / 32;
+
+// One pipeline stage: the CTA's codes, token tile and group constants of one
+// 128-column tile (MT tokens).
+template <int BITS, int MT>
+struct Stage {
+  static constexpr int kRowBytes = BITS == 8 ? kKT : kKT / 2;
+  unsigned char w[kRows][kRowBytes];        // codes of the CTA's 64 rows
+  uint4 x[MT][kChunks];                     // token rows, chunks swizzled by x_chunk()
+  float s[kRows][kMaxGroupsPerTile];        // scales of the tile's groups
+  float z[kRows][kMaxGroupsPerTile];        // zero points (asymmetric)
+};
+
+template <int DT, int BITS, int MT>
+__global__ void __launch_bounds__(kThreads) wq_gemm_kernel(const QuantLinearArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  using P = Pair<DT>;
+  using S = Stage<BITS, MT>;
+  constexpr int NT = MT / 8;                                   // 8-token n-tiles
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  S* st = reinterpret_cast<S*>(smem_raw);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int gid = lane >> 2;
+  const int tid4 = lane & 3;
+  const long long rbase = (long long)blockIdx.x * kRows;       // the CTA's first row
+  const int wrow = warp * 16 + gid;                            // this lane's rows: wrow, +8
+  const long long m0 = (long long)blockIdx.z * MT;
+  const long long kb = (long long)blockIdx.y * a.k_per_split;
+  const long long ke = kb + a.k_per_split < a.k ? kb + a.k_per_split : a.k;
+  const int ntiles = (int)((ke - kb) / kKT);
+  const long long mrem = a.m - m0;
+  const int n_tiles = mrem >= MT ? NT : (int)((mrem + 7) / 8);   // useful 8-token n-tiles
+  const long long groups = a.k / a.group;
+  const int gpt = a.group >= kKT ? 1 : kKT / a.group;            // groups per tile (<= 4)
+  const long long row_bytes = BITS == 8 ? a.k : a.k / 2;
+
+  // Stage t <- codes, token tile and group constants of tile t (all threads).
+  auto issue = [&](int t) {
+    S& s = st[t % kStages];
+    const long long k0 = kb + (long long)t * kKT;
+    constexpr int wchunks = kRows * S::kRowBytes / 16;           // 16-byte pieces of codes
+    for (int i = threadIdx.x; i < wchunks; i += kThreads) {
+      const int r = i / (S::kRowBytes / 16), c = i % (S::kRowBytes / 16);
+      cp_async16(&s.w[r][16 * c],
+                 a.qweight + (rbase + r) * row_bytes + (BITS == 8 ? k0 : k0 / 2) + 16 * c, 16);
+    }
+    for (int i = threadIdx.x; i < MT * kChunks; i += kThreads) {
+      const int r = i / kChunks, c = i % kChunks;
+      const bool ok = m0 + r < a.m;
+      const unsigned short* src = static_cast<const unsigned short*>(a.x) +
+                                  (ok ? (m0 + r) * a.ldx + k0 + 8 * c : 0);
+      cp_async16(&s.x[r][x_chunk(r, c)], src, ok ? 16 : 0);
+    }
+    const long long g0 = k0 / a.group;
+    for (int i = threadIdx.x; i < kRows * gpt; i += kThreads) {
+      const int r = i / gpt, j = i % gpt;
+      cp_async4(&s.s[r][j], a.scales + (rbase + r) * groups + g0 + j);
+      if (!a.symmetric) cp_async4(&s.z[r][j], a.zeros + (rbase + r) * groups + g0 + j);
+    }
+  };
+
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+
+#pragma unroll
+  for (int t = 0; t < kStages - 1; ++t) {
+    if (t < ntiles) issue(t);
+    cp_async_commit();
+  }
+  // symmetric sub-byte codes carry the 2^(bits-1) bias (2- and 4-bit share the
+  // nibble layout, so the width comes from the arguments)
+  const float zsym = BITS < 8 ? (float)(1 << (a.bits - 1)) : 0.f;
+
+  for (int t = 0; t < ntiles; ++t) {
+    cp_async_wait<kStages - 2>();
+    __syncthreads();                       // tile t landed; tile t-1's stage is free
+    if (t + kStages - 1 < ntiles) issue(t + kStages - 1);
+    cp_async_commit();
+    const S& s = st[t % kStages];
+    // this lane's 32 codes of each row lie in group j = (32 t4) / group of the tile
+    const int j = a.group >= kKT ? 0 : (32 * tid4) / a.group;
+    // the lane's codes of rows wrow and wrow + 8 (16-byte reads: a quarter warp
+    // covers 128 contiguous bytes) and their group constants
+    constexpr int kCw = BITS == 8 ? 2 : 1;
+    uint4 cw[2][kCw];
+    float sf[2], zf[2];
+    typename P::T shi[2], slo[2], off2[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = wrow + 8 * h;
+#pragma unroll
+      for (int q = 0; q < kCw; ++q) {
+        cw[h][q] = *reinterpret_cast<const uint4*>(&s.w[r][(BITS == 8 ? 32 : 16) * tid4 + 16 * q]);
+      }
+      sf[h] = s.s[r][j];
+      zf[h] = a.symmetric ? zsym : s.z[r][j];
+      shi[h] = P::splat(sf[h]);
+      slo[h] = P::splat(sf[h] - P::low_as_float(shi[h]));
+      off2[h] = P::splat(P::kBase + zf[h]);
+    }
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {          // chunk 4 t4 + w: k-steps 2w, 2w + 1
+      uint32_t pa[2][4];                   // [row half][pair (code i, code i+4)]
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if constexpr (BITS == 8) {
+          // codes 8w .. 8w+7: words 2w and 2w + 1 of the lane's 32 bytes
+          const uint4& c = cw[h][w >> 1];
+          const uint32_t w0 = (w & 1) ? c.z : c.x;
+          const uint32_t w1 = (w & 1) ? c.w : c.y;
+          const uint32_t flip = a.symmetric ? 0x80u : 0u;
+          const float zoff = 8388608.f + (a.symmetric ? 128.f : zf[h]);
+          dequant_chunk8<DT>(w0, w1, flip, zoff, sf[h], pa[h]);
+        } else {
+          const uint4& c = cw[h][0];
+          const uint32_t cwv = w == 0 ? c.x : w == 1 ? c.y : w == 2 ? c.z : c.w;
+          dequant_chunk4<DT>(cwv, off2[h], shi[h], slo[h], pa[h]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (nt < n_tiles) {
+          const int i = nt * 8 + gid;
+          const uint4 xv = s.x[i][x_chunk(i, 4 * tid4 + w)];     // x0..x7 of the chunk
+          // pair (x_i, x_i+4) as the codes: (x0 x4) (x1 x5) (x2 x6) (x3 x7)
+          const uint32_t b[4] = {__byte_perm(xv.x, xv.z, 0x5410), __byte_perm(xv.x, xv.z, 0x7632),
+                                 __byte_perm(xv.y, xv.w, 0x5410), __byte_perm(xv.y, xv.w, 0x7632)};
+#pragma unroll
+          for (int hs = 0; hs < 2; ++hs) {   // k-step 2w + hs: pairs 2hs (a0/a1), 2hs+1 (a2/a3)
+            const uint32_t af[4] = {pa[0][2 * hs], pa[1][2 * hs], pa[0][2 * hs + 1],
+                                    pa[1][2 * hs + 1]};
+            mma_16816<DT>(acc[nt], af, b[2 * hs], b[2 * hs + 1]);
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  // c-fragment e of n-tile nt: feature wrow + 8 (e >> 1), token m0 + 8 nt + 2 t4 + (e & 1)
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const long long tok = m0 + nt * 8 + 2 * tid4 + (e & 1);
+      const long long f = rbase + wrow + 8 * (e >> 1);
+      if (tok >= a.m) continue;
+      if (a.partial != nullptr) {
+        a.partial[((long long)blockIdx.y * a.m + tok) * a.n + f] = acc[nt][e];
+      } else {
+        float v = acc[nt][e];
+        if (a.bias != nullptr) v += load_f32<DT>(a.bias, f);
+        store_f32<DT>(a.out, tok * a.ldo + f, v);
+      }
+    }
+  }
+}
+
+// Sum of the split partials (split order) plus the bias, cast to the compute dtype.
+template <int DT>
+__global__ void __launch_bounds__(256) wq_reduce_kernel(const QuantLinearArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const long long total = a.m * a.n;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    float v = 0.f;
+    for (int s = 0; s < a.splits; ++s) v += a.partial[(long long)s * total + i];
+    const long long tok = i / a.n, f = i % a.n;
+    if (a.bias != nullptr) v += load_f32<DT>(a.bias, f);
+    store_f32<DT>(a.out, tok * a.ldo + f, v);
+  }
+}
+
+template <int DT>
+const void* gemm_ptr(int bits, int mt) {
+  if (mt == kMTSmall) {
+    return bits == 8 ? reinterpret_cast<const void*>(&wq_gemm_kernel<DT, 8, kMTSmall>)
+                     : reinterpret_cast<const void*>(&wq_gemm_kernel<DT, 4, kMTSmall>);
+  }
+  return bits == 8 ? reinterpret_cast<const void*>(&wq_gemm_kernel<DT, 8, kMT>)
+                   : reinterpret_cast<const void*>(&wq_gemm_kernel<DT, 4, kMT>);
+}
+
+int tokens_per_cta(long long m) { return m <= kMTSmall ? kMTSmall : kMT; }
+
+size_t gemm_smem(int bits, int mt) {
+  if (mt == kMTSmall) {
+    return kStages * (bits == 8 ? sizeof(Stage<8, kMTSmall>) : sizeof(Stage<4, kMTSmall>));
+  }
+  return kStages * (bits == 8 ? sizeof(Stage<8, kMT>) : sizeof(Stage<4, kMT>));
+}
+
+const void* gemm_fn(const QuantLinearArgs& a) {
+  const int mt = tokens_per_cta(a.m);
+  return a.x_dtype == kBF16 ? gemm_ptr<kBF16>(a.bits, mt) : gemm_ptr<kF16>(a.bits, mt);
+}
+
+long long grid_blocks(long long work, int threads) {
+  long long b = (work + threads - 1) / threads;
+  if (b > 148LL * 32) b = 148LL * 32;
+  return b < 1 ? 1 : b;
+}
+
+}  // namespace
+
+bool quant_linear_tc_supported(const QuantLinearArgs& a) {
+  // groups tile the 128-column tiles: 32, 64, 128 or multiples of 128
+  const bool groups_ok = a.group % 32 == 0 && (kKT % a.group == 0 || a.group % kKT == 0);
+  return (a.x_dtype == kBF16 || a.x_dtype == kF16) && a.k % kKT == 0 && a.n % kRows == 0 &&
+         groups_ok && a.ldx % 8 == 0 &&
+         (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(a.qweight) & 15) == 0;
+}
+
+// Splits of the k range: about two full waves of CTAs at the kernel's
+// occupancy (one wave leaves a ragged tail when the tile count is not a
+// multiple of the slots; more splits cost partial traffic).
+int quant_linear_splits(const QuantLinearArgs& a, int sm_count) {
+  const int mt = tokens_per_cta(a.m);
+  const long long ctas = (a.n / kRows) * ((a.m + mt - 1) / mt);
+  const long long tiles = a.k / kKT;
+  const void* fn = gemm_fn(a);
+  const size_t smem = gemm_smem(a.bits, mt);
+  int occ = 1;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, smem) != cudaSuccess ||
+      occ < 1) {
+    occ = 1;
+  }
+  const long long slots = (long long)occ * sm_count;
+  long long splits = (2 * slots + ctas / 2) / (ctas > 0 ? ctas : 1);
+  if (splits > tiles) splits = tiles;
+  if (splits > 16) splits = 16;
+  if (splits < 1) splits = 1;
+  return (int)splits;
+}
+
+cudaError_t quant_linear_launch(const QuantLinearArgs& a, cudaStream_t stream) {
+  if (a.m <= 0 || a.n <= 0) return cudaSuccess;
+  void* args[] = {const_cast<QuantLinearArgs*>(&a)};
+  if (!quant_linear_tc_supported(a)) {
+    const void* fn = a.x_dtype == kBF16 ? reinterpret_cast<const void*>(&wq_generic_kernel<kBF16>)
+                     : a.x_dtype == kF16 ? reinterpret_cast<const void*>(&wq_generic_kernel<kF16>)
+                                         : reinterpret_cast<const void*>(&wq_generic_kernel<kF32>);
+    const long long gx = (a.n + 63) / 64, gy = (a.m + 15) / 16;
+    if (gx > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidConfiguration;
+    return launch_pdl(fn, dim3((unsigned)gx, (unsigned)gy), dim3(256), args, 0, stream);
+  }
+  const void* fn = gemm_fn(a);
+  const int mt = tokens_per_cta(a.m);
+  const long long gx = a.n / kRows, gz = (a.m + mt - 1) / mt;
+  if (gx > 0x7fffffffLL || gz > 65535 || a.splits > 65535) return cudaErrorInvalidConfiguration;
+  const size_t smem = gemm_smem(a.bits, mt);
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(fn, dim3((unsigned)gx, (unsigned)a.splits, (unsigned)gz), dim3(kThreads), args,
+                 smem, stream);
+  if (e != cudaSuccess || a.partial == nullptr) return e;
+  const void* rfn = a.x_dtype == kBF16 ? reinterpret_cast<const void*>(&wq_reduce_kernel<kBF16>)
+                                       : reinterpret_cast<const void*>(&wq_reduce_kernel<kF16>);
+  return launch_pdl(rfn, dim3((unsigned)grid_blocks(a.m * a.n, 256)), dim3(256), args, 0,
+                    stream);
+}
+
+cudaError_t dequantize_launch(const QuantLinearArgs& a, void* out, int out_dtype,
+                              cudaStream_t stream) {
+  if (a.n <= 0 || a.k <= 0) return cudaSuccess;
+  const void* fn = out_dtype == kBF16 ? reinterpret_cast<const void*>(&wq_dequant_kernel<kBF16>)
+                   : out_dtype == kF16 ? reinterpret_cast<const void*>(&wq_dequant_kernel<kF16>)
+                                       : reinterpret_cast<const void*>(&wq_dequant_kernel<kF32>);
+  void* args[] = {const_cast<QuantLinearArgs*>(&a), &out};
+  return launch_pdl(fn, dim3((unsigned)grid_blocks(a.n * a.k, 256)), dim3(256), args, 0,
+                    stream);
+}
+
+}  // namespace llmopt

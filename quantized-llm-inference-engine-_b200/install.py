@@ -12,7 +12,10 @@ prefix cache, ``BlockPool``) keeps working unchanged:
 * ``llmopt.cache.PagedKVCache`` and ``llmopt.cache.paged_cache.PagedKVCache``
   (``DecoderOnlyModel.allocate_cache`` imports it from there at call time,
   src/llmopt/model/modeling.py:133-147), plus the names imported by
-  ``llmopt.engine.llm_engine`` and ``llmopt.engine.model_runner``.
+  ``llmopt.engine.llm_engine`` and ``llmopt.engine.model_runner``;
+* ``QuantLinear`` / ``QuantLinearConfig`` in ``llmopt.quantization`` and
+  ``llmopt.quantization.quant_linear`` (``quantize_model_`` builds its layers
+  with ``QuantLinear.from_float``, quant_linear.py:199-201).
 
 Install before building the engine; ``uninstall(token)`` restores the originals.
 """
@@ -24,6 +27,7 @@ import sys
 
 from .attention import PagedAttention, merge_states
 from .cache import PagedKVCache
+from .quant import QuantLinear, QuantLinearConfig
 
 #: (module, attribute, replacement)
 _TARGETS = (
@@ -36,6 +40,10 @@ _TARGETS = (
     ("llmopt.cache.paged_cache", "PagedKVCache", PagedKVCache),
     ("llmopt.engine.llm_engine", "PagedKVCache", PagedKVCache),
     ("llmopt.engine.model_runner", "PagedKVCache", PagedKVCache),
+    ("llmopt.quantization", "QuantLinear", QuantLinear),
+    ("llmopt.quantization", "QuantLinearConfig", QuantLinearConfig),
+    ("llmopt.quantization.quant_linear", "QuantLinear", QuantLinear),
+    ("llmopt.quantization.quant_linear", "QuantLinearConfig", QuantLinearConfig),
 )
 
 

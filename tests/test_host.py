@@ -152,6 +152,18 @@ def test_install_rebinds_the_reference_hot_path(pkg):
             assert llmopt.attention.merge_states is pkg.merge_states
             assert llmopt.cache.paged_cache.PagedKVCache is pkg.PagedKVCache
             assert llmopt.engine.llm_engine.PagedKVCache is pkg.PagedKVCache
+            import llmopt.quantization.quant_linear as ql
+
+            assert ql.QuantLinear is pkg.QuantLinear
+            assert llmopt.quantization.QuantLinear is pkg.QuantLinear
+            # quantize_model_ now builds the B200 layer (its from_float runs on CPU)
+            import torch
+            from torch import nn
+
+            model = nn.Sequential(nn.Linear(128, 64), nn.ReLU(), nn.Linear(64, 32))
+            ql.quantize_model_(model, bits=4, group_size=64)
+            assert sum(isinstance(m, pkg.QuantLinear) for m in model.modules()) == 2
+            assert model[0].qweight.dtype == torch.uint8 and model[0].qweight.shape == (64, 64)
             # The reference's own config object is accepted by our attention.
             from llmopt.attention.paged_attention import PagedAttentionConfig as RefCfg
 
@@ -246,3 +258,67 @@ def test_gather_and_peer_entries_reject_bad_arguments(pkg):
     assert lib.llmopt_peer_alloc(0, 64, None, handle) == 1                  # no output slot
     assert lib.llmopt_peer_open(0, None, ctypes.byref(ptr)) == 1            # no handle
     assert lib.llmopt_peer_close(0, None) == 0 and lib.llmopt_peer_free(0, None) == 0
+
+
+def _packed_layer(pkg, bits=4, group=64, symmetric=True, n=32, k=128):
+    """A QuantLinear built from a stand-in of the reference's QuantizedTensor."""
+    from types import SimpleNamespace
+
+    import numpy as np
+    import torch
+
+    from oracle import quant_oracle as qo
+
+    rng = np.random.default_rng(0)
+    w = rng.standard_normal((n, k)).astype(np.float32) * 0.05
+    s, z = qo.choose_qparams(w, bits, group, symmetric)
+    codes = qo.quantize_to_codes(w, s, z, bits, group, symmetric)
+    qt = SimpleNamespace(qweight=torch.from_numpy(codes if bits == 8 else qo.pack_int4(codes)),
+                         scales=torch.from_numpy(s), zeros=torch.from_numpy(z), bits=bits,
+                         group_size=group, symmetric=symmetric)
+    lin = torch.nn.Linear(k, n)
+    return pkg.QuantLinear.from_float(lin, qt, compute_dtype=torch.bfloat16), lin
+
+
+def test_quant_linear_mirrors_the_reference_layer(pkg):
+    import torch
+
+    layer, lin = _packed_layer(pkg)
+    assert layer.config.bits == 4 and layer.config.group_size == 64
+    assert layer.config.compute_dtype == torch.bfloat16
+    assert layer.scales.shape == (32, 2) and layer.qzeros.shape == (32, 2)
+    assert torch.equal(layer.bias.data, lin.bias.data)
+    assert layer.extra_repr() == "in_features=128, out_features=32, bits=4, bias=True"
+    assert "qweight" not in dict(layer.named_buffers())   # a plain attribute, as the reference
+    layer.invalidate()
+    # no CPU path: a CPU input fails loudly instead of falling back
+    with pytest.raises(RuntimeError, match="CUDA"):
+        layer(torch.zeros(2, 128, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError, match="quantized weight"):
+        pkg.QuantLinear(128, 32)._operands(torch.device("cpu"))
+
+
+def test_quant_linear_entry_points_validate_arguments(lib):
+    import ctypes
+
+    n = ctypes.c_size_t(0)
+    # 4096 x 4096 int4, 64 tokens: a split-k workspace is reported
+    assert lib.llmopt_quant_linear_workspace_size(0, 64, 4096, 4096, 4, 128, 2,
+                                                  ctypes.byref(n)) == 0
+    assert n.value % (64 * 4096 * 4) == 0
+    assert lib.llmopt_quant_linear_workspace_size(0, 0, 4096, 4096, 4, 128, 2,
+                                                  ctypes.byref(n)) == 0 and n.value == 0
+    assert lib.llmopt_quant_linear_workspace_size(0, 8, 64, 128, 3, 64, 2, ctypes.byref(n)) == 2
+    assert lib.llmopt_quant_linear_workspace_size(0, 8, 64, 100, 4, 64, 2, ctypes.byref(n)) == 1
+    dummy = ctypes.c_void_p(16)
+    # bad bit width, group not dividing k, missing zeros for an asymmetric grid
+    assert lib.llmopt_quant_linear(dummy, 2, 4, 128, dummy, 3, 64, 1, dummy, None, 32, 128,
+                                   None, dummy, 32, None, 0, None) == 2
+    assert lib.llmopt_quant_linear(dummy, 2, 4, 128, dummy, 4, 48, 1, dummy, None, 32, 128,
+                                   None, dummy, 32, None, 0, None) == 1
+    assert lib.llmopt_quant_linear(dummy, 2, 4, 128, dummy, 4, 64, 0, dummy, None, 32, 128,
+                                   None, dummy, 32, None, 0, None) == 1
+    assert lib.llmopt_dequantize(dummy, 4, 64, 1, dummy, None, 32, 128, dummy, 7, None) == 2
+    # m == 0 is a no-op
+    assert lib.llmopt_quant_linear(dummy, 2, 0, 128, dummy, 4, 64, 1, dummy, None, 32, 128,
+                                   None, dummy, 32, None, 0, None) == 0
