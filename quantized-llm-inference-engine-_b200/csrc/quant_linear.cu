@@ -259,27 +259,72 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_kernel(const QuantLinearArgs
   const long long row_bytes = BITS == 8 ? a.k : a.k / 2;
 
   // Stage t <- codes, token tile and group constants of tile t (all threads).
+  // A thread's copy slots are the same for every tile: their shared-memory
+  // offsets and global addresses are set up once, and a tile only adds its
+  // column offset.
+  constexpr int kWPieces = kRows * S::kRowBytes / 16;           // 16-byte pieces of codes
+  constexpr int kWPer = (kWPieces + kThreads - 1) / kThreads;
+  constexpr int kXPer = (MT * kChunks + kThreads - 1) / kThreads;
+  const unsigned char* wsrc[kWPer];
+  int wdst[kWPer];
+#pragma unroll
+  for (int q = 0; q < kWPer; ++q) {
+    const int i = threadIdx.x + q * kThreads;
+    const int r = i / (S::kRowBytes / 16), c = i % (S::kRowBytes / 16);
+    wsrc[q] = a.qweight + (rbase + r) * row_bytes + 16 * c;
+    wdst[q] = (int)(reinterpret_cast<const unsigned char*>(&st[0].w[r][16 * c]) -
+                    reinterpret_cast<const unsigned char*>(&st[0]));
+  }
+  const unsigned short* xsrc[kXPer];
+  int xdst[kXPer], xbytes[kXPer];
+#pragma unroll
+  for (int q = 0; q < kXPer; ++q) {
+    const int i = threadIdx.x + q * kThreads;
+    const int r = i / kChunks, c = i % kChunks;
+    const bool ok = i < MT * kChunks && m0 + r < a.m;
+    xsrc[q] = static_cast<const unsigned short*>(a.x) + (ok ? (m0 + r) * a.ldx + kb + 8 * c : 0);
+    xbytes[q] = ok ? 16 : 0;
+    xdst[q] = i < MT * kChunks
+                  ? (int)(reinterpret_cast<const unsigned char*>(&st[0].x[r][x_chunk(r, c)]) -
+                          reinterpret_cast<const unsigned char*>(&st[0]))
+                  : -1;
+  }
+  // group constants: kRows * gpt entries (up to 256: two per thread)
+  constexpr int kGPer = (kRows * kMaxGroupsPerTile + kThreads - 1) / kThreads;
+  bool has_g[kGPer];
+  int gr[kGPer], gj[kGPer];
+  const float* ssrc[kGPer];
+  const float* zsrc[kGPer];
+#pragma unroll
+  for (int q = 0; q < kGPer; ++q) {
+    const int i = threadIdx.x + q * kThreads;
+    has_g[q] = i < kRows * gpt;
+    gr[q] = has_g[q] ? i / gpt : 0;
+    gj[q] = has_g[q] ? i % gpt : 0;
+    ssrc[q] = a.scales + (rbase + gr[q]) * groups + gj[q];
+    zsrc[q] = a.zeros != nullptr ? a.zeros + (rbase + gr[q]) * groups + gj[q] : nullptr;
+  }
   auto issue = [&](int t) {
-    S& s = st[t % kStages];
+    unsigned char* base = reinterpret_cast<unsigned char*>(&st[t % kStages]);
     const long long k0 = kb + (long long)t * kKT;
-    constexpr int wchunks = kRows * S::kRowBytes / 16;           // 16-byte pieces of codes
-    for (int i = threadIdx.x; i < wchunks; i += kThreads) {
-      const int r = i / (S::kRowBytes / 16), c = i % (S::kRowBytes / 16);
-      cp_async16(&s.w[r][16 * c],
-                 a.qweight + (rbase + r) * row_bytes + (BITS == 8 ? k0 : k0 / 2) + 16 * c, 16);
+    const long long wk = BITS == 8 ? k0 : k0 / 2;
+#pragma unroll
+    for (int q = 0; q < kWPer; ++q) {
+      if (threadIdx.x + q * kThreads < kWPieces) cp_async16(base + wdst[q], wsrc[q] + wk, 16);
     }
-    for (int i = threadIdx.x; i < MT * kChunks; i += kThreads) {
-      const int r = i / kChunks, c = i % kChunks;
-      const bool ok = m0 + r < a.m;
-      const unsigned short* src = static_cast<const unsigned short*>(a.x) +
-                                  (ok ? (m0 + r) * a.ldx + k0 + 8 * c : 0);
-      cp_async16(&s.x[r][x_chunk(r, c)], src, ok ? 16 : 0);
+    const long long xk = (long long)t * kKT;
+#pragma unroll
+    for (int q = 0; q < kXPer; ++q) {
+      if (xdst[q] >= 0) cp_async16(base + xdst[q], xsrc[q] + (xbytes[q] ? xk : 0), xbytes[q]);
     }
     const long long g0 = k0 / a.group;
-    for (int i = threadIdx.x; i < kRows * gpt; i += kThreads) {
-      const int r = i / gpt, j = i % gpt;
-      cp_async4(&s.s[r][j], a.scales + (rbase + r) * groups + g0 + j);
-      if (!a.symmetric) cp_async4(&s.z[r][j], a.zeros + (rbase + r) * groups + g0 + j);
+    S& s = *reinterpret_cast<S*>(base);
+#pragma unroll
+    for (int q = 0; q < kGPer; ++q) {
+      if (has_g[q]) {
+        cp_async4(&s.s[gr[q]][gj[q]], ssrc[q] + g0);
+        if (!a.symmetric) cp_async4(&s.z[gr[q]][gj[q]], zsrc[q] + g0);
+      }
     }
   };
 
