@@ -1149,8 +1149,6 @@ def run_quant(args) -> None:
     pkg = importlib.import_module(PACKAGE)
     from types import SimpleNamespace
 
-    from oracle.quant_oracle import weight_bytes
-
     group, bits = 128, 4
     g = torch.Generator(device=dev)
     g.manual_seed(4000)
@@ -1197,7 +1195,9 @@ def run_quant(args) -> None:
             iters = max(10, min(args.steps, 50))
             ms_q = timed(lambda: layer(x), iters)
             ms_d = timed(lambda: torch.nn.functional.linear(x, dense), iters)
-            wb = weight_bytes(n, k, bits, group) + 2 * m * (k + n)
+            # algorithmic bytes: packed codes + fp32 scales (symmetric: no zeros
+            # are read) + the bf16 input and output rows
+            wb = n * k * bits // 8 + 4 * n * (k // group) + 2 * m * (k + n)
             db = n * k * 2 + 2 * m * (k + n)
             rows.append({"k": k, "n": n, "tokens": m,
                          "quant_ms": round(ms_q, 5), "dense_bf16_ms": round(ms_d, 5),
