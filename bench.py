@@ -1218,7 +1218,7 @@ def run_quant(args) -> None:
         "rows": rows,
         "roofline": {"bound": "hbm", "achieved": top["quant_GBps"], "peak": peak,
                      "unit": "GB/s", "frac": top["quant_frac_of_hbm"],
-                     "kernel": "wq_gemm_kernel", "peak_kind": f"{peak_kind} hbm_gbs"},
+                     "kernel": "wq_gemm_acc_kernel", "peak_kind": f"{peak_kind} hbm_gbs"},
     }), flush=True)
 
 

@@ -435,12 +435,15 @@ LLMOPT_API int llmopt_paged_gather_scaled(const void* key_cache, const void* val
  * The weight element is (q - offset) * s or (q - z) * s in float32 rounded to
  * the compute dtype, as the reference's dequantize.  16-bit compute dtypes
  * with k % 128 == 0, n % 64 == 0, group_size 32, 64, 128 or a multiple of
- * 128, and 16-byte aligned x / qweight run on tensor cores (2- and 4-bit codes
- * are scaled there in 16-bit arithmetic with the scale split into two 16-bit
- * parts and one rounding, which matches the reference's float32 product
- * rounded to the compute dtype up to the split's precision); everything else
- * runs on CUDA cores.  The workspace (fp32 split-k partials)
- * is sized by llmopt_quant_linear_workspace_size for the same m, n, k.
+ * 128, and 16-byte aligned x / qweight run on tensor cores; everything else
+ * runs on CUDA cores.  On tensor cores, 2- and 4-bit codes are not rounded
+ * weight by weight: the MMAs sum the exact products (q - z) * x of each group
+ * in fp32 and the group's scale multiplies that sum, which is at least as
+ * accurate as the reference's weights rounded to the compute dtype; 8-bit
+ * weights are the reference's bit for bit.  Zero points are integers in
+ * [0, 2^bits), as the reference's quantizers round them.  The workspace (fp32
+ * split-k partials) is sized by llmopt_quant_linear_workspace_size for the
+ * same m, n, k.
  */
 LLMOPT_API int llmopt_quant_linear_workspace_size(int device, int64_t m, int64_t n, int64_t k,
                     int32_t bits, int32_t group_size, int32_t x_dtype, size_t* bytes);

@@ -17,25 +17,27 @@
 // Kernels:
 // * wq_dequant_kernel: the dense weight in the compute dtype, bit-exact with the
 //   reference's dequantize.
-// * wq_gemm_kernel (f16 / bf16, k % 128 == 0, n % 64 == 0, group 32, 64, 128 or
-//   a multiple of 128):
-//   tensor cores.  A CTA owns 64 output features (four warps of 16) and 32
-//   tokens (8 when a call has at most 8); a 4-stage cp.async ring brings each 128-column tile's codes,
-//   token rows and group constants into shared memory, and each warp
-//   dequantizes its 16 rows in registers into m16n8k16 A fragments (weight
-//   rows = M, tokens = N: decode batches need no padding to 16 rows).  2- and
-//   4-bit codes become 16-bit pairs by one LOP3 each (a nibble in the mantissa
-//   of 128.0 for bf16 / 1024.0 for f16, the magic-number trick), then an exact
-//   subtraction of (magic + zero) and a multiply by the scale split into two
-//   16-bit parts (one FMA, one rounding);
-//   8-bit codes go through float32 (exact), so their weights are bit-exact.
-//   The pairs come out as (code j, code j+4) of each 8-code chunk; the B
-//   fragments pair the token values the same way with byte permutes after a
-//   16-byte read of the chunk (token rows are stored swizzled, so the reads of
-//   a quarter warp hit eight bank groups).  The k range is split across CTAs
-//   when n and m alone do not fill the GPU; splits write fp32 partials that
-//   wq_reduce_kernel sums (with the bias) in a fixed order.
+// * Tensor-core path (f16 / bf16, k % 128 == 0, n % 64 == 0, group 32, 64, 128
+//   or a multiple of 128): a CTA owns 64 output features (four warps of 16 rows)
+//   and 8 or 32 tokens; a 4-stage cp.async ring brings each 128-column
+//   tile's codes, token rows and group constants into shared memory, and each
+//   warp builds m16n8k16 A fragments from its 16 rows in registers (weight rows
+//   = M, tokens = N: a decode batch pads to 8 tokens, not 16).  Code pairs come
+//   out as (code j, code j+4) of each 8-code chunk; the B fragments pair the
+//   token values the same way with byte permutes after a 16-byte read.
+//   - wq_gemm_acc_kernel, 2- and 4-bit codes: one LOP3 puts two nibbles into
+//     the mantissas of a 16-bit pair (128.0 for bf16, 1024.0 for f16, the
+//     magic-number trick) and an exact subtraction leaves (q - z).  Each MMA's
+//     k-range lies inside one group, so the MMAs sum exact (q - z) x products
+//     and the group's scale multiplies the fp32 sum once per group.
+//   - wq_gemm_u8_kernel, 8-bit codes: dequantized in float32 (exact), rounded
+//     once to the compute dtype, so its weights are the reference's bit for bit.
+//   The k range is split across CTAs when n and m alone do not fill the GPU;
+//   splits write fp32 partials that wq_reduce_kernel sums (with the bias) in a
+//   fixed order.
 // * wq_generic_kernel: CUDA cores, fp32 accumulation, any shape and dtype.
+#include <cstddef>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -145,7 +147,6 @@ template <> struct Pair<kBF16> {
   static constexpr float kBase = 128.f;
   __device__ static T splat(float v) { return __floats2bfloat162_rn(v, v); }
   __device__ static T pack(float lo, float hi) { return __floats2bfloat162_rn(lo, hi); }
-  __device__ static float low_as_float(T v) { return __low2float(v); }
 };
 template <> struct Pair<kF16> {
   using T = __half2;
@@ -153,7 +154,6 @@ template <> struct Pair<kF16> {
   static constexpr float kBase = 1024.f;
   __device__ static T splat(float v) { return __floats2half2_rn(v, v); }
   __device__ static T pack(float lo, float hi) { return __floats2half2_rn(lo, hi); }
-  __device__ static float low_as_float(T v) { return __low2float(v); }
 };
 
 template <class T>
@@ -165,26 +165,8 @@ __device__ __forceinline__ T from_u32(uint32_t u) {
   return *reinterpret_cast<const T*>(&u);
 }
 
-// Dequantized pairs (code j, code j+4), j = 0..3, of the 8-code chunk `word`
-// (sub-byte codes: 8 nibbles).  d = (magic + q) - (magic + z) is exact; the
-// scale is split into a 16-bit head and a 16-bit residual (s = hi + lo to ~16
-// bits) and w = fma(d, hi, d * lo) rounds once, like the reference's float32
-// product rounded to the compute dtype, instead of carrying the scale's own
-// rounding error into every weight of the group.
-template <int DT>
-__device__ __forceinline__ void dequant_chunk4(uint32_t word, typename Pair<DT>::T off2,
-                                               typename Pair<DT>::T s_hi,
-                                               typename Pair<DT>::T s_lo, uint32_t (&p)[4]) {
-  using P = Pair<DT>;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t h = ((word >> (4 * j)) & 0x000F000Fu) | P::kMagic;
-    const typename P::T d = __hsub2(from_u32<typename P::T>(h), off2);
-    p[j] = as_u32(__hfma2(d, s_hi, __hmul2(d, s_lo)));
-  }
-}
-
-// The same for 8-bit codes (two words: codes 0-3 and 4-7), exact in float32.
+// Dequantized pairs (code j, code j+4), j = 0..3, of 8 8-bit codes (two words:
+// codes 0-3 and 4-7), exact in float32 and rounded once to the compute dtype.
 template <int DT>
 __device__ __forceinline__ void dequant_chunk8(uint32_t w0, uint32_t w1, uint32_t flip,
                                                float zoff, float s, uint32_t (&p)[4]) {
@@ -221,23 +203,25 @@ __device__ __forceinline__ void cp_async_wait() {
 constexpr int kStages = 4;
 constexpr int kMaxGroupsPerTile = kKT / 32;
 
+// ---- 8-bit codes: weights dequantized in float32 -------------------------------
+//
 // One pipeline stage: the CTA's codes, token tile and group constants of one
 // 128-column tile (MT tokens).
-template <int BITS, int MT>
-struct Stage {
-  static constexpr int kRowBytes = BITS == 8 ? kKT : kKT / 2;
+template <int MT>
+struct Stage8 {
+  static constexpr int kRowBytes = kKT;
   unsigned char w[kRows][kRowBytes];        // codes of the CTA's 64 rows
   uint4 x[MT][kChunks];                     // token rows, chunks swizzled by x_chunk()
   float s[kRows][kMaxGroupsPerTile];        // scales of the tile's groups
   float z[kRows][kMaxGroupsPerTile];        // zero points (asymmetric)
 };
 
-template <int DT, int BITS, int MT>
-__global__ void __launch_bounds__(kThreads) wq_gemm_kernel(const QuantLinearArgs a) {
+template <int DT, int MT>
+__global__ void __launch_bounds__(kThreads) wq_gemm_u8_kernel(const QuantLinearArgs a) {
   griddep_wait();
   griddep_launch_dependents();
   using P = Pair<DT>;
-  using S = Stage<BITS, MT>;
+  using S = Stage8<MT>;
   constexpr int NT = MT / 8;                                   // 8-token n-tiles
   extern __shared__ __align__(16) unsigned char smem_raw[];
   S* st = reinterpret_cast<S*>(smem_raw);
@@ -256,7 +240,7 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_kernel(const QuantLinearArgs
   const int n_tiles = mrem >= MT ? NT : (int)((mrem + 7) / 8);   // useful 8-token n-tiles
   const long long groups = a.k / a.group;
   const int gpt = a.group >= kKT ? 1 : kKT / a.group;            // groups per tile (<= 4)
-  const long long row_bytes = BITS == 8 ? a.k : a.k / 2;
+  const long long row_bytes = a.k;
 
   // Stage t <- codes, token tile and group constants of tile t (all threads).
   // A thread's copy slots are the same for every tile: their shared-memory
@@ -307,7 +291,7 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_kernel(const QuantLinearArgs
   auto issue = [&](int t) {
     unsigned char* base = reinterpret_cast<unsigned char*>(&st[t % kStages]);
     const long long k0 = kb + (long long)t * kKT;
-    const long long wk = BITS == 8 ? k0 : k0 / 2;
+    const long long wk = k0;
 #pragma unroll
     for (int q = 0; q < kWPer; ++q) {
       if (threadIdx.x + q * kThreads < kWPieces) cp_async16(base + wdst[q], wsrc[q] + wk, 16);
@@ -337,9 +321,6 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_kernel(const QuantLinearArgs
     if (t < ntiles) issue(t);
     cp_async_commit();
   }
-  // symmetric sub-byte codes carry the 2^(bits-1) bias (2- and 4-bit share the
-  // nibble layout, so the width comes from the arguments)
-  const float zsym = BITS < 8 ? (float)(1 << (a.bits - 1)) : 0.f;
 
   for (int t = 0; t < ntiles; ++t) {
     cp_async_wait<kStages - 2>();
@@ -349,43 +330,33 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_kernel(const QuantLinearArgs
     const S& s = st[t % kStages];
     // this lane's 32 codes of each row lie in group j = (32 t4) / group of the tile
     const int j = a.group >= kKT ? 0 : (32 * tid4) / a.group;
-    // the lane's codes of rows wrow and wrow + 8 (16-byte reads: a quarter warp
-    // covers 128 contiguous bytes) and their group constants
-    constexpr int kCw = BITS == 8 ? 2 : 1;
-    uint4 cw[2][kCw];
+    // the lane's 32 codes of rows wrow and wrow + 8 (16-byte reads) and their
+    // group constants
+    uint4 cw[2][2];
     float sf[2], zf[2];
-    typename P::T shi[2], slo[2], off2[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int r = wrow + 8 * h;
 #pragma unroll
-      for (int q = 0; q < kCw; ++q) {
-        cw[h][q] = *reinterpret_cast<const uint4*>(&s.w[r][(BITS == 8 ? 32 : 16) * tid4 + 16 * q]);
+      for (int q = 0; q < 2; ++q) {
+        cw[h][q] = *reinterpret_cast<const uint4*>(&s.w[r][32 * tid4 + 16 * q]);
       }
       sf[h] = s.s[r][j];
-      zf[h] = a.symmetric ? zsym : s.z[r][j];
-      shi[h] = P::splat(sf[h]);
-      slo[h] = P::splat(sf[h] - P::low_as_float(shi[h]));
-      off2[h] = P::splat(P::kBase + zf[h]);
+      zf[h] = a.symmetric ? 0.f : s.z[r][j];
     }
 #pragma unroll
     for (int w = 0; w < 4; ++w) {          // chunk 4 t4 + w: k-steps 2w, 2w + 1
       uint32_t pa[2][4];                   // [row half][pair (code i, code i+4)]
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        if constexpr (BITS == 8) {
-          // codes 8w .. 8w+7: words 2w and 2w + 1 of the lane's 32 bytes
-          const uint4& c = cw[h][w >> 1];
-          const uint32_t w0 = (w & 1) ? c.z : c.x;
-          const uint32_t w1 = (w & 1) ? c.w : c.y;
-          const uint32_t flip = a.symmetric ? 0x80u : 0u;
-          const float zoff = 8388608.f + (a.symmetric ? 128.f : zf[h]);
-          dequant_chunk8<DT>(w0, w1, flip, zoff, sf[h], pa[h]);
-        } else {
-          const uint4& c = cw[h][0];
-          const uint32_t cwv = w == 0 ? c.x : w == 1 ? c.y : w == 2 ? c.z : c.w;
-          dequant_chunk4<DT>(cwv, off2[h], shi[h], slo[h], pa[h]);
-        }
+        // codes 8w .. 8w+7: words 2w and 2w + 1 of the lane's 32 bytes; symmetric
+        // codes are int8, flipped to offset binary (q + 128)
+        const uint4& c = cw[h][w >> 1];
+        const uint32_t w0 = (w & 1) ? c.z : c.x;
+        const uint32_t w1 = (w & 1) ? c.w : c.y;
+        const uint32_t flip = a.symmetric ? 0x80u : 0u;
+        const float zoff = 8388608.f + (a.symmetric ? 128.f : zf[h]);
+        dequant_chunk8<DT>(w0, w1, flip, zoff, sf[h], pa[h]);
       }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
@@ -401,6 +372,213 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_kernel(const QuantLinearArgs
                                     pa[1][2 * hs + 1]};
             mma_16816<DT>(acc[nt], af, b[2 * hs], b[2 * hs + 1]);
           }
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  // c-fragment e of n-tile nt: feature wrow + 8 (e >> 1), token m0 + 8 nt + 2 t4 + (e & 1)
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const long long tok = m0 + nt * 8 + 2 * tid4 + (e & 1);
+      const long long f = rbase + wrow + 8 * (e >> 1);
+      if (tok >= a.m) continue;
+      if (a.partial != nullptr) {
+        a.partial[((long long)blockIdx.y * a.m + tok) * a.n + f] = acc[nt][e];
+      } else {
+        float v = acc[nt][e];
+        if (a.bias != nullptr) v += load_f32<DT>(a.bias, f);
+        store_f32<DT>(a.out, tok * a.ldo + f, v);
+      }
+    }
+  }
+}
+
+// ---- 2- and 4-bit codes: the group scale applied to the fp32 accumulators ------
+//
+// The k-steps of every MMA are aligned to the groups.  ldmatrix hands lane
+// (g, t4) word w (w = 0..3) of a row as the codes of columns 32 w + 8 t4 ..
+// 32 w + 8 t4 + 7 of the tile, so the two MMAs of word w cover only the 32
+// columns [32 w, 32 w + 32) of the tile, which lie inside one group (groups
+// are 32, 64 or 128 columns, or multiples of 128).  Those MMAs therefore run
+// on the exact integers (q - z) in the compute dtype (products exact in fp32),
+// and the group's scale multiplies the group's fp32 sum once:
+// y += s_row * sum_{k in group} (q_k - z) x_k.  Per 8 codes that is one LOP3
+// (plus a shift) per pair and one exact subtraction per pair; the scale costs
+// one FMA per accumulator per group.
+template <int MT, int GPT>
+struct StageQ {
+  static constexpr int kRowBytes = kKT / 2;   // 64 bytes of codes per row and tile
+  // codes; 16-byte piece p of row r sits at piece position p ^ ((r >> 1) & 3),
+  // so the eight rows of each ldmatrix phase hit eight different bank groups
+  unsigned char w[kRows][kRowBytes];
+  // token rows; chunk c of token i sits at chunk position c ^ ((i & 1) << 2)
+  uint4 x[MT][kChunks];
+  float s[kRows][GPT];                        // scales of the tile's groups
+  float z[kRows][GPT];                        // zero points (asymmetric)
+};
+
+__device__ __forceinline__ int w_piece_pos(int r, int p) { return p ^ ((r >> 1) & 3); }
+__device__ __forceinline__ int x_chunk_pos(int i, int c) { return c ^ ((i & 1) << 2); }
+
+template <int DT, int MT, int GPT>
+__global__ void __launch_bounds__(kThreads) wq_gemm_acc_kernel(const QuantLinearArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  using P = Pair<DT>;
+  using S = StageQ<MT, GPT>;
+  constexpr int NT = MT / 8;                    // 8-token n-tiles
+  constexpr int kWordsPerGroup = 4 / GPT;       // 32-column words per group within a tile
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int gid = lane >> 2;
+  const int tid4 = lane & 3;
+  const long long rbase = (long long)blockIdx.x * kRows;
+  const int wrow = warp * 16 + gid;             // this lane's rows: wrow, wrow + 8
+  const long long m0 = (long long)blockIdx.z * MT;
+  const long long kb = (long long)blockIdx.y * a.k_per_split;
+  const long long ke = kb + a.k_per_split < a.k ? kb + a.k_per_split : a.k;
+  const int ntiles = (int)((ke - kb) / kKT);
+  const long long mrem = a.m - m0;
+  const int n_tiles = mrem >= MT ? NT : (int)((mrem + 7) / 8);
+  const long long groups = a.k / a.group;
+  const long long row_bytes = a.k / 2;
+  const int tile0 = (int)(kb / kKT);
+
+  // Copy slots.  Codes: 64 rows x 4 pieces, two per thread (rows tid/4 and
+  // tid/4 + 32, piece tid % 4).
+  const unsigned char* wsrc = a.qweight + (rbase + (tid >> 2)) * row_bytes + kb / 2 + 16 * (tid & 3);
+  const long long wstep = 32 * row_bytes;
+  const int wdst = (tid >> 2) * S::kRowBytes + 16 * w_piece_pos(tid >> 2, tid & 3);
+  constexpr int kWDstStep = 32 * S::kRowBytes;
+  // Token rows: MT x 16 chunks, MT / 8 per thread (tokens tid/16 + 8 q, chunk tid % 16).
+  constexpr int kXPer = MT * kChunks / kThreads;
+  const int xr0 = tid >> 4;
+  const int xc = tid & 15;
+  const unsigned short* xsrc =
+      static_cast<const unsigned short*>(a.x) + (m0 + xr0) * a.ldx + kb + 8 * xc;
+  const long long xstep = 8 * a.ldx;
+  const int xdst = (int)offsetof(S, x) + (xr0 * kChunks + x_chunk_pos(xr0, xc)) * 16;
+  constexpr int kXDstStep = 8 * kChunks * 16;
+  // tokens of this thread's slots that exist: xr0 + 8 q < mrem
+  const int x_valid = mrem > xr0 ? (int)((mrem - xr0 + 7) / 8) : 0;
+  // Group constants: 64 x GPT entries (row i / GPT, group i % GPT of the tile).
+  constexpr int kGPer = (kRows * GPT + kThreads - 1) / kThreads;
+  // first group of tile t: (tile0 + t) * GPT, or (tile0 + t) / tpg for groups
+  // of tpg tiles; issue() runs for t = 0, 1, 2, ... in order and keeps a cursor
+  const int tpg = GPT > 1 ? 1 : a.group / kKT;
+  long long g_cur = GPT > 1 ? (long long)tile0 * GPT : tile0 / tpg;
+  int g_in = GPT > 1 ? 0 : tile0 % tpg;
+
+  auto issue = [&](int t) {
+    unsigned char* base = smem_raw + (size_t)(t % kStages) * sizeof(S);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      cp_async16(base + wdst + q * kWDstStep, wsrc + q * wstep + (long long)t * (kKT / 2), 16);
+    }
+#pragma unroll
+    for (int q = 0; q < kXPer; ++q) {
+      const bool ok = q < x_valid;
+      // a slot past the last token copies nothing (source size 0) from a valid address
+      cp_async16(base + xdst + q * kXDstStep,
+                 ok ? xsrc + q * xstep + (long long)t * kKT : static_cast<const unsigned short*>(a.x),
+                 ok ? 16 : 0);
+    }
+    S& sg = *reinterpret_cast<S*>(base);
+#pragma unroll
+    for (int q = 0; q < kGPer; ++q) {
+      const int i = tid + q * kThreads;
+      if (i < kRows * GPT) {
+        const int r = i / GPT, g = i % GPT;
+        const long long gi = (rbase + r) * groups + g_cur + g;
+        cp_async4(&sg.s[r][g], a.scales + gi);
+        if (!a.symmetric) cp_async4(&sg.z[r][g], a.zeros + gi);
+      }
+    }
+    if (GPT > 1) {
+      g_cur += GPT;
+    } else if (++g_in == tpg) {
+      g_in = 0;
+      ++g_cur;
+    }
+  };
+
+  float acc[NT][4];
+  float part[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+
+#pragma unroll
+  for (int t = 0; t < kStages - 1; ++t) {
+    if (t < ntiles) issue(t);
+    cp_async_commit();
+  }
+  // ldmatrix rows: matrix q = lane / 8 is piece q of rows warp*16 + 8h + lane % 8
+  const int lr = warp * 16 + (lane & 7);
+  const int lm_off = lr * S::kRowBytes + 16 * w_piece_pos(lr, lane >> 3);
+  const float zsym = (float)(1 << (a.bits - 1));
+  const int xi_pos = gid & 1;                   // parity of every token row this lane reads
+
+  for (int t = 0; t < ntiles; ++t) {
+    cp_async_wait<kStages - 2>();
+    __syncthreads();                            // tile t landed; tile t-1's stage is free
+    if (t + kStages - 1 < ntiles) issue(t + kStages - 1);
+    cp_async_commit();
+    const unsigned char* base = smem_raw + (size_t)(t % kStages) * sizeof(S);
+    const S& sg = *reinterpret_cast<const S*>(base);
+    uint32_t cw[2][4];                          // [row half][word w]
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      ldsm_x4(smem_addr(base + lm_off + h * 8 * S::kRowBytes), cw[h][0], cw[h][1], cw[h][2],
+              cw[h][3]);
+    }
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int g = w / kWordsPerGroup;
+      if (w % kWordsPerGroup == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.f;
+      }
+      uint32_t pa[2][4];                        // [row half][pair (code j, code j+4)]
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float zf = a.symmetric ? zsym : sg.z[wrow + 8 * h][g];
+        const typename P::T off2 = P::splat(P::kBase + zf);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t v = ((cw[h][w] >> (4 * j)) & 0x000F000Fu) | P::kMagic;
+          pa[h][j] = as_u32(__hsub2(from_u32<typename P::T>(v), off2));
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (nt < n_tiles) {
+          const uint4 xv = sg.x[nt * 8 + gid][(4 * w + tid4) ^ (xi_pos << 2)];
+          const uint32_t b[4] = {__byte_perm(xv.x, xv.z, 0x5410), __byte_perm(xv.x, xv.z, 0x7632),
+                                 __byte_perm(xv.y, xv.w, 0x5410), __byte_perm(xv.y, xv.w, 0x7632)};
+#pragma unroll
+          for (int hs = 0; hs < 2; ++hs) {
+            const uint32_t af[4] = {pa[0][2 * hs], pa[1][2 * hs], pa[0][2 * hs + 1],
+                                    pa[1][2 * hs + 1]};
+            mma_16816<DT>(part[nt], af, b[2 * hs], b[2 * hs + 1]);
+          }
+        }
+      }
+      if (w % kWordsPerGroup == kWordsPerGroup - 1) {
+        const float s0 = sg.s[wrow][g];
+        const float s1 = sg.s[wrow + 8][g];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          acc[nt][0] = fmaf(part[nt][0], s0, acc[nt][0]);
+          acc[nt][1] = fmaf(part[nt][1], s0, acc[nt][1]);
+          acc[nt][2] = fmaf(part[nt][2], s1, acc[nt][2]);
+          acc[nt][3] = fmaf(part[nt][3], s1, acc[nt][3]);
         }
       }
     }
@@ -442,28 +620,47 @@ __global__ void __launch_bounds__(256) wq_reduce_kernel(const QuantLinearArgs a)
   }
 }
 
-template <int DT>
-const void* gemm_ptr(int bits, int mt) {
-  if (mt == kMTSmall) {
-    return bits == 8 ? reinterpret_cast<const void*>(&wq_gemm_kernel<DT, 8, kMTSmall>)
-                     : reinterpret_cast<const void*>(&wq_gemm_kernel<DT, 4, kMTSmall>);
-  }
-  return bits == 8 ? reinterpret_cast<const void*>(&wq_gemm_kernel<DT, 8, kMT>)
-                   : reinterpret_cast<const void*>(&wq_gemm_kernel<DT, 4, kMT>);
+int groups_per_tile(int group) { return group >= kKT ? 1 : kKT / group; }
+
+// 8 tokens per CTA up to 8 tokens, else 32.  (64-token tiles of the 2/4-bit
+// kernel measured slower at 64 tokens: two CTAs per SM, latency-bound.)
+int tokens_per_cta(const QuantLinearArgs& a) { return a.m <= kMTSmall ? kMTSmall : kMT; }
+
+template <int DT, int MT>
+const void* acc_ptr(int gpt) {
+  return gpt == 1   ? reinterpret_cast<const void*>(&wq_gemm_acc_kernel<DT, MT, 1>)
+         : gpt == 2 ? reinterpret_cast<const void*>(&wq_gemm_acc_kernel<DT, MT, 2>)
+                    : reinterpret_cast<const void*>(&wq_gemm_acc_kernel<DT, MT, 4>);
 }
 
-int tokens_per_cta(long long m) { return m <= kMTSmall ? kMTSmall : kMT; }
-
-size_t gemm_smem(int bits, int mt) {
-  if (mt == kMTSmall) {
-    return kStages * (bits == 8 ? sizeof(Stage<8, kMTSmall>) : sizeof(Stage<4, kMTSmall>));
+template <int DT>
+const void* gemm_ptr(const QuantLinearArgs& a, int mt) {
+  if (a.bits == 8) {
+    return mt == kMTSmall ? reinterpret_cast<const void*>(&wq_gemm_u8_kernel<DT, kMTSmall>)
+                          : reinterpret_cast<const void*>(&wq_gemm_u8_kernel<DT, kMT>);
   }
-  return kStages * (bits == 8 ? sizeof(Stage<8, kMT>) : sizeof(Stage<4, kMT>));
+  const int gpt = groups_per_tile(a.group);
+  return mt == kMTSmall ? acc_ptr<DT, kMTSmall>(gpt) : acc_ptr<DT, kMT>(gpt);
+}
+
+template <int MT>
+size_t acc_smem(int gpt) {
+  return kStages * (gpt == 1   ? sizeof(StageQ<MT, 1>)
+                    : gpt == 2 ? sizeof(StageQ<MT, 2>)
+                               : sizeof(StageQ<MT, 4>));
+}
+
+size_t gemm_smem(const QuantLinearArgs& a, int mt) {
+  if (a.bits == 8) {
+    return kStages * (mt == kMTSmall ? sizeof(Stage8<kMTSmall>) : sizeof(Stage8<kMT>));
+  }
+  const int gpt = groups_per_tile(a.group);
+  return mt == kMTSmall ? acc_smem<kMTSmall>(gpt) : acc_smem<kMT>(gpt);
 }
 
 const void* gemm_fn(const QuantLinearArgs& a) {
-  const int mt = tokens_per_cta(a.m);
-  return a.x_dtype == kBF16 ? gemm_ptr<kBF16>(a.bits, mt) : gemm_ptr<kF16>(a.bits, mt);
+  const int mt = tokens_per_cta(a);
+  return a.x_dtype == kBF16 ? gemm_ptr<kBF16>(a, mt) : gemm_ptr<kF16>(a, mt);
 }
 
 long long grid_blocks(long long work, int threads) {
@@ -487,11 +684,11 @@ bool quant_linear_tc_supported(const QuantLinearArgs& a) {
 // occupancy (one wave leaves a ragged tail when the tile count is not a
 // multiple of the slots; more splits cost partial traffic).
 int quant_linear_splits(const QuantLinearArgs& a, int sm_count) {
-  const int mt = tokens_per_cta(a.m);
+  const int mt = tokens_per_cta(a);
   const long long ctas = (a.n / kRows) * ((a.m + mt - 1) / mt);
   const long long tiles = a.k / kKT;
   const void* fn = gemm_fn(a);
-  const size_t smem = gemm_smem(a.bits, mt);
+  const size_t smem = gemm_smem(a, mt);
   int occ = 1;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
           cudaSuccess ||
@@ -519,10 +716,10 @@ cudaError_t quant_linear_launch(const QuantLinearArgs& a, cudaStream_t stream) {
     return launch_pdl(fn, dim3((unsigned)gx, (unsigned)gy), dim3(256), args, 0, stream);
   }
   const void* fn = gemm_fn(a);
-  const int mt = tokens_per_cta(a.m);
+  const int mt = tokens_per_cta(a);
   const long long gx = a.n / kRows, gz = (a.m + mt - 1) / mt;
   if (gx > 0x7fffffffLL || gz > 65535 || a.splits > 65535) return cudaErrorInvalidConfiguration;
-  const size_t smem = gemm_smem(a.bits, mt);
+  const size_t smem = gemm_smem(a, mt);
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   e = launch_pdl(fn, dim3((unsigned)gx, (unsigned)a.splits, (unsigned)gz), dim3(kThreads), args,

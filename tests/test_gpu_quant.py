@@ -5,12 +5,14 @@
   with the oracle at larger shapes;
 * ``forward`` against the oracle (x @ W^T + b in float64 over the exact
   compute-dtype weight) within 1e-2 * |y| + 1e-2 * rms(y): the reference's own
-  output is rounded to the compute dtype, and the tensor-core path scales 2-
-  and 4-bit codes in 16-bit arithmetic (a two-part scale, one rounding);
-  fp32 layers within 1e-5 relative.  Covered: 2/4/8-bit codes, symmetric and
-  asymmetric grids, groups 32/64/128, bf16/f16/fp32, token counts from 1 to
-  300 (partial 8-token tiles, several 32-token tiles), split-k over k = 4096,
-  shapes outside the tensor-core path, leading batch dimensions, no bias;
+  output is rounded to the compute dtype, and the tensor-core path for 2- and
+  4-bit codes applies each group's scale to fp32 sums of exact (q - z) * x
+  products instead of rounding every weight; fp32 layers within 1e-5
+  relative.  Covered: 2/4/8-bit codes, symmetric and asymmetric grids, groups
+  32/64/128 and 256/384 (groups spanning several tiles, with the k range
+  split inside a group), bf16/f16/fp32, token counts from 1 to 300 (partial
+  8-token tiles, several 32-token tiles), split-k over k = 4096, shapes
+  outside the tensor-core path, leading batch dimensions, no bias;
 * the golden forward outputs of the reference itself.
 """
 
@@ -118,6 +120,21 @@ def test_split_k_at_llama_width(cuda, group, m):
     x = po.from_f32(rng.standard_normal((m, k)).astype(np.float32), "bf16")
     y = layer(to_dev(x, "bf16", cuda)).float().cpu().numpy()
     want = qo.quant_linear(x, "bf16", qw, s, z, 4, group, True, (n, k), b)
+    _assert_close(y, want, "bf16", f"m={m}")
+
+
+@pytest.mark.parametrize("group,symmetric", [(256, True), (384, False)])
+@pytest.mark.parametrize("m", [1, 20, 40])
+def test_groups_wider_than_a_tile(cuda, group, symmetric, m):
+    """Groups of 2 and 3 column tiles; n = 256 leaves the k range split into
+    pieces of 2 tiles, so splits start inside a group."""
+    n, k = 256, 3072
+    layer, (qw, s, z, b) = _random_layer(960 + group + m, n, k, 4, group, symmetric, "bf16",
+                                          device=cuda)
+    rng = np.random.default_rng(m + 3)
+    x = po.from_f32(rng.standard_normal((m, k)).astype(np.float32), "bf16")
+    y = layer(to_dev(x, "bf16", cuda)).float().cpu().numpy()
+    want = qo.quant_linear(x, "bf16", qw, s, z, 4, group, symmetric, (n, k), b)
     _assert_close(y, want, "bf16", f"m={m}")
 
 
