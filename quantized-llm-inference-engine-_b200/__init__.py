@@ -9,6 +9,10 @@ backed by the C-ABI library ``libllmopt_b200.so`` (``include/llmopt_b200.h``):
 * the KV append into the block pool, fused with the dtype cast;
 * FP8 (e4m3) KV storage; the weight-only quantized linear layer (``QuantLinear``).
 
+The same entry points are registered as ``torch.ops.llmopt_b200.*`` custom
+operators with fake implementations (``ops``), for ``torch.compile`` /
+``torch.export`` tracing and CUDA-graph capture.
+
 ``install()`` rebinds the reference engine's names; ``dist`` shards the path by
 KV head over several GPUs.  The package directory name is not a Python
 identifier; it is importable with ``importlib.import_module`` and registers
@@ -22,6 +26,7 @@ import sys as _sys
 from ._lib import check, lib, version
 from .attention import AttentionBackend, PagedAttention, PagedAttentionConfig, merge_states
 from .cache import PagedKVCache
+from . import ops
 from .install import install, uninstall
 from .quant import QuantLinear, QuantLinearConfig
 from .rope import RotaryEmbedding, rope_kv_append
@@ -40,6 +45,7 @@ __all__ = [
     "QuantLinearConfig",
     "install",
     "uninstall",
+    "ops",
     "lib",
     "check",
     "version",

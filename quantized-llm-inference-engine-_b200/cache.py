@@ -77,6 +77,31 @@ class PagedKVCache:
             self.key_scale = torch.zeros(sshape, dtype=torch.float32, device=dev)
             self.value_scale = torch.zeros_like(self.key_scale)
 
+    @classmethod
+    def from_storage(cls, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                     key_scale: torch.Tensor | None = None,
+                     value_scale: torch.Tensor | None = None) -> "PagedKVCache":
+        """A cache over existing storage (no copy): ``key_cache`` / ``value_cache``
+        ``[num_layers, num_blocks, block_size, num_kv_heads, head_dim]`` on a CUDA
+        device, plus the two fp32 scale arrays for float8_e4m3fn storage."""
+        if key_cache.dim() != 5 or value_cache.shape != key_cache.shape:
+            raise ValueError("key_cache/value_cache must be [num_layers, num_blocks, block_size, "
+                             "num_kv_heads, head_dim] and alike")
+        if key_cache.dtype not in rt.KV_DTYPE_CODE:
+            raise ValueError(f"PagedKVCache: unsupported dtype {key_cache.dtype}")
+        rt.require_cuda(key_cache, "key_cache")
+        self = cls.__new__(cls)
+        (self.num_layers, self.num_blocks, self.block_size, self.num_kv_heads,
+         self.head_dim) = key_cache.shape
+        self.dtype = key_cache.dtype
+        self.device = key_cache.device
+        self.key_cache = key_cache
+        self.value_cache = value_cache
+        self.key_scale = key_scale if self.is_fp8 else None
+        self.value_scale = value_scale if self.is_fp8 else None
+        self._check_storage()
+        return self
+
     @property
     def is_fp8(self) -> bool:
         """e4m3 codes with per-row fp32 scales (``key_scale`` / ``value_scale``)."""

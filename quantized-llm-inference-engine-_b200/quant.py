@@ -120,39 +120,70 @@ class QuantLinear(nn.Module):
             raise RuntimeError(f"expected input dtype {dtype}, got {x.dtype}")
         if x.shape[-1] != self.in_features:
             raise RuntimeError(f"input has {x.shape[-1]} features, expected {self.in_features}")
-        device = x.device
-        qweight, scales, zeros, group = self._operands(device)
-        lead = x.shape[:-1]
-        x2 = x.reshape(-1, self.in_features)
-        if x2.stride(-1) != 1:
-            x2 = x2.contiguous()
-        m = x2.shape[0]
-        out = torch.empty((*lead, self.out_features), dtype=dtype, device=device)
-        if m == 0:
-            return out
-        bias = self.bias
-        if bias is not None:
-            bias = bias.to(device=device, dtype=dtype).contiguous()
-        L = _lib.lib()
-        code = rt.dtype_code(dtype, "compute_dtype")
-        nbytes = _ctypes_size_t()
-        _lib.check(L.llmopt_quant_linear_workspace_size(
-            device.index, m, self.out_features, self.in_features, self.config.bits, group,
-            code, nbytes), "QuantLinear workspace size")
-        ws = rt.workspace(device, nbytes.value) if nbytes.value else None
-        st = L.llmopt_quant_linear(
-            x2.data_ptr(), code, m, x2.stride(0), qweight.data_ptr(), self.config.bits, group,
-            int(self.config.symmetric), scales.data_ptr(),
-            zeros.data_ptr() if zeros.numel() else None, self.out_features, self.in_features,
-            bias.data_ptr() if bias is not None else None, out.data_ptr(), self.out_features,
-            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-            rt.stream_handle(device))
-        _lib.check(st, "QuantLinear.forward")
-        return out
+        qweight, scales, zeros, group = self._operands(x.device)
+        return quant_linear(x, qweight, scales, zeros, self.bias, self.config.bits, group,
+                            self.config.symmetric)
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
                 f"bits={self.config.bits}, bias={self.bias is not None}")
+
+
+def quant_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                 zeros: torch.Tensor | None, bias: torch.Tensor | None, bits: int,
+                 group_size: int, symmetric: bool) -> torch.Tensor:
+    """``x @ dequantize(qweight)^T + bias`` in ``x``'s dtype, by the fused kernel.
+
+    ``qweight`` / ``scales`` / ``zeros`` are device tensors in the reference's
+    layout (``scales`` / ``zeros`` fp32 ``[out, in / group_size]``); the output
+    has ``x``'s leading dimensions and ``scales.shape[0]`` features.
+    """
+    rt.require_cuda(x, "quant_linear input")
+    device = x.device
+    dtype = x.dtype
+    k = x.shape[-1]
+    n = scales.shape[0]
+    group = group_size if group_size > 0 else k
+    if group <= 0 or k % group or scales.shape != (n, k // group):
+        raise ValueError(f"scales must be [out_features, {k} / group_size]")
+    if not symmetric and (zeros is None or zeros.shape != scales.shape):
+        raise ValueError("asymmetric quantization needs zeros shaped like scales")
+    for t, name in ((qweight, "qweight"), (scales, "scales")):
+        if t.device != device:
+            raise ValueError(f"{name} must be on {device}")
+    if qweight.dtype not in (torch.uint8, torch.int8):
+        raise ValueError(f"qweight must be uint8/int8, got {qweight.dtype}")
+    if scales.dtype != torch.float32 or not scales.is_contiguous():
+        scales = scales.to(torch.float32).contiguous()
+    if zeros is not None and zeros.numel():
+        zeros = zeros.to(device=device, dtype=torch.float32).contiguous()
+    else:
+        zeros = None
+    qweight = qweight.contiguous()
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    out = torch.empty((*lead, n), dtype=dtype, device=device)
+    if m == 0:
+        return out
+    if bias is not None:
+        bias = bias.to(device=device, dtype=dtype).contiguous()
+    L = _lib.lib()
+    code = rt.dtype_code(dtype, "compute_dtype")
+    nbytes = _ctypes_size_t()
+    _lib.check(L.llmopt_quant_linear_workspace_size(device.index, m, n, k, bits, group, code,
+                                                    nbytes), "QuantLinear workspace size")
+    ws = rt.workspace(device, nbytes.value) if nbytes.value else None
+    st = L.llmopt_quant_linear(
+        x2.data_ptr(), code, m, x2.stride(0), qweight.data_ptr(), bits, group, int(symmetric),
+        scales.data_ptr(), zeros.data_ptr() if zeros is not None else None, n, k,
+        bias.data_ptr() if bias is not None else None, out.data_ptr(), n,
+        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+        rt.stream_handle(device))
+    _lib.check(st, "QuantLinear.forward")
+    return out
 
 
 def _ctypes_size_t():
