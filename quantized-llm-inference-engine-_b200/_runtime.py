@@ -46,7 +46,12 @@ def stream_handle(device: torch.device) -> int:
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """A uint8 device buffer of at least ``nbytes`` (cached per device)."""
+    """A uint8 device buffer of at least ``nbytes`` (cached per device).
+
+    One buffer serves every call on the device.  Calls issued on one stream
+    are ordered by it, which is how the engine runs (one stream, one lock);
+    calls overlapping on two streams would share the buffer.
+    """
     idx = device.index if device.index is not None else torch.cuda.current_device()
     with _lock:
         buf = _workspaces.get(idx)
