@@ -117,6 +117,27 @@ def test_ops_refuse_cpu_tensors(pkg):
     lse = torch.zeros(2, 3)
     with pytest.raises(RuntimeError, match="CUDA"):
         pkg.merge_states(o, o, lse, lse)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        torch.ops.llmopt_b200.merge_states(o, o, lse, lse)
+    from importlib import import_module
+
+    quant = import_module("quantized-llm-inference-engine-_b200.quant")
+    with pytest.raises(RuntimeError, match="CUDA"):
+        quant.quant_linear(torch.zeros(2, 128, dtype=torch.bfloat16),
+                           torch.zeros(64, 64, dtype=torch.uint8), torch.ones(64, 1), None, None,
+                           4, 128, True)
+
+
+def test_cache_from_storage_validates(pkg):
+    kc = torch.zeros(1, 4, 16, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pkg.PagedKVCache.from_storage(kc, kc.clone())
+    with pytest.raises(ValueError, match="num_layers"):
+        pkg.PagedKVCache.from_storage(kc[0], kc[0].clone())
+    with pytest.raises(ValueError, match="alike"):
+        pkg.PagedKVCache.from_storage(kc, kc[:, :2].clone())
+    with pytest.raises(ValueError, match="dtype"):
+        pkg.PagedKVCache.from_storage(kc.to(torch.int8), kc.to(torch.int8))
 
 
 def test_missing_library_fails_loudly(monkeypatch):
