@@ -8,6 +8,8 @@ very long sequence, batches past the balanced-plan limit).  At BASELINE
 config-2 size it checks size-independent properties: every split mode gives
 the same answer, relocating physical blocks changes nothing bit-for-bit, and
 sequences that share prefix blocks with equal queries get identical outputs.
+At config-4 size (4 x 131072 tokens) it checks attention's closed forms and
+the agreement of the split plans.
 """
 
 from __future__ import annotations
@@ -282,3 +284,65 @@ def test_output_into_strided_view(cuda):
                           out=head_major.permute(1, 0, 2, 3))
     ref = attn.forward(q, cache, 0, table, ctx, 1)
     assert torch.equal(head_major.permute(1, 0, 2, 3), ref)
+
+
+# ---------------------------------------------------------------------------
+# BASELINE config 4 (full size: 4 x 131072 tokens): closed forms
+# ---------------------------------------------------------------------------
+
+def test_config4_full_size_closed_forms(cuda):
+    """At 131072 tokens per sequence (2.1 GB of KV) the oracle's padded,
+    group-expanded copies do not fit a test, but attention's closed forms hold
+    at any size.  With K = 0 every score is equal, so the LSE is ln(ctx) and
+    the output is the mean of V over the context.  With V constant per
+    (KV head, dim) the output is that constant whatever K is (the softmax
+    weights sum to 1).  On random K and V the balanced, fixed-512 and
+    one-split plans agree."""
+    import math
+
+    pkg = load_package()
+    B, H, KVH, D, bs, ctx_len = 4, 64, 8, 128, 16, 131072
+    group = H // KVH
+    nblk = ctx_len // bs
+    nb = B * nblk + 64
+    cache = pkg.PagedKVCache(1, nb, bs, KVH, D, dtype=torch.bfloat16, device=cuda)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(4)
+    cache.value_cache.normal_(0.0, 0.5, generator=g)
+    table = torch.randperm(nb, generator=g, device=cuda)[:B * nblk].reshape(B, nblk)
+    table = table.to(torch.int32)
+    ctx = torch.full((B,), ctx_len, dtype=torch.int64, device=cuda)
+    q = torch.randn(B, H, 1, D, generator=g, device=cuda).to(torch.bfloat16)
+    attn = pkg.PagedAttention(H, KVH, D)
+
+    # K = 0 (a new cache is zeroed)
+    out, lse = attn.forward_with_lse(q, cache, 0, table, ctx)
+    torch.cuda.synchronize(cuda)
+    assert torch.all((lse - math.log(ctx_len)).abs() <= 1e-4)
+    for s in range(B):
+        mean = cache.value_cache[0][table[s].long()].float().mean(dim=(0, 1))   # [KVH, D]
+        want = mean.repeat_interleave(group, dim=0)                              # [H, D]
+        err = (out[s, :, 0].float() - want).abs().max().item()
+        assert err <= 1e-3, f"sequence {s}: mean-of-V error {err:.3e}"
+
+    # random K and V: the three plans agree
+    cache.key_cache.normal_(0.0, 0.5, generator=g)
+    results = {}
+    for mode in ("auto", "fixed", "none"):
+        cfg = pkg.PagedAttentionConfig(split_kv=mode != "none", split_size=512)
+        a = pkg.PagedAttention(H, KVH, D, config=cfg,
+                               split_mode="fixed" if mode == "fixed" else "auto")
+        o, l = a.forward_with_lse(q, cache, 0, table, ctx)
+        results[mode] = (o.float().cpu().numpy(), l.cpu().numpy())
+    for mode in ("fixed", "none"):
+        assert_lowp_close(results[mode][0], results["auto"][0], f"config 4 {mode} vs auto")
+        assert_lse_close(results[mode][1], results["auto"][1], f"config 4 {mode} vs auto lse")
+
+    # V constant per (KV head, dim): the output is that constant
+    const = torch.randn(KVH, D, generator=g, device=cuda).to(torch.bfloat16)
+    cache.value_cache[0].copy_(const.expand(nb, bs, KVH, D))
+    out, _ = attn.forward_with_lse(q, cache, 0, table, ctx)
+    want = const.float().repeat_interleave(group, dim=0)
+    assert_lowp_close(out[:, :, 0].float().cpu().numpy(),
+                      want.expand(B, H, D).cpu().numpy(), "config 4 constant V")
+    assert device_errors(cuda) == 0
