@@ -457,6 +457,12 @@ LLMOPT_API int llmopt_quant_linear(const void* x, int32_t x_dtype, int64_t m, in
 LLMOPT_API int llmopt_dequantize(const void* qweight, int32_t bits, int32_t group_size,
                     int32_t symmetric, const float* scales, const float* zeros, int64_t n,
                     int64_t k, void* out, int32_t out_dtype, void* stream);
+/* LLMOPT_DEVERR_* bits that the quantized-linear kernels' bounded waits recorded
+ * on the current device since the last clear (synchronous read; cleared when
+ * `clear` is non-zero).  Only the tcgen05 path, enabled by
+ * LLMOPT_B200_QUANT_TC05=1, waits on the device; its outputs are NaN where a
+ * wait gave up. */
+LLMOPT_API int llmopt_quant_linear_device_errors(int32_t clear, uint32_t* bits);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -139,6 +139,7 @@ SIGNATURES = {
         _p, _i32, _i64, _i64, _p, _i32, _i32, _i32, _p, _p, _i64, _i64, _p, _p, _i64,
         _p, ctypes.c_size_t, _p],
     "llmopt_dequantize": [_p, _i32, _i32, _i32, _p, _p, _i64, _i64, _p, _i32, _p],
+    "llmopt_quant_linear_device_errors": [_i32, _p],
 }
 
 DTYPE_E4M3 = 3

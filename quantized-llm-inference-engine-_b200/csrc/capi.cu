@@ -843,6 +843,15 @@ int llmopt_dequantize(const void* qweight, int32_t bits, int32_t group_size, int
   return ok();
 }
 
+int llmopt_quant_linear_device_errors(int32_t clear, uint32_t* bits) {
+  if (bits == nullptr) return fail(LLMOPT_ERR_INVALID_ARGUMENT, "bits is null");
+  unsigned v = 0u;
+  cudaError_t e = quant_linear_device_errors(&v, clear != 0);
+  if (e != cudaSuccess) return cuda_fail(e, "quant_linear device errors");
+  *bits = v;
+  return ok();
+}
+
 int llmopt_merge_states(const void* o1, const void* o2, const void* l1, const void* l2,
                         void* out, void* lse_out, int64_t rows, int32_t head_dim,
                         int32_t o_dtype, int32_t lse_dtype, void* stream) {

@@ -216,6 +216,9 @@ struct QuantLinearArgs {
 bool quant_linear_tc_supported(const QuantLinearArgs& a);
 int quant_linear_splits(const QuantLinearArgs& a, int sm_count);
 cudaError_t quant_linear_launch(const QuantLinearArgs& a, cudaStream_t stream);
+// LLMOPT_DEVERR_* bits recorded by the quantized-linear kernels' bounded waits
+// on the current device (read, and cleared when `clear`).
+cudaError_t quant_linear_device_errors(unsigned* bits, bool clear);
 cudaError_t dequantize_launch(const QuantLinearArgs& a, void* out, int out_dtype,
                               cudaStream_t stream);
 

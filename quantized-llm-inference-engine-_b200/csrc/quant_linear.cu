@@ -37,9 +37,11 @@
 //   fixed order.
 // * wq_generic_kernel: CUDA cores, fp32 accumulation, any shape and dtype.
 #include <cstddef>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_common.cuh"
 
 namespace llmopt {
 namespace {
@@ -604,6 +606,247 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_acc_kernel(const QuantLinear
   }
 }
 
+// ---- 2- and 4-bit codes on the 5th-generation tensor cores (opt-in) ------------
+//
+// For token batches the weight is dequantized once per CTA into shared memory
+// and multiplied by tcgen05.mma.  A CTA owns 128 output features (TMEM lanes,
+// MMA M) and 64 tokens (MMA N) and walks its k range in 64-column slices:
+// * all 128 threads copy a slice's codes (128 rows x 32 bytes), token rows
+//   (64 x 128 bytes, in the 128-byte-swizzled K-major layout the MMA reads)
+//   and group constants with cp.async into a 4-stage ring;
+// * thread r dequantizes row r of the slice as the reference does, (q - z) * s
+//   in float32 rounded once to the compute dtype, into a swizzled K-major A
+//   tile (two A buffers), so the weights are the reference's bit for bit;
+// * one thread issues the slice's four MMAs (K = 16 each) into the fp32
+//   accumulator in tensor memory and commits them to an mbarrier.
+// Slice t waits only for the MMAs of slice t - 2, which free its A buffer and
+// the copy stage it refills, so one slice's dequantization overlaps the MMAs
+// of the one before.  The epilogue reads the accumulator with tcgen05.ld
+// (thread r = feature r, 32 tokens per load).  Every wait is bounded; a wait
+// that gives up sets g_wq_err and the CTA skips the rest of its MMAs.
+namespace tc05 {
+constexpr int kBM = 128;                    // features per CTA
+constexpr int kBN = 64;                     // tokens per CTA
+constexpr int kBK = 64;                     // k per slice (one 128-byte row of 16-bit values)
+constexpr int kThreads = 128;
+constexpr int kStages = 4;
+constexpr int kGroups = 2;                  // groups per slice at most (group 32)
+constexpr int kATile = kBM * 128;
+constexpr int kXTile = kBN * 128;
+constexpr int kCodes = kBM * 32;
+constexpr int kConsts = kBM * kGroups * 4;
+constexpr int kOffA = 0;                    // offsets from the 1024-byte aligned base
+constexpr int kOffX = kOffA + 2 * kATile;
+constexpr int kOffC = kOffX + kStages * kXTile;
+constexpr int kOffS = kOffC + kStages * kCodes;
+constexpr int kOffZ = kOffS + kStages * kConsts;
+constexpr int kOffBar = kOffZ + kStages * kConsts;
+constexpr int kSmem = kOffBar + 64 + 1024;  // barriers, TMEM address, alignment slack
+static_assert(kBN % 32 == 0 && kBN >= 32 && kBN <= 256, "TMEM columns / MMA N");
+static_assert(kBN * 8 % kThreads == 0, "token-row copy slots");
+}  // namespace tc05
+
+__device__ unsigned g_wq_err;               // LLMOPT_DEVERR_* bits of the tcgen05 path
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <int DT>
+__global__ void __launch_bounds__(tc05::kThreads) wq_gemm_tc05_kernel(const QuantLinearArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* mma_done = reinterpret_cast<uint64_t*>(base + tc05::kOffBar);   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + tc05::kOffBar + 16);
+  uint32_t* abort_flag = reinterpret_cast<uint32_t*>(base + tc05::kOffBar + 20);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const long long rbase = (long long)blockIdx.x * tc05::kBM;
+  const long long m0 = (long long)blockIdx.z * tc05::kBN;
+  const long long kb = (long long)blockIdx.y * a.k_per_split;
+  const long long ke = kb + a.k_per_split < a.k ? kb + a.k_per_split : a.k;
+  const int nslices = (int)((ke - kb) / tc05::kBK);
+  const long long mrem = a.m - m0;
+  const long long groups = a.k / a.group;
+  const long long row_bytes = a.k / 2;
+  const int gps = a.group >= tc05::kBK ? 1 : tc05::kBK / a.group;   // groups per slice: 1 or 2
+  const int sps = a.group >= tc05::kBK ? a.group / tc05::kBK : 1;   // slices per group
+  const int slice0 = (int)(kb / tc05::kBK);
+
+  if (tid == 0) {
+    mbar_init(&mma_done[0], 1);
+    mbar_init(&mma_done[1], 1);
+    *abort_flag = 0u;
+    mbar_init_fence();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, tc05::kBN);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  auto wait_mma = [&](int slice) {           // bounded; the first give-up aborts the CTA
+    if (*reinterpret_cast<volatile uint32_t*>(abort_flag) != 0u) return;
+    if (!mbar_wait(&mma_done[slice & 1], (unsigned)((slice >> 1) & 1))) {
+      atomicOr(&g_wq_err, kErrWaitTimeout | kErrWaitData);
+      *reinterpret_cast<volatile uint32_t*>(abort_flag) = 1u;
+    }
+  };
+
+  // Copy slots, fixed per thread.  Codes: row tid, its two 16-byte pieces,
+  // piece p stored at p ^ ((row >> 2) & 1) so a quarter warp's reads hit eight
+  // bank groups.  Token rows: rows tid/8 + 16 q, chunk tid % 8, stored at
+  // chunk position chunk ^ (row & 7) (the 128-byte swizzle).
+  const unsigned char* csrc = a.qweight + (rbase + tid) * row_bytes + kb / 2;
+  const int cdst0 = tid * 32 + 16 * ((tid >> 2) & 1);
+  const int cdst1 = tid * 32 + 16 * (1 ^ ((tid >> 2) & 1));
+  const int xr0 = tid >> 3;
+  const int xc = tid & 7;
+  const unsigned short* xsrc =
+      static_cast<const unsigned short*>(a.x) + (m0 + xr0) * a.ldx + kb + 8 * xc;
+  const int xdst = xr0 * 128 + 16 * (xc ^ (xr0 & 7));
+  const float* ssrc = a.scales + (rbase + tid) * groups;
+  const float* zsrc = a.zeros != nullptr ? a.zeros + (rbase + tid) * groups : nullptr;
+  // first group of slice t: (slice0 + t) * gps, or (slice0 + t) / sps; issue()
+  // runs for t = 0, 1, 2, ... in order and keeps a cursor
+  long long g_cur = gps > 1 ? (long long)slice0 * gps : slice0 / sps;
+  int g_in = gps > 1 ? 0 : slice0 % sps;
+
+  auto issue = [&](int t) {
+    const int st = t % tc05::kStages;
+    unsigned char* cst = base + tc05::kOffC + st * tc05::kCodes;
+    const unsigned char* src = csrc + (long long)t * (tc05::kBK / 2);
+    cp_async16(cst + cdst0, src, 16);
+    cp_async16(cst + cdst1, src + 16, 16);
+    unsigned char* xst = base + tc05::kOffX + st * tc05::kXTile;
+#pragma unroll
+    for (int q = 0; q < tc05::kBN * 8 / tc05::kThreads; ++q) {
+      const bool ok = xr0 + 16 * q < mrem;
+      // a row past the last token copies nothing (source size 0) from a valid address
+      cp_async16(xst + xdst + q * 16 * 128,
+                 ok ? xsrc + 16 * q * a.ldx + (long long)t * tc05::kBK
+                    : static_cast<const unsigned short*>(a.x),
+                 ok ? 16 : 0);
+    }
+    float* sst = reinterpret_cast<float*>(base + tc05::kOffS + st * tc05::kConsts) + tid * tc05::kGroups;
+    float* zst = reinterpret_cast<float*>(base + tc05::kOffZ + st * tc05::kConsts) + tid * tc05::kGroups;
+    for (int g = 0; g < gps; ++g) {
+      cp_async4(sst + g, ssrc + g_cur + g);
+      if (!a.symmetric) cp_async4(zst + g, zsrc + g_cur + g);
+    }
+    if (gps > 1) {
+      g_cur += gps;
+    } else if (++g_in == sps) {
+      g_in = 0;
+      ++g_cur;
+    }
+  };
+
+#pragma unroll
+  for (int t = 0; t < tc05::kStages - 2; ++t) {
+    if (t < nslices) issue(t);
+    cp_async_commit();
+  }
+  const float zsym = (float)(1 << (a.bits - 1));
+  const uint32_t idesc = tc::instr_desc_f16(DT == kBF16, tc05::kBM, tc05::kBN, false, false);
+  int last_committed = -1;                   // thread 0: the last slice whose MMAs it issued
+
+  for (int t = 0; t < nslices; ++t) {
+    cp_async_wait<tc05::kStages - 3>();
+    fence_proxy_async_smem();                // the copies, for the tensor core's reads
+    __syncthreads();                         // slice t landed for every thread
+    if (t >= 2) wait_mma(t - 2);             // frees A[t & 1] and stage (t - 2) % tc05::kStages
+    if (t + tc05::kStages - 2 < nslices) issue(t + tc05::kStages - 2);
+    cp_async_commit();
+    const int st = t % tc05::kStages;
+    const unsigned char* cst = base + tc05::kOffC + st * tc05::kCodes;
+    const uint4 c0 = *reinterpret_cast<const uint4*>(cst + cdst0);
+    const uint4 c1 = *reinterpret_cast<const uint4*>(cst + cdst1);
+    const float* sst = reinterpret_cast<const float*>(base + tc05::kOffS + st * tc05::kConsts) + tid * tc05::kGroups;
+    const float* zst = reinterpret_cast<const float*>(base + tc05::kOffZ + st * tc05::kConsts) + tid * tc05::kGroups;
+    unsigned char* arow = base + tc05::kOffA + (t & 1) * tc05::kATile + tid * 128;
+    const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {            // 16-byte chunk c of the row: codes 8c .. 8c + 7
+      const int g = gps > 1 ? (c >> 2) : 0;  // group 32: chunks 0-3 and 4-7
+      const float sc = sst[g];
+      const float zoff = 8388608.f + (a.symmetric ? zsym : zst[g]);
+      uint32_t pk[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {          // codes 2j (low nibble) and 2j + 1
+        const float f0 = __int_as_float(0x4B000000u | ((words[c] >> (8 * j)) & 0xFu)) - zoff;
+        const float f1 = __int_as_float(0x4B000000u | ((words[c] >> (8 * j + 4)) & 0xFu)) - zoff;
+        pk[j] = as_u32(Pair<DT>::pack(__fmul_rn(f0, sc), __fmul_rn(f1, sc)));
+      }
+      *reinterpret_cast<uint4*>(arow + 16 * (c ^ (tid & 7))) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+    fence_proxy_async_smem();                // A, for the tensor core's reads
+    __syncthreads();
+    if (tid == 0 && *reinterpret_cast<volatile uint32_t*>(abort_flag) == 0u) {
+      tc::fence_after_sync();
+      const uint32_t a_addr = smem_addr(base + tc05::kOffA + (t & 1) * tc05::kATile);
+      const uint32_t x_addr = smem_addr(base + tc05::kOffX + st * tc05::kXTile);
+#pragma unroll
+      for (int kk = 0; kk < tc05::kBK / 16; ++kk) {
+        tc::mma_f16(tmem, tc::smem_desc_sw128(a_addr + kk * 32, 16, 1024),
+                    tc::smem_desc_sw128(x_addr + kk * 32, 16, 1024), idesc,
+                    (t > 0 || kk > 0) ? 1u : 0u);
+      }
+      tc::commit(&mma_done[t & 1]);
+      last_committed = t;
+    }
+  }
+  cp_async_wait<0>();
+  // The last committed slice's commit covers every MMA the CTA issued: drained
+  // (bounded) even after an abort, before tensor memory is read or freed.
+  if (tid == 0 && last_committed >= 0) {
+    if (!mbar_wait(&mma_done[last_committed & 1], (unsigned)((last_committed >> 1) & 1))) {
+      atomicOr(&g_wq_err, kErrWaitTimeout | kErrWaitDrain);
+      *reinterpret_cast<volatile uint32_t*>(abort_flag) = 1u;
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const bool ok = *reinterpret_cast<volatile uint32_t*>(abort_flag) == 0u && nslices > 0;
+
+  // thread tid = feature rbase + tid = TMEM lane tid; columns = tokens m0 ..
+  const long long f = rbase + tid;
+  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  float bias = 0.f;
+  if (a.partial == nullptr && a.bias != nullptr) bias = load_f32<DT>(a.bias, f);
+#pragma unroll
+  for (int cb = 0; cb < tc05::kBN / 32; ++cb) {
+    float v[32];
+    tc::tmem_ld32(lane_addr + cb * 32, v);
+    tc::tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const long long tok = m0 + cb * 32 + j;
+      if (tok >= a.m) break;
+      const float val = ok ? v[j] : __int_as_float(0x7FC00000);   // NaN after a give-up
+      if (a.partial != nullptr) {
+        a.partial[((long long)blockIdx.y * a.m + tok) * a.n + f] = val;
+      } else {
+        store_f32<DT>(a.out, tok * a.ldo + f, val + bias);
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, tc05::kBN);
+  }
+}
+
 // Sum of the split partials (split order) plus the bias, cast to the compute dtype.
 template <int DT>
 __global__ void __launch_bounds__(256) wq_reduce_kernel(const QuantLinearArgs a) {
@@ -663,6 +906,38 @@ const void* gemm_fn(const QuantLinearArgs& a) {
   return a.x_dtype == kBF16 ? gemm_ptr<kBF16>(a, mt) : gemm_ptr<kF16>(a, mt);
 }
 
+// LLMOPT_B200_QUANT_TC05=1 routes 2- and 4-bit token batches (more than 8
+// tokens, n % 128 == 0) to wq_gemm_tc05_kernel.  Off by default: that kernel
+// has not been run on a GPU yet.
+bool tc05_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LLMOPT_B200_QUANT_TC05");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
+}
+
+// The tensor-core kernel a call runs and its CTA shape.
+struct GemmShape {
+  const void* fn;
+  int threads;
+  size_t smem;
+  long long rows;      // output features per CTA
+  long long tokens;    // tokens per CTA
+};
+
+GemmShape gemm_shape(const QuantLinearArgs& a) {
+  if (tc05_enabled() && a.bits < 8 && a.m > kMTSmall && a.n % tc05::kBM == 0 &&
+      (a.group == 32 || a.group % tc05::kBK == 0)) {
+    const void* fn = a.x_dtype == kBF16
+                         ? reinterpret_cast<const void*>(&wq_gemm_tc05_kernel<kBF16>)
+                         : reinterpret_cast<const void*>(&wq_gemm_tc05_kernel<kF16>);
+    return {fn, tc05::kThreads, (size_t)tc05::kSmem, tc05::kBM, tc05::kBN};
+  }
+  const int mt = tokens_per_cta(a);
+  return {gemm_fn(a), kThreads, gemm_smem(a, mt), kRows, mt};
+}
+
 long long grid_blocks(long long work, int threads) {
   long long b = (work + threads - 1) / threads;
   if (b > 148LL * 32) b = 148LL * 32;
@@ -684,15 +959,14 @@ bool quant_linear_tc_supported(const QuantLinearArgs& a) {
 // occupancy (one wave leaves a ragged tail when the tile count is not a
 // multiple of the slots; more splits cost partial traffic).
 int quant_linear_splits(const QuantLinearArgs& a, int sm_count) {
-  const int mt = tokens_per_cta(a);
-  const long long ctas = (a.n / kRows) * ((a.m + mt - 1) / mt);
+  const GemmShape g = gemm_shape(a);
+  const long long ctas = (a.n / g.rows) * ((a.m + g.tokens - 1) / g.tokens);
   const long long tiles = a.k / kKT;
-  const void* fn = gemm_fn(a);
-  const size_t smem = gemm_smem(a, mt);
   int occ = 1;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+  if (cudaFuncSetAttribute(g.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem) !=
           cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, smem) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, g.fn, g.threads, g.smem) !=
+          cudaSuccess ||
       occ < 1) {
     occ = 1;
   }
@@ -715,20 +989,26 @@ cudaError_t quant_linear_launch(const QuantLinearArgs& a, cudaStream_t stream) {
     if (gx > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidConfiguration;
     return launch_pdl(fn, dim3((unsigned)gx, (unsigned)gy), dim3(256), args, 0, stream);
   }
-  const void* fn = gemm_fn(a);
-  const int mt = tokens_per_cta(a);
-  const long long gx = a.n / kRows, gz = (a.m + mt - 1) / mt;
+  const GemmShape g = gemm_shape(a);
+  const long long gx = a.n / g.rows, gz = (a.m + g.tokens - 1) / g.tokens;
   if (gx > 0x7fffffffLL || gz > 65535 || a.splits > 65535) return cudaErrorInvalidConfiguration;
-  const size_t smem = gemm_smem(a, mt);
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e =
+      cudaFuncSetAttribute(g.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
   if (e != cudaSuccess) return e;
-  e = launch_pdl(fn, dim3((unsigned)gx, (unsigned)a.splits, (unsigned)gz), dim3(kThreads), args,
-                 smem, stream);
+  e = launch_pdl(g.fn, dim3((unsigned)gx, (unsigned)a.splits, (unsigned)gz),
+                 dim3((unsigned)g.threads), args, g.smem, stream);
   if (e != cudaSuccess || a.partial == nullptr) return e;
   const void* rfn = a.x_dtype == kBF16 ? reinterpret_cast<const void*>(&wq_reduce_kernel<kBF16>)
                                        : reinterpret_cast<const void*>(&wq_reduce_kernel<kF16>);
   return launch_pdl(rfn, dim3((unsigned)grid_blocks(a.m * a.n, 256)), dim3(256), args, 0,
                     stream);
+}
+
+cudaError_t quant_linear_device_errors(unsigned* bits, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(bits, g_wq_err, sizeof(unsigned));
+  if (e != cudaSuccess || !clear) return e;
+  const unsigned zero = 0u;
+  return cudaMemcpyToSymbol(g_wq_err, &zero, sizeof(unsigned));
 }
 
 cudaError_t dequantize_launch(const QuantLinearArgs& a, void* out, int out_dtype,
