@@ -2,6 +2,7 @@
 // split planning, TMA descriptor cache and kernel dispatch.  Apart from the
 // llmopt_peer_* buffer routines, no entry point allocates device memory or
 // synchronises the stream.
+#include <nvtx3/nvToolsExt.h>
 #include <cudaTypedefs.h>
 
 #include <cstdarg>
@@ -369,6 +370,18 @@ long long workspace_bound(long long batch, int num_heads, int kv_heads, int head
 
 }  // namespace
 
+namespace {
+// NVTX range around a C-ABI call, so the entry points appear by name on
+// Nsight timelines (header-only NVTX 3; a no-op unless a tool is attached).
+struct Range {
+  explicit Range(const char* name) { nvtxRangePushA(name); }
+  ~Range() { nvtxRangePop(); }
+  Range(const Range&) = delete;
+  Range& operator=(const Range&) = delete;
+};
+}  // namespace
+#define LLMOPT_RANGE(name) Range llmopt_range_(name)
+
 extern "C" {
 
 const char* llmopt_b200_version(void) { return "llmopt-b200 0.1.0 (sm_100a)"; }
@@ -423,6 +436,7 @@ int llmopt_paged_attention(const void* query, int32_t q_dtype, int64_t q_s, int6
                            int32_t q_len, float scale, float softcap, int64_t split_tokens,
                            void* workspace, size_t workspace_bytes, uint32_t* err,
                            void* stream) {
+  LLMOPT_RANGE("llmopt_paged_attention");
   return llmopt_paged_attention_phase(
       query, q_dtype, q_s, q_h, q_t, key_cache, value_cache, kv_dtype, num_layers, num_blocks,
       block_size, num_kv_heads, head_dim, layer_idx, block_table, table_is_i64, table_width,
@@ -573,6 +587,7 @@ int llmopt_paged_attention_phase(const void* query, int32_t q_dtype, int64_t q_s
                                  int32_t num_heads, int32_t q_len, float scale, float softcap,
                                  int64_t split_tokens, void* workspace, size_t workspace_bytes,
                                  uint32_t* err, void* stream, int32_t phases) {
+  LLMOPT_RANGE("llmopt_paged_attention_phase");
   return phase_impl(query, q_dtype, q_s, q_h, q_t, key_cache, value_cache, kv_dtype, num_layers,
                     num_blocks, block_size, num_kv_heads, head_dim, layer_idx, block_table,
                     table_is_i64, table_width, table_stride, context_lens, ctx_is_i64, out,
@@ -590,6 +605,7 @@ int llmopt_paged_attention_scaled(
     float* lse, int64_t batch, int32_t num_heads, int32_t q_len, float scale, float softcap,
     int64_t split_tokens, void* workspace, size_t workspace_bytes, uint32_t* err, void* stream,
     int32_t phases) {
+  LLMOPT_RANGE("llmopt_paged_attention_scaled");
   if (kv_dtype != kE4M3 || key_scale == nullptr || value_scale == nullptr) {
     return fail(LLMOPT_ERR_INVALID_ARGUMENT,
                 "llmopt_paged_attention_scaled takes an e4m3 cache and both scale arrays");
@@ -686,6 +702,7 @@ int llmopt_paged_attention_gather(
     int32_t out_dtype, float* lse, int64_t batch, int32_t num_heads, int32_t q_len, float scale,
     float softcap, int64_t split_tokens, void* workspace, size_t workspace_bytes,
     uint32_t* err, void* stream, int32_t phases) {
+  LLMOPT_RANGE("llmopt_paged_attention_gather");
   if (world < 1 || world > LLMOPT_MAX_PEERS || rank < 0 || rank >= world) {
     return fail(LLMOPT_ERR_INVALID_ARGUMENT, "rank %d of world %d (at most %d ranks)", rank,
                 world, LLMOPT_MAX_PEERS);
@@ -796,6 +813,7 @@ int llmopt_quant_linear(const void* x, int32_t x_dtype, int64_t m, int64_t ldx,
                         int32_t symmetric, const float* scales, const float* zeros, int64_t n,
                         int64_t k, const void* bias, void* out, int64_t ldo, void* workspace,
                         size_t workspace_bytes, void* stream) {
+  LLMOPT_RANGE("llmopt_quant_linear");
   if (!valid_dtype(x_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype %d", x_dtype);
   QuantLinearArgs a{};
   int st = quant_args(qweight, bits, group_size, symmetric, scales, zeros, n, k, &a);
@@ -833,6 +851,7 @@ int llmopt_quant_linear(const void* x, int32_t x_dtype, int64_t m, int64_t ldx,
 int llmopt_dequantize(const void* qweight, int32_t bits, int32_t group_size, int32_t symmetric,
                       const float* scales, const float* zeros, int64_t n, int64_t k, void* out,
                       int32_t out_dtype, void* stream) {
+  LLMOPT_RANGE("llmopt_dequantize");
   if (!valid_dtype(out_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype %d", out_dtype);
   QuantLinearArgs a{};
   int st = quant_args(qweight, bits, group_size, symmetric, scales, zeros, n, k, &a);
@@ -855,6 +874,7 @@ int llmopt_quant_linear_device_errors(int32_t clear, uint32_t* bits) {
 int llmopt_merge_states(const void* o1, const void* o2, const void* l1, const void* l2,
                         void* out, void* lse_out, int64_t rows, int32_t head_dim,
                         int32_t o_dtype, int32_t lse_dtype, void* stream) {
+  LLMOPT_RANGE("llmopt_merge_states");
   if (!valid_dtype(o_dtype) || !valid_dtype(lse_dtype)) {
     return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported dtype");
   }
@@ -981,6 +1001,7 @@ int llmopt_kv_write(const void* keys, const void* values, int32_t in_dtype, int6
                     int32_t table_is_i64, int64_t table_width, int64_t table_stride,
                     const void* token_offsets, int32_t off_is_i64, int64_t batch, int32_t q_len,
                     uint32_t* err, void* stream) {
+  LLMOPT_RANGE("llmopt_kv_write");
   if (!valid_dtype(kv_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported cache dtype");
   return kv_write_impl(keys, values, in_dtype, k_s, k_t, k_h, v_s, v_t, v_h, key_cache,
                        value_cache, kv_dtype, nullptr, nullptr, num_layers, num_blocks,
@@ -998,6 +1019,7 @@ int llmopt_kv_write_scaled(const void* keys, const void* values, int32_t in_dtyp
                            int32_t table_is_i64, int64_t table_width, int64_t table_stride,
                            const void* token_offsets, int32_t off_is_i64, int64_t batch,
                            int32_t q_len, uint32_t* err, void* stream) {
+  LLMOPT_RANGE("llmopt_kv_write_scaled");
   const int st = check_e4m3(kv_dtype, key_scale, value_scale, head_dim);
   if (st != LLMOPT_OK) return st;
   return kv_write_impl(keys, values, in_dtype, k_s, k_t, k_h, v_s, v_t, v_h, key_cache,
@@ -1072,6 +1094,7 @@ int llmopt_kv_write_decode(const void* keys, const void* values, int32_t in_dtyp
                            int32_t table_is_i64, int64_t table_width, int64_t table_stride,
                            const void* token_offsets, int32_t off_is_i64, int64_t batch,
                            uint32_t* err, void* stream) {
+  LLMOPT_RANGE("llmopt_kv_write_decode");
   if (!valid_dtype(kv_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported cache dtype");
   return kv_write_decode_impl(keys, values, in_dtype, k_s, k_h, v_s, v_h, key_cache, value_cache,
                               kv_dtype, nullptr, nullptr, num_layers, num_blocks, block_size,
@@ -1090,6 +1113,7 @@ int llmopt_kv_write_decode_scaled(const void* keys, const void* values, int32_t 
                                   int64_t table_stride, const void* token_offsets,
                                   int32_t off_is_i64, int64_t batch, uint32_t* err,
                                   void* stream) {
+  LLMOPT_RANGE("llmopt_kv_write_decode_scaled");
   const int st = check_e4m3(kv_dtype, key_scale, value_scale, head_dim);
   if (st != LLMOPT_OK) return st;
   return kv_write_decode_impl(keys, values, in_dtype, k_s, k_h, v_s, v_h, key_cache, value_cache,
@@ -1157,6 +1181,7 @@ int llmopt_paged_gather(const void* key_cache, const void* value_cache, int32_t 
                         int64_t table_stride, const void* context_lens, int32_t ctx_is_i64,
                         int64_t batch, int64_t max_len, void* out_keys, void* out_values,
                         uint8_t* valid, uint32_t* err, void* stream) {
+  LLMOPT_RANGE("llmopt_paged_gather");
   if (!valid_dtype(kv_dtype)) return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported cache dtype");
   return gather_impl(key_cache, value_cache, kv_dtype, nullptr, nullptr, num_layers, num_blocks,
                      block_size, num_kv_heads, head_dim, layer_idx, block_table, table_is_i64,
@@ -1173,6 +1198,7 @@ int llmopt_paged_gather_scaled(const void* key_cache, const void* value_cache, i
                                const void* context_lens, int32_t ctx_is_i64, int64_t batch,
                                int64_t max_len, float* out_keys, float* out_values,
                                uint8_t* valid, uint32_t* err, void* stream) {
+  LLMOPT_RANGE("llmopt_paged_gather_scaled");
   const int st = check_e4m3(kv_dtype, key_scale, value_scale, head_dim);
   if (st != LLMOPT_OK) return st;
   return gather_impl(key_cache, value_cache, kv_dtype, key_scale, value_scale, num_layers,
@@ -1194,6 +1220,7 @@ extern "C" int llmopt_rope_kv_append(
     int32_t table_is_i64, int64_t table_width, int64_t table_stride, const void* token_offsets,
     int32_t off_is_i64, int64_t batch, int32_t num_heads, int32_t q_len, uint32_t* err,
     void* stream) {
+  LLMOPT_RANGE("llmopt_rope_kv_append");
   if (!valid_dtype(in_dtype) || !valid_dtype(table_dtype)) {
     return fail(LLMOPT_ERR_UNSUPPORTED, "unsupported input or table dtype");
   }
@@ -1282,6 +1309,7 @@ extern "C" int llmopt_decode_step_advance(const int64_t* updates, int64_t capaci
                                           int64_t* token_offsets, int64_t* positions,
                                           int64_t max_rows, int64_t batch, uint32_t* err,
                                           void* stream) {
+  LLMOPT_RANGE("llmopt_decode_step_advance");
   if (capacity < 0 || table_width < 1 || table_stride < table_width || max_rows < 1 ||
       batch < 0 || batch > max_rows) {
     return fail(LLMOPT_ERR_INVALID_ARGUMENT, "invalid step-state shape");
@@ -1367,6 +1395,7 @@ extern "C" int llmopt_paged_attention_noalloc(
     int32_t out_dtype, int64_t o_s, int64_t o_h, int64_t o_t, float* lse, int64_t batch,
     int32_t num_heads, int32_t q_len, float scale, float softcap, int64_t split_tokens,
     uint32_t* err, void* stream) {
+  LLMOPT_RANGE("llmopt_paged_attention_noalloc");
   if (batch <= 0 || q_len <= 0) {
     // Nothing to launch; the regular entry validates the remaining arguments.
     return llmopt_paged_attention(query, q_dtype, q_s, q_h, q_t, key_cache, value_cache,
