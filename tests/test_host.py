@@ -42,6 +42,45 @@ def test_ctypes_binding_covers_the_header(pkg):
     assert set(header_symbols()) == set(_lib.SIGNATURES)
 
 
+C_HOST = r"""
+#include <stdio.h>
+#include <string.h>
+#include "llmopt_b200.h"
+
+int main(void) {
+  size_t bytes = 1;
+  /* num_heads not a multiple of num_kv_heads: refused before any device work */
+  int st = llmopt_paged_attention_workspace_size(0, 4, 6, 4, 64, 1, 16, 8,
+                                                 LLMOPT_DTYPE_BF16, LLMOPT_SPLIT_AUTO, &bytes);
+  printf("%s|%d|%d|%s|%d\n", llmopt_b200_version(), llmopt_b200_abi_version(), st,
+         llmopt_status_string(st), (int)(strlen(llmopt_last_error()) > 0));
+  return 0;
+}
+"""
+
+
+def test_header_is_c_and_links_from_a_c_host(pkg, tmp_path):
+    """A C99 host compiles against the header with warnings as errors, links
+    the library and calls its GPU-free entry points."""
+    import shutil
+    import subprocess
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "host.c"
+    src.write_text(C_HOST)
+    exe = tmp_path / "host"
+    libdir = os.path.dirname(pkg.__file__)
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-I",
+                    os.path.join(REPO, "include"), str(src), "-L", libdir, "-lllmopt_b200",
+                    f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.strip()
+    version, abi, status, status_name, has_msg = out.split("|")
+    assert "sm_100a" in version and abi == "1"
+    assert int(status) == 1 and status_name and has_msg == "1"
+
+
 def test_version_and_status_strings_without_gpu(pkg):
     lib = pkg.lib()
     assert b"sm_100a" in lib.llmopt_b200_version()
