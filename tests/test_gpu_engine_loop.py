@@ -47,8 +47,9 @@ def _weights(dev):
     layers = [dict(wq=rnd(H * D, DM, scale=s), wk=rnd(KVH * D, DM, scale=s),
                    wv=rnd(KVH * D, DM, scale=s), wo=rnd(DM, H * D, scale=(H * D) ** -0.5))
               for _ in range(L)]
-    return rnd(V, DM), layers, [int(t) for t in torch.randint(0, V, (sum(PROMPTS),),
-                                                               generator=g)]
+    emb, head = rnd(V, DM), rnd(V, DM, scale=s)       # untied output head
+    prompts = [int(t) for t in torch.randint(0, V, (sum(PROMPTS),), generator=g)]
+    return emb, head, layers, prompts
 
 
 def _rotate_half(x):
@@ -56,7 +57,7 @@ def _rotate_half(x):
     return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
 
 
-def stateless_logits(tokens, emb, layers, cos, sin):
+def stateless_logits(tokens, emb, head, layers, cos, sin):
     """[T, V] logits of one sequence, recomputed from its tokens alone (fp32)."""
     T = len(tokens)
     x = emb[torch.tensor(tokens, device=emb.device)]
@@ -74,12 +75,12 @@ def stateless_logits(tokens, emb, layers, cos, sin):
         scores = scores.masked_fill(~causal, float("-inf"))
         o = torch.einsum("htu,uhd->thd", scores.softmax(dim=-1), v).reshape(T, H * D)
         x = x + o @ lw["wo"].T
-    return x @ emb.T
+    return x @ head.T
 
 
 def test_paged_greedy_decode_equals_stateless_forward(cuda):
     pkg = load_package()
-    emb, layers, prompt_tokens = _weights(cuda)
+    emb, head, layers, prompt_tokens = _weights(cuda)
     rot = pkg.RotaryEmbedding(D, 256, device=cuda)
     cache = pkg.PagedKVCache(L, NB, BS, KVH, D, dtype=torch.float32, device=cuda)
     attn = pkg.PagedAttention(H, KVH, D)
@@ -97,7 +98,7 @@ def test_paged_greedy_decode_equals_stateless_forward(cuda):
                                    num_heads=H)
             o = attn.forward(q, cache, li, rows, ctx)             # [seq, H, q_len, D]
             x = x + o.permute(0, 2, 1, 3).reshape(n, H * D) @ lw["wo"].T
-        return x @ emb.T
+        return x @ head.T
 
     seqs, start = [], 0
     for s, plen in enumerate(PROMPTS):                           # prefill, one sequence at a time
@@ -119,10 +120,12 @@ def test_paged_greedy_decode_equals_stateless_forward(cuda):
 
     checked = 0
     for s, plen in enumerate(PROMPTS):
-        full = stateless_logits(seqs[s][:-1], emb, layers, rot.cos_cached, rot.sin_cached)
+        full = stateless_logits(seqs[s][:-1], emb, head, layers, rot.cos_cached,
+                                rot.sin_cached)
         for t in range(plen - 1, len(seqs[s]) - 1):
             top2 = full[t].topk(2).values
             if float(top2[0] - top2[1]) > 1e-3:
                 assert int(full[t].argmax()) == seqs[s][t + 1], (s, t)
                 checked += 1
     assert checked >= B * STEPS // 2
+    assert all(len(set(t[p:])) > 3 for t, p in zip(seqs, PROMPTS))   # not one repeated token
