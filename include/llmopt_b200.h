@@ -227,7 +227,10 @@ LLMOPT_API int llmopt_peer_free(int32_t device, void* ptr);
  * and flag buffer (LLMOPT_PEER_FLAGS_BYTES, zeroed before first use), as
  * mapped in this process; gathered[rank] / flags[rank] are this rank's own.
  * Every rank makes the same sequence of calls with the same shapes, each with
- * an `epoch` one above its previous call (starting at 1).  When the COMBINE
+ * an `epoch` one above its previous call, modulo 2^32 (starting at 1; 0
+ * follows 0xFFFFFFFF: arrivals are compared by serial-number arithmetic, so
+ * the count may wrap, as long as ranks stay within 2^31 calls of each other).
+ * When the COMBINE
  * kernel ends, this rank's gathered output holds every rank's heads.  Peers
  * write a call's rows into gathered[] while this rank may still be reading
  * the previous call's: alternate two gathered buffers between calls.  A peer

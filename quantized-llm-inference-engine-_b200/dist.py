@@ -116,6 +116,16 @@ class _RawDevice:
                                          "data": (ptr, False), "version": 2, "strides": None}
 
 
+def _next_epoch(epoch: int) -> int:
+    """The epoch after ``epoch``, modulo 2^32.
+
+    The first call gets 1 (the flags start at 0).  After 0xFFFFFFFF comes 0:
+    the kernel compares flags by serial-number arithmetic, and the parity keeps
+    alternating the two gathered buffers across the wrap.
+    """
+    return (epoch + 1) & 0xFFFFFFFF
+
+
 @dataclass
 class _Mapped:
     nbytes: int
@@ -183,7 +193,7 @@ class PeerGroup:
     def next_call(self, nbytes: int):
         """Epoch, buffer index and ctypes pointer arrays for the next gathered call."""
         self.reserve(nbytes)
-        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        self.epoch = _next_epoch(self.epoch)
         which = self.epoch & 1
         arrays = self._arrays.get(which)
         if arrays is None:
@@ -284,7 +294,7 @@ class ShardedPagedAttention:
             # The split phase touches no peer memory; it only needs the shapes
             # and this rank's slice of the buffer the next combine will use.
             self.peers.reserve(nbytes)
-            epoch = (self.peers.epoch + 1) & 0xFFFFFFFF or 1
+            epoch = _next_epoch(self.peers.epoch)
             which = epoch & 1
             bufs = flags = None
         full = self.peers.local_buffer(which)[:nbytes].view(dtype).view(

@@ -143,6 +143,10 @@ def _peer_group_worker(rank: int, world: int, port: int, result_q):
         checks.append((e3, w3) == (3, 1))
         checks.append(all(b.nbytes == 4 << 20 for b in pg._bufs))
         checks.append(sorted(mem.freed) == sorted(old))
+        # the epoch wraps modulo 2^32 and keeps alternating the two buffers
+        pg.epoch = 0xFFFFFFFE
+        wrap = [pg.next_call(1000)[:2] for _ in range(3)]
+        checks.append(wrap == [(0xFFFFFFFF, 1), (0, 0), (1, 1)])
         pg.close()
         checks.append(not mem.live and sorted(mem.closed) == sorted(mem.opened))
         checks.append(len(mem.opened) == 5 * (world - 1))   # flags + 2 + 2 buffers per peer
