@@ -394,4 +394,14 @@ QUANT_CASES = {
                                                   group=64, symmetric=True, m=6, kind="bf16"),
     "quant_rtn4_asym_g64_f16": lambda: case_quant(47, out_features=64, in_features=192, bits=4,
                                                   group=64, symmetric=False, m=3, kind="f16"),
+    # one group per row (the quantizers take group_size = in_features)
+    "quant_rtn4_asym_row_bf16": lambda: case_quant(48, out_features=64, in_features=256, bits=4,
+                                                   group=256, symmetric=False, m=9, kind="bf16"),
+    "quant_gptq4_asym_g128_bf16": lambda: case_quant(49, out_features=64, in_features=256,
+                                                     bits=4, group=128, symmetric=False, m=5,
+                                                     kind="bf16", strategy="gptq", calib=96),
+    "quant_rtn2_asym_g64_f16": lambda: case_quant(50, out_features=64, in_features=256, bits=2,
+                                                  group=64, symmetric=False, m=7, kind="f16"),
+    "quant_rtn8_sym_g128_bf16": lambda: case_quant(51, out_features=64, in_features=256, bits=8,
+                                                   group=128, symmetric=True, m=33, kind="bf16"),
 }
