@@ -130,6 +130,23 @@ def case_f16_decode(seed: int = 5) -> dict:
                             ctx=[9, 64, 129], kv_kind="f16", q_kind="f16")
 
 
+def case_bf16_decode_d256(seed: int = 6) -> dict:
+    """head_dim 256 (the largest the tensor-core decode takes), group 4."""
+    return build_paged_case(seed, batch=4, heads=8, kv_heads=2, head_dim=256, block_size=16,
+                            ctx=[3, 64, 250, 511], kv_kind="bf16", q_kind="bf16",
+                            value_scale=0.5)
+
+
+def case_f16_prefill(seed: int = 7) -> dict:
+    """fp16 chunked prefill on the tensor-core path: q_len 24 x group 4 = 96 rows,
+    prefixes 40 (unaligned) and 100."""
+    prefix = np.array([40, 100])
+    q_len = 24
+    return build_paged_case(seed, batch=2, heads=8, kv_heads=2, head_dim=128, block_size=16,
+                            ctx=prefix + q_len, kv_kind="f16", q_kind="f16", q_len=q_len,
+                            value_scale=0.5)
+
+
 ATTENTION_CASES = {
     "c1": case_c1,
     "bf16_decode": case_bf16_decode,
@@ -138,6 +155,8 @@ ATTENTION_CASES = {
     "edge_f32_q3": lambda: case_edge_f32(q_len=3),
     "mixed_q": case_mixed_q,
     "f16_decode": case_f16_decode,
+    "bf16_decode_d256": case_bf16_decode_d256,
+    "f16_prefill": case_f16_prefill,
 }
 
 #: (name, softcap, split_kv, split_size or None for the case default) runs recorded per case.
@@ -149,6 +168,8 @@ ATTENTION_RUNS = {
     "edge_f32_q3": [("dense", 0.0, False, 512), ("split", 0.0, True, 3), ("softcap", 5.0, False, 512)],
     "mixed_q": [("dense", 0.0, False, 512), ("split", 0.0, True, 16)],
     "f16_decode": [("dense", 0.0, False, 512), ("split", 2.5, True, 24)],
+    "bf16_decode_d256": [("dense", 0.0, False, 512), ("split", 0.0, True, 64)],
+    "f16_prefill": [("dense", 0.0, False, 512), ("split", 0.0, True, 32)],
 }
 
 

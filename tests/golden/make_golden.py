@@ -2,7 +2,7 @@
 
 Run once, in a container where the reference source is present::
 
-    python tests/golden/make_golden.py /path/to/reference/src [--only=rope|step|quant]
+    python tests/golden/make_golden.py /path/to/reference/src [--only=attn|rope|step|quant]
 
 It imports ``llmopt.attention`` / ``llmopt.cache`` from that path, runs them
 on CPU on the seeded inputs of ``cases.py`` (plus the reference's own
@@ -371,6 +371,8 @@ def main(ref_src: str, only: str | None = None) -> None:
         out["versions"] = np.array(str(meta))
         np.savez_compressed(os.path.join(HERE, f"attn_{name}.npz"), **out)
         print("wrote", name)
+    if only == "attn":
+        return
     for name, build in cases.WRITE_CASES.items():
         out = make_write(name, build, PagedKVCache)
         out["versions"] = np.array(str(meta))
