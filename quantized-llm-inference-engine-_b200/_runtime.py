@@ -25,6 +25,10 @@ CHECK = os.environ.get("LLMOPT_B200_CHECK", "0") not in ("", "0", "false", "Fals
 
 _lock = threading.Lock()
 _workspaces: dict[int, torch.Tensor] = {}
+# Outgrown workspaces are kept, not freed: a CUDA graph captured earlier still
+# launches kernels on their addresses.  Growth doubles, so they add up to less
+# than the current buffer.
+_retired: list[torch.Tensor] = []
 _err_words: dict[int, torch.Tensor] = {}
 
 
@@ -50,7 +54,8 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
 
     One buffer serves every call on the device.  Calls issued on one stream
     are ordered by it, which is how the engine runs (one stream, one lock);
-    calls overlapping on two streams would share the buffer.
+    calls overlapping on two streams would share the buffer.  A buffer that
+    is outgrown stays allocated, so graphs captured with it stay valid.
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
     with _lock:
@@ -59,6 +64,8 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
             # Round up so slowly growing shapes do not reallocate every call.
             size = max(nbytes, 1 << 20)
             size = 1 << (size - 1).bit_length()
+            if buf is not None:
+                _retired.append(buf)
             buf = torch.empty(size, dtype=torch.uint8, device=torch.device("cuda", idx))
             _workspaces[idx] = buf
         return buf
