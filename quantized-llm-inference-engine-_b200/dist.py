@@ -249,7 +249,6 @@ class ShardedPagedAttention:
         self.local = PagedAttention(self.shard.q_heads, self.shard.kv_heads, head_dim,
                                     scale=scale if scale is not None else head_dim ** -0.5,
                                     config=config, split_mode=split_mode)
-        self._bufs: dict = {}
         self.peers: PeerGroup | None = None
 
     def local_query(self, query: torch.Tensor) -> torch.Tensor:
@@ -257,13 +256,11 @@ class ShardedPagedAttention:
         return query[:, self.shard.q_lo:self.shard.q_hi]
 
     def _buffer(self, seq: int, q_len: int, dtype, device) -> torch.Tensor:
-        key = (seq, q_len, dtype, device)
-        buf = self._bufs.get(key)
-        if buf is None:
-            buf = torch.empty((self.shard.q_heads, seq, q_len, self.head_dim), dtype=dtype,
-                              device=device)
-            self._bufs = {key: buf}
-        return buf
+        # A fresh all-gather input per call (the caching allocator makes it cheap):
+        # a cached one replaced when the shape changes would leave a captured CUDA
+        # graph writing into freed memory.
+        return torch.empty((self.shard.q_heads, seq, q_len, self.head_dim), dtype=dtype,
+                           device=device)
 
     def forward(self, query_local: torch.Tensor, cache: PagedKVCache, layer_idx: int,
                 block_ids: torch.Tensor, context_lens: torch.Tensor,
