@@ -141,7 +141,9 @@ class PeerGroup:
     collectively (synchronise, barrier, unmap, free, allocate, exchange the
     IPC handles with ``all_gather_object``, map); the steady state allocates
     nothing.  Calls alternate between the two buffers, so the result of one
-    call stays intact until the call after next.
+    call stays intact until the call after next.  Growth replaces the
+    buffers, so before capturing calls in a CUDA graph ``reserve`` the largest
+    size the graph will need.
     """
 
     def __init__(self, group=None, device: torch.device | None = None, memory=None) -> None:
