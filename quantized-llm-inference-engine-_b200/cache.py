@@ -163,6 +163,8 @@ class PagedKVCache:
             raise ValueError(f"keys/values must be [seq, q_len, {self.num_kv_heads}, {self.head_dim}]")
         table, t64 = rt.index_tensor(block_ids, self.device, "block_ids")
         offs, o64 = rt.index_tensor(token_offsets, self.device, "token_offsets")
+        if table.dim() != 2 or table.shape[0] < seq_len or offs.shape[0] < seq_len:
+            raise IndexError("block_ids/token_offsets have fewer rows than keys")
         err = rt.err_word(self.device)
         L = _lib.lib()
         fn, pool = ((L.llmopt_kv_write_scaled, self._scaled_pool_args(layer)) if self.is_fp8
@@ -194,7 +196,7 @@ class PagedKVCache:
         layer = self._layer(layer_idx)
         table, t64 = rt.index_tensor(block_ids, self.device, "block_ids")
         offs, o64 = rt.index_tensor(token_offsets, self.device, "token_offsets")
-        if table.shape[0] < seq_len or offs.shape[0] < seq_len:
+        if table.dim() != 2 or table.shape[0] < seq_len or offs.shape[0] < seq_len:
             raise IndexError("block_ids/token_offsets have fewer rows than keys")
         err = rt.err_word(self.device)
         L = _lib.lib()
@@ -216,6 +218,8 @@ class PagedKVCache:
         layer = self._layer(layer_idx)
         self._check_storage()
         ctx, c64 = rt.index_tensor(context_lens, self.device, "context_lens")
+        if ctx.dim() != 1 or ctx.shape[0] < seq_len:
+            raise IndexError("context_lens has fewer entries than block_ids rows")
         max_len = int(ctx.max().item()) if seq_len else 0
         head = (self.num_kv_heads, self.head_dim)
         out_dtype = torch.float32 if self.is_fp8 else self.dtype

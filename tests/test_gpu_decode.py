@@ -256,6 +256,24 @@ def test_shared_prefix_blocks_give_identical_outputs(cuda):
         assert_lse_close(lse, want_lse, f"shared prefix lse {mode}")
 
 
+def test_short_tables_raise_before_any_launch(cuda):
+    """A block table, offsets or lengths with fewer rows than the batch raise
+    IndexError (the reference's torch indexing raises) instead of launching a
+    kernel that would read past them."""
+    pkg = load_package()
+    cache = pkg.PagedKVCache(1, 8, 16, 2, 64, dtype=torch.bfloat16, device=cuda)
+    table = torch.zeros(1, 2, dtype=torch.int32, device=cuda)
+    offs = torch.zeros(1, dtype=torch.int64, device=cuda)
+    keys = torch.zeros(2, 3, 2, 64, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(IndexError):
+        cache.write(0, table, offs, keys, keys)
+    with pytest.raises(IndexError):
+        cache.write_decode(0, table, offs, keys[:, 0], keys[:, 0])
+    with pytest.raises(IndexError):
+        cache.gather(0, torch.zeros(2, 2, dtype=torch.int32, device=cuda), offs + 1)
+    assert device_errors(cuda) == 0
+
+
 def test_q_len_zero_and_empty_batch(cuda):
     pkg = load_package()
     cache = pkg.PagedKVCache(1, 4, 16, 2, 64, dtype=torch.bfloat16, device=cuda)
