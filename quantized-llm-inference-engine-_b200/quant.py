@@ -82,8 +82,7 @@ class QuantLinear(nn.Module):
             # reference, so .to() does not move it: move it once here
             self.qweight = self.qweight.to(device)
         qweight = self.qweight.contiguous()
-        if qweight.dtype not in (torch.uint8, torch.int8):
-            raise ValueError(f"qweight must be uint8/int8, got {qweight.dtype}")
+        _check_qweight(qweight, self.out_features, self.in_features, cfg.bits)
         scales = self.scales.to(device=device, dtype=torch.float32).contiguous()
         zeros = self.qzeros.to(device=device, dtype=torch.float32).contiguous()
         groups = self.in_features // cfg.group_size if cfg.group_size > 0 else 1
@@ -129,6 +128,16 @@ class QuantLinear(nn.Module):
                 f"bits={self.config.bits}, bias={self.bias is not None}")
 
 
+def _check_qweight(qweight: torch.Tensor, n: int, k: int, bits: int) -> None:
+    """The reference's packed layout: [n, k/2] bytes for 2/4-bit codes, [n, k] for 8-bit."""
+    if qweight.dtype not in (torch.uint8, torch.int8):
+        raise ValueError(f"qweight must be uint8/int8, got {qweight.dtype}")
+    want = (n, k if bits == 8 else k // 2)
+    if tuple(qweight.shape) != want:
+        raise ValueError(f"qweight must be {list(want)} for {bits}-bit codes, got "
+                         f"{list(qweight.shape)}")
+
+
 def quant_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
                  zeros: torch.Tensor | None, bias: torch.Tensor | None, bits: int,
                  group_size: int, symmetric: bool) -> torch.Tensor:
@@ -151,8 +160,7 @@ def quant_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
     for t, name in ((qweight, "qweight"), (scales, "scales")):
         if t.device != device:
             raise ValueError(f"{name} must be on {device}")
-    if qweight.dtype not in (torch.uint8, torch.int8):
-        raise ValueError(f"qweight must be uint8/int8, got {qweight.dtype}")
+    _check_qweight(qweight, n, k, bits)
     if scales.dtype != torch.float32 or not scales.is_contiguous():
         scales = scales.to(torch.float32).contiguous()
     if zeros is not None and zeros.numel():

@@ -167,6 +167,18 @@ def test_ops_refuse_cpu_tensors(pkg):
                            4, 128, True)
 
 
+def test_quant_weight_layout_is_checked(pkg):
+    from importlib import import_module
+
+    quant = import_module("quantized-llm-inference-engine-_b200.quant")
+    quant._check_qweight(torch.zeros(64, 64, dtype=torch.uint8), 64, 128, 4)
+    quant._check_qweight(torch.zeros(64, 128, dtype=torch.int8), 64, 128, 8)
+    with pytest.raises(ValueError, match="qweight must be"):
+        quant._check_qweight(torch.zeros(64, 128, dtype=torch.uint8), 64, 128, 4)
+    with pytest.raises(ValueError, match="uint8/int8"):
+        quant._check_qweight(torch.zeros(64, 64, dtype=torch.int32), 64, 128, 4)
+
+
 def test_cache_from_storage_validates(pkg):
     kc = torch.zeros(1, 4, 16, 2, 64, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
