@@ -170,7 +170,7 @@ class ClockSampler:
                 self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
             except Exception:
                 pass
-            time.sleep(0.005)
+            time.sleep(0.0005)
 
     def start(self):
         if self._handle is not None:
@@ -184,6 +184,30 @@ class ClockSampler:
         names = sorted(n for bit, n in _REASONS.items() if self.reasons & bit)
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+KERNEL_ITERS = 200
+
+
+def kernel_loop_ms(fn, dev, barrier, iters: int = KERNEL_ITERS) -> float:
+    """Average device time of ``fn`` over ``iters`` back-to-back calls.
+
+    Two events on the current stream bracket the loop (the stream every kernel
+    of the step is launched on); three untimed calls come first.
+    """
+    import torch
+
+    for _ in range(3):
+        fn()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    barrier()
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b) / iters
 
 
 # ---------------------------------------------------------------------------
@@ -352,30 +376,32 @@ def run_ours(args) -> None:
     sharded_step = (pdist.ShardedPagedAttention(HEADS, KV_HEADS, HEAD_DIM, transport="peer")
                     if peer else None)
 
-    def step(ev=None):
-        if ev is not None:
-            ev[0].record()
+    def append():
         cache.write_decode(0, table, offs, knew, vnew)
-        if ev is not None:
-            ev[1].record()
+
+    def decode():
         if peer:
             sharded_step.forward(q, cache, 0, table, ctx, 1, phases=_lib.PHASE_SPLIT)
         else:
             attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out_view,
                                   phases=_lib.PHASE_SPLIT)
-        if ev is not None:
-            ev[2].record()
+
+    def combine():
         if peer:
             sharded_step.forward(q, cache, 0, table, ctx, 1, phases=_lib.PHASE_COMBINE)
         else:
             attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out_view,
                                   phases=_lib.PHASE_COMBINE)
-        if ev is not None:
-            ev[3].record()
+
+    def gather():
         if gathered is not None:
             dist.all_gather_into_tensor(gathered, head_major)
-        if ev is not None:
-            ev[4].record()
+
+    def step():
+        append()
+        decode()
+        combine()
+        gather()
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -385,32 +411,31 @@ def run_ours(args) -> None:
 
     for _ in range(max(args.warmup, 3)):
         step()
-    # Per-kernel events break the programmatic-launch overlap between the
-    # step's kernels, so only every EVERY-th timed step carries them; the step
-    # time itself is the whole timed region.
-    every = 10
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)]
-           for _ in range((args.steps + every - 1) // every)]
+    # The timed region holds the steps and nothing else: an event between two
+    # kernels would break the programmatic-launch overlap of the step.
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local)
     barrier()
     sampler.start()
     start.record()
-    for i in range(args.steps):
-        step(evs[i // every] if i % every == 0 else None)
+    for _ in range(args.steps):
+        step()
     end.record()
     torch.cuda.synchronize(dev)
     clocks = sampler.stop()
     ms_total = start.elapsed_time(end)
-    append_ms = statistics.fmean(e[0].elapsed_time(e[1]) for e in evs)
-    decode_ms = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
-    combine_ms = statistics.fmean(e[2].elapsed_time(e[3]) for e in evs)
-    gather_ms = statistics.fmean(e[3].elapsed_time(e[4]) for e in evs)
     if world > 1:
         t = torch.tensor([ms_total], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
+    # Per-kernel durations (the roofline's denominator): each kernel of the
+    # step alone, KERNEL_ITERS launches back to back on the launching stream,
+    # after the timed region.
+    append_ms = kernel_loop_ms(append, dev, barrier)
+    decode_ms = kernel_loop_ms(decode, dev, barrier)
+    combine_ms = kernel_loop_ms(combine, dev, barrier)
+    gather_ms = kernel_loop_ms(gather, dev, barrier) if gathered is not None else 0.0
     ms_step = ms_total / args.steps
     dec_bytes, app_bytes = step_bytes(wl["ctx"], kvh, qh, B)
     value = world * (dec_bytes + app_bytes) / (ms_step * 1e-3) / 1e9
@@ -570,7 +595,10 @@ def run_ours(args) -> None:
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": profiled_traffic(),
                      "kernel": "decode_tma_kernel (split-K paged decode)",
-                     "bytes_per_launch": int(dec_bytes), "peak_kind": f"{peak_kind} hbm_gbs"},
+                     "bytes_per_launch": int(dec_bytes), "peak_kind": f"{peak_kind} hbm_gbs",
+                     "timing": f"CUDA events around {KERNEL_ITERS} back-to-back decode launches "
+                               f"on the launching stream, after the timed region",
+                     "kernel_share_of_step": round(decode_ms / ms_step, 4)},
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": 3 * args.steps,
@@ -677,38 +705,39 @@ def run_extra(args) -> None:
     sharded = (pdist.ShardedPagedAttention(H, KVH, HEAD_DIM, transport="peer")
                if peer else None)
 
-    def step(ev=None):
-        if ev is not None:
-            ev[0].record()
+    def append():
         if wl["kind"] == "prefill":
             cache.write(0, table, offs, knew, vnew)
         else:
             cache.write_decode(0, table, offs, knew, vnew)
-        if ev is not None:
-            ev[1].record()
+
+    def attention():
         if peer:
             sharded.forward(q, cache, 0, table, ctx, q_len)
         else:
             attn.forward_with_lse(q, cache, 0, table, ctx, q_len, want_lse=False, out=out_view)
-        if ev is not None:
-            ev[2].record()
+
+    def step():
+        append()
+        attention()
         if gathered is not None:
             dist.all_gather_into_tensor(gathered, head_major)
 
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
     for _ in range(max(args.warmup, 3)):
         step()
-    every = 10   # per-kernel events on every 10th step only (they break launch overlap)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)]
-           for _ in range((args.steps + every - 1) // every)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
+    barrier()
     sampler = ClockSampler(local)
     sampler.start()
     start.record()
-    for i in range(args.steps):
-        step(evs[i // every] if i % every == 0 else None)
+    for _ in range(args.steps):
+        step()
     end.record()
     torch.cuda.synchronize(dev)
     clocks = sampler.stop()
@@ -718,8 +747,9 @@ def run_extra(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_step = ms / args.steps
-    append_ms = statistics.fmean(e[0].elapsed_time(e[1]) for e in evs)
-    attn_ms = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
+    iters = max(20, min(KERNEL_ITERS, int(2000 / max(ms_step, 1e-3))))
+    append_ms = kernel_loop_ms(append, dev, barrier, iters)
+    attn_ms = kernel_loop_ms(attention, dev, barrier, iters)
     if rank == 0:
         line = {"config": args.config, "workload": wl["note"], "n_gpus": world,
                 "exchange": (("combine fused with the all-gather (NVLink peer stores)" if peer
@@ -1074,48 +1104,50 @@ def run_fp8(args) -> None:
             for s in (cache.key_scale, cache.value_scale):
                 s.copy_(torch.rand(s.shape, generator=g, device=dev) * (1.0 / 448) + 1e-4)
 
-        def step(ev=None):
-            if ev is not None:
-                ev[0].record()
+        def append():
             cache.write_decode(0, table, offs, knew, vnew)
-            if ev is not None:
-                ev[1].record()
+
+        def decode():
             attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out,
                                   phases=_lib.PHASE_SPLIT)
-            if ev is not None:
-                ev[2].record()
+
+        def combine():
             attn.forward_with_lse(q, cache, 0, table, ctx, 1, want_lse=False, out=out,
                                   phases=_lib.PHASE_COMBINE)
-            if ev is not None:
-                ev[3].record()
+
+        def step():
+            append()
+            decode()
+            combine()
+
+        def barrier():
+            torch.cuda.synchronize(dev)
 
         for _ in range(max(args.warmup, 3)):
             step()
-        every = 10
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)]
-               for _ in range((args.steps + every - 1) // every)]
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
         sampler = ClockSampler(0)
         sampler.start()
         start.record()
-        for i in range(args.steps):
-            step(evs[i // every] if i % every == 0 else None)
+        for _ in range(args.steps):
+            step()
         end.record()
         torch.cuda.synchronize(dev)
         clocks = sampler.stop()
+        append_ms = kernel_loop_ms(append, dev, barrier)
+        decode_ms = kernel_loop_ms(decode, dev, barrier)
+        combine_ms = kernel_loop_ms(combine, dev, barrier)
         ms_step = start.elapsed_time(end) / args.steps
         kv_bytes = 1 if cache.is_fp8 else 2
         dec = decode_bytes(ctx_np, KV_HEADS, HEAD_DIM, kv_bytes, B, HEADS, 2, 2, BLOCK)
         if cache.is_fp8:
             dec += int(ctx_np.sum()) * KV_HEADS * 2 * 4        # K and V row scales
-        decode_ms = statistics.fmean(e[1].elapsed_time(e[2]) for e in evs)
         lines[name] = dict(
             ms_per_step=round(ms_step, 5), decode_tok_s=round(B / (ms_step * 1e-3), 1),
             bytes_per_step=int(dec), step_GBps=round(dec / (ms_step * 1e-3) / 1e9, 1),
-            kernel_ms={"append": round(statistics.fmean(e[0].elapsed_time(e[1]) for e in evs), 5),
-                       "decode_split": round(decode_ms, 5),
-                       "combine": round(statistics.fmean(e[2].elapsed_time(e[3]) for e in evs), 5)},
+            kernel_ms={"append": round(append_ms, 5), "decode_split": round(decode_ms, 5),
+                       "combine": round(combine_ms, 5)},
             decode_kernel_GBps=round(dec / (decode_ms * 1e-3) / 1e9, 1), clocks=clocks)
         del cache
         torch.cuda.empty_cache()

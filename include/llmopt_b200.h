@@ -175,8 +175,11 @@ LLMOPT_API int llmopt_paged_attention_phase(const void* query, int32_t q_dtype, 
  *
  * The split-K scratch is a fixed array of LLMOPT_NOALLOC_SCRATCH_BYTES compiled
  * into the library, held in device memory by every GPU that loads it until the
- * process exits.  The first call on a device looks up the array's address on
- * that device (make that first call before any stream capture).  All calls on
+ * process exits.  The first call in each CUDA context looks up the array's
+ * address there, with the device current, and keeps it by the context's unique
+ * id, so a context that replaces another (after cudaDeviceReset, or a caller's
+ * own non-primary context) gets its own lookup; make the first call on each
+ * device before any stream capture.  All calls on
  * a device share the array and it keeps the last call's contents, so calls
  * that may overlap on the GPU (other streams, other threads) race and must be
  * serialised by the caller.  A shape needing more scratch than the array holds
@@ -443,8 +446,10 @@ LLMOPT_API int llmopt_paged_gather_scaled(const void* key_cache, const void* val
  * weight by weight: the MMAs sum the exact products (q - z) * x of each group
  * in fp32 and the group's scale multiplies that sum, which is at least as
  * accurate as the reference's weights rounded to the compute dtype; 8-bit
- * weights are the reference's bit for bit.  Zero points are integers in
- * [0, 2^bits), as the reference's quantizers round them.  The workspace (fp32
+ * weights are the reference's bit for bit.  Zero points must be whole numbers,
+ * as the reference's quantizers round them: the kernels subtract them exactly
+ * only then (a fractional zero point is rounded to an integer; the Python layer
+ * refuses one with ValueError).  The workspace (fp32
  * split-k partials) is sized by llmopt_quant_linear_workspace_size for the
  * same m, n, k.
  */

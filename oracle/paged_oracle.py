@@ -515,11 +515,22 @@ def merge_states(output, partial, prefix_lse, suffix_lse):
         return output * s1 + partial * s2, merged_lse
 
 
-def _expand_kv(k: np.ndarray, group: int) -> np.ndarray:
-    """``_expand_kv`` (paged_attention.py:189-210): query head h reads KV head h // group."""
-    if group == 1:
-        return k
-    return np.repeat(k, group, axis=1)
+def _grouped(x: np.ndarray, kv_heads: int) -> np.ndarray:
+    """``[B, H, rows, n]`` -> ``[B, KVH, group * rows, n]`` (a view).
+
+    ``_expand_kv`` (paged_attention.py:189-210) gives query head h the KV head
+    h // group by repeating each KV head ``group`` times.  The same mapping,
+    without the copies: the ``group`` query heads of KV head j are heads
+    j * group ... j * group + group - 1, so grouping the query heads by KV head
+    lines every query row up with its KV head.
+    """
+    B, H, rows, n = x.shape
+    return x.reshape(B, kv_heads, (H // kv_heads) * rows, n)
+
+
+def _ungrouped(x: np.ndarray, heads: int) -> np.ndarray:
+    B, kvh, grows, n = x.shape
+    return x.reshape(B, heads, grows * kvh // heads, n)
 
 
 def _build_mask(valid: np.ndarray, context_lens: np.ndarray, q_len: int) -> np.ndarray:
@@ -534,7 +545,10 @@ def _build_mask(valid: np.ndarray, context_lens: np.ndarray, q_len: int) -> np.n
 
 
 def _scores(q, k, scale, softcap):
-    s = np.matmul(q, np.swapaxes(k, -1, -2)) * scale
+    """Scaled (and soft-capped) ``q kᵀ`` per query head, query head h reading KV head
+    h // group (``_expand_kv``, paged_attention.py:189-210, :242)."""
+    s = _ungrouped(np.matmul(_grouped(q, k.shape[1]), np.swapaxes(k, -1, -2)), q.shape[1])
+    s = s * scale
     if softcap > 0:                               # paged_attention.py:243-244
         s = np.tanh(s / softcap) * softcap
     return s
@@ -556,19 +570,22 @@ def _logsumexp(scores):
     return out
 
 
+def _pv(p, v):
+    """``p @ v`` per query head over its KV head's values (h // group)."""
+    return _ungrouped(np.matmul(_grouped(p, v.shape[1]), v), p.shape[1])
+
+
 def _forward_dense(q, k, v, valid, ctx, q_len, scale, softcap, group):
     """``_forward_dense`` (paged_attention.py:231-250); also returns the row LSE."""
-    k, v = _expand_kv(k, group), _expand_kv(v, group)
     scores = _scores(q, k, scale, softcap)
     mask = _build_mask(valid, ctx, q_len)
     scores = np.where(mask, scores, -np.inf)
-    out = np.matmul(_softmax_rows(scores), v)
+    out = _pv(_softmax_rows(scores), v)
     return out, _logsumexp(scores)
 
 
 def _forward_split(q, k, v, valid, ctx, q_len, scale, softcap, group, chunk):
     """``_forward_split`` (paged_attention.py:252-293): chunks merged by LSE."""
-    k, v = _expand_kv(k, group), _expand_kv(v, group)
     total = k.shape[2]
     outs, lses = [], []
     for start in range(0, total, chunk):          # paged_attention.py:269
@@ -577,7 +594,7 @@ def _forward_split(q, k, v, valid, ctx, q_len, scale, softcap, group, chunk):
         mask = _build_mask(valid[:, start:end], ctx - start, q_len)  # :277-279
         scores = np.where(mask, scores, -np.inf)
         lses.append(_logsumexp(scores))           # :281
-        outs.append(np.matmul(_softmax_rows(scores), v[:, :, start:end]))
+        outs.append(_pv(_softmax_rows(scores), v[:, :, start:end]))
     acc, acc_lse = outs[0], lses[0]
     for part, part_lse in zip(outs[1:], lses[1:]):  # :287-290
         acc, acc_lse = merge_states(acc, part, acc_lse, part_lse)

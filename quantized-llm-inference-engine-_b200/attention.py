@@ -259,6 +259,49 @@ class PagedAttention:
 
     __call__ = forward
 
+    def _forward_dense(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                       valid: torch.Tensor, context_lens: torch.Tensor,
+                       q_len: int) -> torch.Tensor:
+        """Attention over dense K/V with no cache (paged_attention.py:231-250).
+
+        ``PagedAttentionLayer._dense_attention`` (layers.py:144-163) calls this
+        for the model's stateless forward (``cache=None``), the path the
+        reference's engine tests compare against.  ``k`` / ``v`` are
+        ``[seq, kv_heads, ctx, head_dim]``; they are copied once into a
+        temporary block pool in ``k``'s dtype, addressed by an identity block
+        table, and the paged kernels run over it, so query row ``i`` of sequence
+        ``s`` attends to key positions ``<= context_lens[s] - q_len + i`` (the
+        causal rule of ``_build_mask``, :212-229).  ``valid`` must hold every
+        position below ``context_lens`` (the layer passes it all true): the
+        kernels mask positions from ``context_lens`` on, and a hole inside the
+        context raises ``ValueError``.
+        """
+        if k.dim() != 4 or v.shape != k.shape:
+            raise ValueError("k and v must be [seq, kv_heads, ctx, head_dim] and alike")
+        seq, kvh, ctx, d = k.shape
+        rt.require_cuda(k, "k")
+        device = k.device
+        lens = context_lens.to(device=device, dtype=torch.int64).reshape(-1)
+        if lens.numel() < seq:
+            raise ValueError("context_lens must have one entry per sequence")
+        pos = torch.arange(ctx, device=device)
+        inside = pos[None, :] < lens[:seq, None]
+        if not bool((valid.to(device)[:seq, :ctx] | ~inside).all()):
+            raise ValueError("valid must hold every position below context_lens")
+        bs = 16
+        nb = max(1, -(-ctx // bs))
+        dtype = k.dtype if k.dtype in rt.KV_DTYPE_CODE else torch.float32
+        pools = []
+        for t in (k, v):
+            pool = torch.zeros((1, seq * nb, bs, kvh, d), dtype=dtype, device=device)
+            pool.view(seq, nb * bs, kvh, d)[:, :ctx] = t.permute(0, 2, 1, 3)
+            pools.append(pool)
+        from .cache import PagedKVCache
+
+        cache = PagedKVCache.from_storage(*pools)
+        table = torch.arange(seq * nb, dtype=torch.int32, device=device).view(seq, nb)
+        return self.forward(q, cache, 0, table, lens[:seq], q_len)
+
     def __repr__(self) -> str:
         return (f"PagedAttention(heads={self.num_heads}, kv_heads={self.num_kv_heads}, "
                 f"head_dim={self.head_dim}, backend={self.backend}, "

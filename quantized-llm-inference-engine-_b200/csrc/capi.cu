@@ -1347,9 +1347,11 @@ extern "C" int llmopt_decode_step_advance(const int64_t* updates, int64_t capaci
 // The scratch lives in device global memory: LLMOPT_NOALLOC_SCRATCH_BYTES per
 // GPU, held by every GPU that loads this code until the process exits.  Host
 // code must not use the array's name as a device address (in host code it is
-// only a stand-in); the address is looked up once per device with
-// cudaGetSymbolAddress, with that device current, by the first call on that
-// device - so make the first call on each device before any stream capture.
+// only a stand-in); the address is looked up with cudaGetSymbolAddress, with
+// the device current, by the first call in each CUDA context (a device's
+// primary context, a context that replaced it after cudaDeviceReset, or a
+// caller's own context) - so make the first call on each device before any
+// stream capture.
 // Every call on a device shares the one array and it keeps whatever the last
 // call left there: calls that can overlap on the GPU (different streams, or
 // several host threads) race on it and must be serialised by the caller.
@@ -1360,27 +1362,71 @@ extern "C" int llmopt_decode_step_advance(const int64_t* updates, int64_t capaci
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr int kNoAllocMaxDevices = 64;
+constexpr int kNoAllocMaxContexts = 64;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[LLMOPT_NOALLOC_SCRATCH_BYTES];
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+// (context id, device address of g_noalloc_scratch in that context)
+unsigned long long g_noalloc_ctx[kNoAllocMaxContexts] = {};
+void* g_noalloc_addr[kNoAllocMaxContexts] = {};
+int g_noalloc_used = 0;
 
-// Device address of g_noalloc_scratch on the current device (looked up once).
-int noalloc_scratch(int device, void** addr) {
-  if (device < 0 || device >= kNoAllocMaxDevices) {
-    return fail(LLMOPT_ERR_INVALID_ARGUMENT, "device ordinal %d not supported", device);
-  }
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[device] == nullptr) {
+// The unique id (cuCtxGetId) of the calling thread's current CUDA context, or
+// 0 when no context is current or the driver does not expose the call.  Unlike
+// a device ordinal, an id is never reused: a context that replaced another
+// (after cudaDeviceReset, or a caller's own non-primary context) gets its own.
+unsigned long long current_context_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static bool resolved = false;
+  if (!resolved) {
     void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      return cuda_fail(e == cudaSuccess ? cudaErrorInvalidSymbol : e,
-                       "cudaGetSymbolAddress(scratch)");
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
     }
-    g_noalloc_addr[device] = p;
+    p = nullptr;
+    q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+    }
+    resolved = true;
   }
-  *addr = g_noalloc_addr[device];
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_noalloc_scratch in the current context.  Looked up with
+// cudaGetSymbolAddress (which allocates nothing) on the first call in each
+// context and remembered by context id; without an id it is looked up on every
+// call.
+int noalloc_scratch(void** addr) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  unsigned long long id = current_context_id();
+  for (int i = 0; id != 0 && i < g_noalloc_used; ++i) {
+    if (g_noalloc_ctx[i] == id) {
+      *addr = g_noalloc_addr[i];
+      return LLMOPT_OK;
+    }
+  }
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    return cuda_fail(e == cudaSuccess ? cudaErrorInvalidSymbol : e,
+                     "cudaGetSymbolAddress(scratch)");
+  }
+  if (id == 0) id = current_context_id();  // the lookup made the primary context current
+  if (id != 0 && g_noalloc_used < kNoAllocMaxContexts) {
+    g_noalloc_ctx[g_noalloc_used] = id;
+    g_noalloc_addr[g_noalloc_used] = p;
+    ++g_noalloc_used;
+  }
+  *addr = p;
   return LLMOPT_OK;
 }
 
@@ -1435,9 +1481,16 @@ extern "C" int llmopt_paged_attention_noalloc(
   a.q_len = q_len;
   a.group = num_heads / num_kv_heads;
   a.rows = q_len * a.group;
+  a.table = block_table;
+  a.table_i64 = table_is_i64;
+  a.table_stride = table_stride;
+  a.ctx = context_lens;
+  a.ctx_i64 = ctx_is_i64;
   const int device = current_device();
+  // The same plan the regular entry picks, tensor maps included (a shape whose
+  // maps cannot be encoded falls back to a plan that may need more scratch).
   Choice c;
-  int st = choose(a, split_tokens, device, false, &c);
+  int st = choose(a, split_tokens, device, true, &c);
   if (st != LLMOPT_OK) return st;
   const long long need = layout_for(batch, c.plan.slots, num_heads, q_len, head_dim).total;
   if (need > (long long)LLMOPT_NOALLOC_SCRATCH_BYTES) {
@@ -1448,7 +1501,7 @@ extern "C" int llmopt_paged_attention_noalloc(
                 need, (long long)LLMOPT_NOALLOC_SCRATCH_BYTES);
   }
   void* scratch = nullptr;
-  st = noalloc_scratch(device, &scratch);
+  st = noalloc_scratch(&scratch);
   if (st != LLMOPT_OK) return st;
   return llmopt_paged_attention(query, q_dtype, q_s, q_h, q_t, key_cache, value_cache, kv_dtype,
                                 num_layers, num_blocks, block_size, num_kv_heads, head_dim,

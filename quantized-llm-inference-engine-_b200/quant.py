@@ -91,6 +91,8 @@ class QuantLinear(nn.Module):
             raise ValueError(f"scales must be [{self.out_features}, {groups}]")
         if not cfg.symmetric and zeros.shape != scales.shape:
             raise ValueError("asymmetric quantization needs zeros shaped like scales")
+        if not cfg.symmetric:
+            _check_integral_zeros(zeros)
         return qweight, scales, zeros, group
 
     def dequantized_weight(self, device=None) -> torch.Tensor:
@@ -105,7 +107,8 @@ class QuantLinear(nn.Module):
         out = torch.empty((self.out_features, self.in_features), dtype=dtype, device=device)
         st = _lib.lib().llmopt_dequantize(
             qweight.data_ptr(), self.config.bits, group, int(self.config.symmetric),
-            scales.data_ptr(), zeros.data_ptr() if zeros.numel() else None, self.out_features,
+            scales.data_ptr(), zeros.data_ptr() if zeros.numel() and not self.config.symmetric
+            else None, self.out_features,
             self.in_features, out.data_ptr(), rt.dtype_code(dtype, "compute_dtype"),
             rt.stream_handle(device))
         _lib.check(st, "QuantLinear.dequantized_weight")
@@ -126,6 +129,26 @@ class QuantLinear(nn.Module):
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
                 f"bits={self.config.bits}, bias={self.bias is not None}")
+
+
+_INTEGRAL_ZEROS: dict = {}
+
+
+def _check_integral_zeros(zeros: torch.Tensor) -> None:
+    """Zero points must be whole numbers, as the reference's quantizers write them
+    (``round(-wmin / scale)``, quantizers.py).  The kernels subtract them exactly
+    only then, so a fractional zero point raises ``ValueError`` instead of being
+    rounded silently.  The check reads the tensor once per (storage, version):
+    later calls with the same unmodified tensor cost nothing."""
+    key = (zeros.device, zeros.data_ptr(), zeros.numel(), zeros._version)
+    if key in _INTEGRAL_ZEROS:
+        return
+    if not bool(torch.equal(zeros, zeros.round())):
+        raise ValueError("QuantLinear zero points must be whole numbers (round(-wmin / scale), "
+                         "as the reference's quantizers write them)")
+    if len(_INTEGRAL_ZEROS) > 4096:
+        _INTEGRAL_ZEROS.clear()
+    _INTEGRAL_ZEROS[key] = True
 
 
 def _check_qweight(qweight: torch.Tensor, n: int, k: int, bits: int) -> None:
@@ -163,8 +186,9 @@ def quant_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
     _check_qweight(qweight, n, k, bits)
     if scales.dtype != torch.float32 or not scales.is_contiguous():
         scales = scales.to(torch.float32).contiguous()
-    if zeros is not None and zeros.numel():
+    if zeros is not None and zeros.numel() and not symmetric:
         zeros = zeros.to(device=device, dtype=torch.float32).contiguous()
+        _check_integral_zeros(zeros)
     else:
         zeros = None
     qweight = qweight.contiguous()

@@ -2,7 +2,7 @@
 
 Run once, in a container where the reference source is present::
 
-    python tests/golden/make_golden.py /path/to/reference/src [--only=attn|rope|step|quant]
+    python tests/golden/make_golden.py /path/to/reference/src [--only=attn|rope|step|quant|engine|c5]
 
 It imports ``llmopt.attention`` / ``llmopt.cache`` from that path, runs them
 on CPU on the seeded inputs of ``cases.py`` (plus the reference's own
@@ -330,6 +330,213 @@ def make_merge(merge_states) -> dict:
             "out": o.numpy(), "lse": lse.numpy()}
 
 
+# The reference's randomized scenario with seed 2 never finishes in the
+# reference's own engine (its scheduler loops), so it is not recorded.
+ENGINE_CASES = ("single", "long", "boundary", "chunked", "prefix_hit", "prefix_chunked",
+                "ragged", "random0", "random1", "random3", "random4", "random5", "random6",
+                "random7")
+
+
+def _engine_runs(name, build_engine, greedy_reference, Request, SamplingParams):
+    """The reference's own engine-correctness scenarios (tests/test_engine_correctness.py
+    and tests/test_cache_and_blocks.py), as (engine, [(prompt, max_tokens)], batched)."""
+    import random
+
+    if name == "single":                                  # test_engine_correctness.py:13-16
+        return build_engine(), [(list(range(1, 11)), 6)], False
+    if name == "long":                                    # :19-24
+        return (build_engine(vocab_size=320, num_gpu_blocks=64, block_size=8),
+                [(list(range(1, 300)), 8)], False)
+    if name == "boundary":                                # :27-32
+        return (build_engine(block_size=16),
+                [([(i * 7) % 200 + 1 for i in range(n)], 4) for n in (15, 16, 17, 32, 33)],
+                False)
+    if name == "chunked":                                 # :35-41
+        eng = build_engine()
+        eng.config.scheduler.prefill_chunk_size = 7
+        eng.config.scheduler.enable_chunked_prefill = True
+        return eng, [(list(range(1, 200)), 8)], False
+    if name == "prefix_hit":                              # test_cache_and_blocks.py:82-90
+        p = [(i * 13) % 200 + 1 for i in range(150)]
+        return build_engine(), [(p, 6), (p, 6)], False
+    if name == "prefix_chunked":                          # test_cache_and_blocks.py:93-98
+        eng = build_engine()
+        eng.config.scheduler.prefill_chunk_size = 5
+        return eng, [([(i * 7) % 200 + 1 for i in range(150)], 6)], False
+    if name == "ragged":                                  # test_engine_correctness.py:68-88
+        rng = random.Random(3)
+        reqs = [([rng.randrange(1, 255) for _ in range(rng.randint(5, 300))],
+                 rng.randint(1, 10)) for _ in range(40)]
+        return build_engine(), reqs, True
+    seed = int(name[len("random"):])                      # test_engine_correctness.py:48-65
+    rng = random.Random(seed)
+    eng = build_engine(num_gpu_blocks=rng.choice([16, 48, 256]),
+                       block_size=rng.choice([8, 16, 32]),
+                       max_num_seqs=rng.choice([1, 2, 8]),
+                       enable_prefix_caching=bool(rng.getrandbits(1)))
+    if rng.getrandbits(1):
+        eng.config.scheduler.prefill_chunk_size = rng.choice([3, 9, 64])
+    prompt = [rng.randrange(1, 255) for _ in range(rng.randint(1, 200))]
+    return eng, [(prompt, rng.randint(1, 8))], False
+
+
+def make_engine_traces(ref_src: str) -> dict:
+    """Run the reference engine on CPU and record every call it makes into the hot path.
+
+    For each scenario the model's forward is wrapped so that every call with a
+    cache records what ``ModelRunner.execute`` hands the model (model_runner.py:92-113):
+    input ids, positions, the int32 block table ``_finalize`` built from the
+    ``BlockPool`` / ``PrefixCache`` chains, post-write context lengths, write
+    offsets and ``q_len``, plus the last-position logits the sampler reads.  The
+    reference's greedy tokens and those of its stateless ``greedy_reference``
+    (tests/_helpers.py:29-46) are recorded per request, with the model weights
+    (one set per vocabulary size).
+    """
+    import json
+
+    import torch
+
+    sys.path.insert(0, os.path.join(os.path.dirname(ref_src.rstrip("/")), "tests"))
+    from _helpers import build_engine, greedy_reference
+    from llmopt.engine import Request, SamplingParams
+
+    out: dict = {}
+    weights_seen: dict = {}
+    names = os.environ.get("ENGINE_CASES", ",".join(ENGINE_CASES)).split(",")
+    for name in names:
+        eng, reqs, batched = _engine_runs(name, build_engine, greedy_reference, Request,
+                                          SamplingParams)
+        model = eng.model
+        cfg = model.config
+        vocab = int(cfg.vocab_size)
+        wkey = f"w{vocab}"
+        sd = {k: v.detach().float().numpy().copy() for k, v in model.state_dict().items()}
+        if wkey in weights_seen:
+            for k, v in sd.items():
+                assert np.array_equal(weights_seen[wkey][k], v), "weights differ for one vocab"
+        else:
+            weights_seen[wkey] = sd
+            for k, v in sd.items():
+                out[f"{wkey}.{k}"] = v
+        calls, ids, pos, tables, ctxs, offs, logits = [], [], [], [], [], [], []
+        orig_forward = model.forward
+
+        def recording(input_ids, positions, cache=None, block_ids=None, context_lens=None,
+                      token_offsets=None, q_len=1, _orig=orig_forward):
+            res = _orig(input_ids, positions, cache=cache, block_ids=block_ids,
+                        context_lens=context_lens, token_offsets=token_offsets, q_len=q_len)
+            if cache is not None:
+                t = block_ids.to(torch.int32).cpu().numpy()
+                calls.append([t.shape[0], int(q_len), t.shape[1]])
+                ids.append(input_ids.reshape(-1).cpu().numpy().astype(np.int64))
+                pos.append(positions.reshape(-1).cpu().numpy().astype(np.int64))
+                tables.append(t.reshape(-1))
+                ctxs.append(context_lens.cpu().numpy().astype(np.int64))
+                offs.append(token_offsets.cpu().numpy().astype(np.int64))
+                logits.append(res.logits[:, -1, :].detach().float().cpu().numpy())
+            return res
+
+        model.forward = recording
+        requests = []
+        if batched:
+            objs = [Request(request_id=f"r{i}", prompt_token_ids=p,
+                            sampling_params=SamplingParams(max_tokens=m, temperature=0.0,
+                                                           ignore_eos=True),
+                            max_model_len=512, arrival_time=0.0)
+                    for i, (p, m) in enumerate(reqs)]
+            results = {o.request_id: list(o.token_ids) for o in eng.run(objs)}
+            got = [results[f"r{i}"] for i in range(len(reqs))]
+        else:
+            got = [list(eng.generate_sync(p, SamplingParams(max_tokens=m, temperature=0.0))
+                        .token_ids) for p, m in reqs]
+        model.forward = orig_forward
+        for (p, m), toks in zip(reqs, got):
+            ref = greedy_reference(model, p, m)
+            requests.append({"prompt": p, "max_tokens": m, "engine_tokens": toks,
+                             "stateless_tokens": ref})
+        cache = eng.cache
+        meta = {"vocab": vocab, "weights": wkey, "hidden": int(cfg.hidden_size),
+                "layers": int(cfg.num_hidden_layers), "heads": int(cfg.num_attention_heads),
+                "kv_heads": int(cfg.num_key_value_heads), "head_dim": int(cfg.head_dim),
+                "rope_theta": float(cfg.rope_theta), "rms_norm_eps": float(cfg.rms_norm_eps),
+                "max_position_embeddings": int(cfg.max_position_embeddings),
+                "num_blocks": int(cache.num_blocks), "block_size": int(cache.block_size),
+                "cache_dtype": str(cache.dtype).replace("torch.", ""),
+                "model_dtype": "float32", "batched": batched, "requests": requests,
+                "prefix_hits": int(getattr(eng.scheduler.stats, "num_prefix_hits", 0))}
+        out[f"{name}.meta"] = np.array(json.dumps(meta))
+        out[f"{name}.calls"] = np.asarray(calls, dtype=np.int64).reshape(-1, 3)
+        out[f"{name}.input_ids"] = np.concatenate(ids)
+        out[f"{name}.positions"] = np.concatenate(pos)
+        out[f"{name}.tables"] = np.concatenate(tables)
+        out[f"{name}.context_lens"] = np.concatenate(ctxs)
+        out[f"{name}.token_offsets"] = np.concatenate(offs)
+        out[f"{name}.logits"] = np.concatenate(logits).astype(np.float32)
+        n_ok = sum(r["engine_tokens"] == r["stateless_tokens"] for r in requests)
+        print(f"engine {name}: {len(calls)} calls, {n_ok}/{len(requests)} requests equal "
+              f"the stateless forward", flush=True)
+    return out
+
+
+C5_SEQS, C5_PREFIX_BLOCKS, C5_BLOCK = 256, 128, 16
+
+
+def make_c5(BlockPool, PrefixCache) -> dict:
+    """BASELINE config 5's block tables, produced by the reference's own block bookkeeping.
+
+    Every sequence's prompt is a shared 2048-token prefix plus a private suffix of
+    U[64, 1024] tokens (the last suffix token is the decode token).  The calls are
+    those the reference scheduler makes (scheduler.py:356-400): ``PrefixCache.find``
+    on admission, ``BlockPool.share_blocks`` for a hit, ``append`` for the rest of
+    the prompt, then ``insert`` + ``mark_shared`` of the newly full blocks
+    (``cache_prefix``); then one decode append per sequence.  The table is built
+    as ``ModelRunner._finalize`` builds it (model_runner.py:203-230): int32, −1
+    padded to the longest chain.
+    """
+    rng = np.random.default_rng(5)
+    suffix = rng.integers(64, 1025, size=C5_SEQS)
+    prefix_tokens = [int(t) for t in rng.integers(1, 30000, size=C5_PREFIX_BLOCKS * C5_BLOCK)]
+    need = C5_PREFIX_BLOCKS + int(sum(-(-int(s) // C5_BLOCK) for s in suffix))
+    num_blocks = int(need * 1.10) + 1
+    pool = BlockPool(num_blocks=num_blocks, block_size=C5_BLOCK)
+    pcache = PrefixCache(pool, C5_BLOCK, max_entries=num_blocks * 2)
+    published = {}
+    hits = 0
+    for s in range(C5_SEQS):
+        prompt = prefix_tokens + [int(t) for t in rng.integers(30000, 60000,
+                                                               size=int(suffix[s]) - 1)]
+        cached = pcache.find(prompt)
+        done = 0
+        if cached is not None and cached.block_ids:
+            pool.share_blocks(s, cached.block_ids, cached.num_tokens)
+            published[s] = len(cached.block_ids)
+            done = cached.num_tokens
+            hits += 1
+        pool.append(s, len(prompt) - done)
+        num_full = pool.tokens_used(s) // C5_BLOCK
+        chain = pool.chains[s]
+        if num_full > published.get(s, 0):
+            pcache.insert(prompt[:num_full * C5_BLOCK], chain[:num_full])
+            pool.mark_shared(chain[published.get(s, 0):num_full])
+            published[s] = num_full
+    for s in range(C5_SEQS):                       # the decode step's token
+        pool.append(s, 1)
+    ctx = np.array([pool.tokens_used(s) for s in range(C5_SEQS)], dtype=np.int64)
+    width = max(len(c) for c in pool.chains.values())
+    table = np.full((C5_SEQS, width), -1, dtype=np.int32)
+    for s in range(C5_SEQS):
+        table[s, :len(pool.chains[s])] = pool.chains[s]
+    shared = np.asarray(pool.chains[0][:C5_PREFIX_BLOCKS], dtype=np.int32)
+    refc = np.array([pool.ref_counts[int(b)] for b in shared], dtype=np.int64)
+    assert (table[:, :C5_PREFIX_BLOCKS] == shared).all(), "prefix blocks not shared"
+    print(f"c5: {C5_SEQS} seqs, pool {num_blocks} blocks, width {width}, prefix hits {hits}, "
+          f"prefix refcount {int(refc.min())}..{int(refc.max())}")
+    return {"block_ids": table, "context_lens": ctx, "token_offsets": ctx - 1,
+            "num_blocks": np.array(num_blocks), "shared_blocks": shared,
+            "shared_refcounts": refc, "suffix": suffix.astype(np.int64),
+            "prefix_hits": np.array(hits)}
+
+
 def main(ref_src: str, only: str | None = None) -> None:
     sys.path.insert(0, ref_src)
     import torch
@@ -339,6 +546,20 @@ def main(ref_src: str, only: str | None = None) -> None:
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     meta = {"torch": torch.__version__, "numpy": np.__version__}
+    if only == "engine":
+        out = make_engine_traces(ref_src)
+        out["versions"] = np.array(str(meta))
+        np.savez_compressed(os.path.join(HERE, "engine_trace.npz"), **out)
+        print("wrote engine_trace")
+        return
+    if only == "c5":
+        from llmopt.cache import PrefixCache
+
+        out = make_c5(BlockPool, PrefixCache)
+        out["versions"] = np.array(str(meta))
+        np.savez_compressed(os.path.join(HERE, "c5_tables.npz"), **out)
+        print("wrote c5_tables")
+        return
     if only == "step":
         from llmopt.engine.model_runner import ModelRunner
 

@@ -51,6 +51,19 @@ def check_case(cuda, case, softcap=0.0, modes=("auto", "fixed", "none"), split_s
     assert device_errors(cuda) == 0
 
 
+def check_all_sequences(case, cache, results, chunk=4):
+    """Every sequence against the oracle, ``chunk`` sequences at a time (the
+    oracle's padded, group-expanded copies of a whole full-size batch would not
+    fit in host memory).  ``results`` maps a label to one run's ``(out, lse)``."""
+    B = len(case["context_lens"])
+    for lo in range(0, B, chunk):
+        rows = list(range(lo, min(B, lo + chunk)))
+        want, want_lse = oracle(subset_case(case, cache, rows))
+        for what, (out, lse) in results.items():
+            assert_lowp_close(out[rows], want, f"{what} rows {rows}")
+            assert_lse_close(lse[rows], want_lse, f"{what} rows {rows} lse")
+
+
 EDGE_CTX = [1, 15, 16, 17, 31, 33, 100, 600]
 
 
@@ -181,7 +194,7 @@ def config2(cuda):
     return device_case(2, cuda, ctx=ctx, heads=32, kv_heads=8, head_dim=128, value_scale=0.5)
 
 
-def test_config2_split_modes_agree_and_match_oracle(cuda, config2):
+def test_config2_split_modes_agree_and_every_sequence_matches_oracle(cuda, config2):
     case, cache = config2
     outs = {}
     for mode in ("auto", "fixed", "none"):
@@ -190,10 +203,7 @@ def test_config2_split_modes_agree_and_match_oracle(cuda, config2):
     for mode in ("fixed", "none"):
         assert_lowp_close(outs[mode][0], outs["auto"][0], f"{mode} vs auto")
         assert_lse_close(outs[mode][1], outs["auto"][1], f"{mode} vs auto lse")
-    pick = [0, 17, 63]
-    want, want_lse = oracle(subset_case(case, cache, pick))
-    assert_lowp_close(outs["auto"][0][pick], want, "oracle subset")
-    assert_lse_close(outs["auto"][1][pick], want_lse, "oracle subset lse")
+    check_all_sequences(case, cache, {f"config 2 {m}": outs[m] for m in outs})
     assert device_errors(cuda) == 0
 
 
@@ -254,6 +264,59 @@ def test_shared_prefix_blocks_give_identical_outputs(cuda):
         want, want_lse = oracle(case)
         assert_lowp_close(out, want, f"shared prefix {mode}")
         assert_lse_close(lse, want_lse, f"shared prefix lse {mode}")
+
+
+def test_config5_reference_block_sharing(cuda):
+    """BASELINE config 5 at its shape: 256 sequences, 32 query / 8 KV heads,
+    head_dim 128, a 2048-token prefix on 128 shared blocks plus private
+    suffixes U[64, 1024].  The int32 tables, context lengths and refcounts come
+    from the reference's own ``BlockPool`` / ``PrefixCache`` calls
+    (``tests/golden/c5_tables.npz``, ``make_golden.py --only=c5``).
+
+    Every sequence is checked against the oracle in every split mode.  With the
+    context cut to the shared prefix and one query for all, the 256 sequences
+    read the same bytes through the same block ids, so their outputs must be
+    bit-identical wherever the split plan is the same for every sequence
+    (``none`` and ``fixed``) and equal within the bar under the balanced plan."""
+    import os
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "c5_tables.npz"))
+    table, ctx = z["block_ids"], z["context_lens"]
+    nb, shared = int(z["num_blocks"]), z["shared_blocks"]
+    assert table.dtype == np.int32 and table.shape[0] == 256
+    assert (table[:, :128] == shared).all() and (z["shared_refcounts"] == 257).all()
+    pkg = load_package()
+    cache = pkg.PagedKVCache(1, nb, 16, 8, 128, dtype=torch.bfloat16, device=cuda)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(55)
+    for t in (cache.key_cache, cache.value_cache):
+        t.copy_(torch.randn(t.shape, generator=g, device=cuda))
+    rng = np.random.default_rng(56)
+    q = po.from_f32(rng.standard_normal((256, 32, 1, 128), dtype=np.float32), "bf16")
+    case = dict(key_cache=None, value_cache=None, block_ids=table, context_lens=ctx, query=q,
+                kv_kind="bf16", q_kind="bf16", heads=32, kv_heads=8, head_dim=128,
+                block_size=16, q_len=1, layer=0)
+    runs = {}
+    for mode in ("auto", "fixed", "none"):
+        runs[f"config 5 {mode}"] = run_attention(
+            case, cuda, split_kv=mode != "none", split_size=512,
+            split_mode="fixed" if mode == "fixed" else "auto", table_dtype=torch.int32,
+            cache=cache)
+    check_all_sequences(case, cache, runs, chunk=8)
+
+    prefix = dict(case)
+    prefix["context_lens"] = np.full(256, 2048, dtype=np.int64)
+    prefix["query"] = np.broadcast_to(q[:1], q.shape).copy()
+    for mode in ("fixed", "none"):
+        out, lse = run_attention(prefix, cuda, split_kv=mode != "none", split_size=512,
+                                 split_mode="fixed" if mode == "fixed" else "auto",
+                                 table_dtype=torch.int32, cache=cache)
+        assert (out == out[:1]).all() and (lse == lse[:1]).all(), mode
+    out, lse = run_attention(prefix, cuda, table_dtype=torch.int32, cache=cache)
+    want, want_lse = oracle(subset_case(prefix, cache, [0]))
+    assert_lowp_close(out, np.broadcast_to(want, out.shape), "shared prefix, balanced plan")
+    assert_lse_close(lse, np.broadcast_to(want_lse, lse.shape), "shared prefix lse")
+    assert device_errors(cuda) == 0
 
 
 def test_short_tables_raise_before_any_launch(cuda):
