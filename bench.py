@@ -170,10 +170,15 @@ class ClockSampler:
                 self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
             except Exception:
                 pass
-            time.sleep(0.0005)
+            time.sleep(0.0002)
 
     def start(self):
         if self._handle is not None:
+            # The launching thread holds the GIL while it issues kernels; a short
+            # switch interval lets the sampler run inside a timed region of a
+            # few milliseconds.
+            self._switch = sys.getswitchinterval()
+            sys.setswitchinterval(1e-4)
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
 
@@ -181,6 +186,7 @@ class ClockSampler:
         if self._thread is not None:
             self._stop.set()
             self._thread.join()
+            sys.setswitchinterval(self._switch)
         names = sorted(n for bit, n in _REASONS.items() if self.reasons & bit)
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}

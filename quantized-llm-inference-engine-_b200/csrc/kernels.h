@@ -84,7 +84,13 @@ cudaError_t decode_fp8_launch(const AttnArgs& a, const DecodeLaunch& launch,
 bool prefill_tc_supported(const AttnArgs& a);
 cudaError_t prefill_tc_launch(const AttnArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
                               const CUtensorMap& tmv, cudaStream_t stream);
-constexpr int kPrefillRows = 128;  // query rows per prefill CTA
+constexpr int kPrefillRows = 128;  // query rows per prefill query tile
+// The same shapes on the two-query-tile ping-pong kernel (prefill_fa.cu), which
+// prefill_tc_launch uses when LLMOPT_B200_PREFILL=fa.
+bool prefill_fa_enabled();
+bool prefill_fa_usable(const AttnArgs& a);
+cudaError_t prefill_fa_launch(const AttnArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
+                              const CUtensorMap& tmv, cudaStream_t stream);
 
 // Generic path: any dtype / head_dim <= 256 / block size / q_len (CUDA cores).
 constexpr int kGenericRowTile = 16;

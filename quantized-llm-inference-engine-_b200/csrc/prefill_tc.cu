@@ -605,6 +605,9 @@ bool prefill_tc_supported(const AttnArgs& a) {
 
 cudaError_t prefill_tc_launch(const AttnArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
                               const CUtensorMap& tmv, cudaStream_t stream) {
+  if (prefill_fa_enabled() && prefill_fa_usable(a)) {
+    return prefill_fa_launch(a, tmq, tmk, tmv, stream);
+  }
   const void* fn = select_prefill(a);
   if (fn == nullptr) return cudaErrorInvalidValue;
   const size_t smem = prefill_smem(a.head_dim);
