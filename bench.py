@@ -159,6 +159,9 @@ class ClockSampler:
             self._nvml = pynvml
             self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+            # the first queries of a handle are slow: make them before any timed region
+            pynvml.nvmlDeviceGetClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+            pynvml.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
         except Exception:
             self._handle = None
 

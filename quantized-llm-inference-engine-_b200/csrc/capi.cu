@@ -776,7 +776,13 @@ void plan_quant_splits(QuantLinearArgs* a, int sms) {
   a->k_per_split = a->k;
   if (!quant_linear_tc_supported(*a)) return;
   const long long tiles = a->k / 128;
-  const int want = quant_linear_splits(*a, sms);
+  int want = quant_linear_splits(*a, sms);
+  // LLMOPT_B200_QUANT_SPLITS=n fixes the split count (tuning measurements).
+  static const int forced = [] {
+    const char* v = std::getenv("LLMOPT_B200_QUANT_SPLITS");
+    return v != nullptr ? std::atoi(v) : 0;
+  }();
+  if (forced > 0) want = forced < (int)tiles ? forced : (int)tiles;
   const long long per = (tiles + want - 1) / want;
   a->k_per_split = per * 128;
   a->splits = (int)((tiles + per - 1) / per);

@@ -42,6 +42,8 @@
 // for its products before tensor memory is released).
 #include <float.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tc_common.cuh"
@@ -53,7 +55,9 @@ constexpr int kBS = 16;
 constexpr int kM = 128;                   // rows per query tile = TMEM lanes
 constexpr int kN = 128;                   // keys per K/V tile
 constexpr int kBlocksPerTile = kN / kBS;  // 8
-constexpr int kStages = 2;                // K ring and V ring depth
+constexpr int kKStages = 2;               // K ring depth
+constexpr int kVStages = 3;               // V ring depth (a V stage is held for a whole
+                                          // key tile: both tiles' P V products read it)
 constexpr int kBitsRing = 8;              // tile valid-block bits, indexed tile % 8
 constexpr int kKWarp = 8;
 constexpr int kVWarp = 9;
@@ -71,18 +75,18 @@ struct Layout {
   static constexpr int kSubs = D / 64;
   static constexpr int kQ = 0;
   static constexpr int kK = kQ + 2 * kSubs * kQSub;
-  static constexpr int kV = kK + kStages * kSubs * kKVSub;
-  static constexpr int kBar = kV + kStages * kSubs * kKVSub;
+  static constexpr int kV = kK + kKStages * kSubs * kKVSub;
+  static constexpr int kBar = kV + kVStages * kSubs * kKVSub;
   static constexpr int kBytes = kBar + 512;
 };
 static_assert(Layout<128>::kBytes <= 227 * 1024, "shared memory");
 
 struct Bars {
   uint64_t q_full;
-  uint64_t k_full[kStages];
-  uint64_t k_empty[kStages];
-  uint64_t v_full[kStages];
-  uint64_t v_empty[kStages];
+  uint64_t k_full[kKStages];
+  uint64_t k_empty[kKStages];
+  uint64_t v_full[kVStages];
+  uint64_t v_empty[kVStages];
   uint64_t bits_full[2];   // s_bits[j % 2] valid for key tile j
   uint64_t s_full[2];      // S(q, j) in TMEM: phase j of tile q's barrier
   uint64_t p_full[2];      // P(q, j) in TMEM (128 arrivals)
@@ -136,9 +140,10 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return x < -126.f ? 0.f : r;
 }
 
-// Columns c with (c & 7) >= 6 use the polynomial (a quarter of them).
+// Columns c with (c & 7) >= 8 - POLY use the polynomial (POLY eighths of them).
+template <int POLY>
 __device__ __forceinline__ float exp2_mixed(float x, int c) {
-  return (c & 7) >= 6 ? exp2_poly(x) : fast_exp2(x);
+  return (c & 7) >= 8 - POLY ? exp2_poly(x) : fast_exp2(x);
 }
 
 __device__ __forceinline__ long long tile_keys(const AttnArgs& a, long long ctx_s, int t_begin,
@@ -151,11 +156,11 @@ __device__ __forceinline__ long long tile_keys(const AttnArgs& a, long long ctx_
   return n < 0 ? 0 : n;
 }
 
-template <int D, int KV_DT>
+template <int D, int KV_DT, int POLY>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_fa_kernel(const __grid_constant__ CUtensorMap tmq,
                       const __grid_constant__ CUtensorMap tmk,
-                      const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
+                      const __grid_constant__ CUtensorMap tmv, const AttnArgs a, int pf) {
   griddep_wait();
   griddep_launch_dependents();
   using L = Layout<D>;
@@ -184,9 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     bars->abort = 0u;
     bars->seq = (int)rank;
     mbar_init(&bars->q_full, 1);
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < kKStages; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->k_empty[i], 1);
+    }
+    for (int i = 0; i < kVStages; ++i) {
       mbar_init(&bars->v_full[i], 1);
       mbar_init(&bars->v_empty[i], 1);
     }
@@ -243,6 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char* ring = is_k ? sK : sV;
     uint64_t* full = is_k ? bars->k_full : bars->v_full;
     uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
+    const int stages = is_k ? kKStages : kVStages;
     if (lane == 0) {
       prefetch_tensormap(map);
       if (is_k) {
@@ -275,6 +283,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
+    // L2 prefetch of the blocks of tile j + pf when tile j is issued (no shared
+    // memory, no completion): the later tile copies then mostly hit L2.
+    auto prefetch_tile = [&](int jj, int id0, bool v0, int id1, bool v1) {
+      const int jt = jj + pf;
+      if (pf <= 0 || jt >= kTilesPerGroup * 2) return;
+      const bool in_next = jt >= kTilesPerGroup;
+      const int id = in_next ? id1 : id0;
+      const bool v = in_next ? v1 : v0;
+      if (v && lane / kBlocksPerTile == jt % kTilesPerGroup) {
+#pragma unroll
+        for (int sub = 0; sub < kSubs; ++sub) {
+          asm volatile(
+              "cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(
+                  reinterpret_cast<uint64_t>(map)),
+              "r"(sub * 64), "r"(kh), "r"(0), "r"(id), "r"(a.layer)
+              : "memory");
+        }
+      }
+    };
     int id_cur, id_next;
     bool valid_cur, valid_next;
     int issued = 0;
@@ -287,11 +314,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool stop = false;
       for (int jj = 0; jj < jn; ++jj) {
         const int j = base + jj;
-        const int st = j % kStages;
+        const int st = j % stages;
         const unsigned mask = (vmask >> (jj * kBlocksPerTile)) & ((1u << kBlocksPerTile) - 1);
         const unsigned bytes = (unsigned)(__popc(mask) * kSubs * kBlockBytes);
-        if (lane == 0 && j >= kStages) {
-          wait_or_flag(&empty[st], (unsigned)((j / kStages - 1) & 1), a.err, &bars->abort);
+        prefetch_tile(jj, id_cur, valid_cur, id_next, valid_next);
+        if (lane == 0 && j >= stages) {
+          wait_or_flag(&empty[st], (unsigned)((j / stages - 1) & 1), a.err, &bars->abort);
         }
         stop = __shfl_sync(0xffffffffu,
                            *reinterpret_cast<volatile uint32_t*>(&bars->abort), 0) != 0u;
@@ -316,9 +344,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) {
       if (is_k) drain_wait(&bars->q_full, 0, a.err);
-      const int first = issued > kStages ? issued - kStages : 0;
+      const int first = issued > stages ? issued - stages : 0;
       for (int j = first; j < issued; ++j) {
-        drain_wait(&full[j % kStages], (unsigned)((j / kStages) & 1), a.err);
+        drain_wait(&full[j % stages], (unsigned)((j / stages) & 1), a.err);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -330,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // Tile j's K staged: relay its valid-block bits to the softmax warps.
     auto k_ready = [&](int j) {
-      wait_or_flag(&bars->k_full[j % kStages], (unsigned)((j / kStages) & 1), a.err,
+      wait_or_flag(&bars->k_full[j % kKStages], (unsigned)((j / kKStages) & 1), a.err,
                    &bars->abort);
       if (lane == 0) {
         bars->s_bits[j & 1] = bars->tile_bits[j % kBitsRing];
@@ -342,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto qk = [&](int q, int j) {
       if (lane == 0) {
         tc::fence_after_sync();
-        const uint32_t k_addr = smem_addr(sK + (j % kStages) * kSubs * kKVSub);
+        const uint32_t k_addr = smem_addr(sK + (j % kKStages) * kSubs * kKVSub);
         const uint32_t qa = q_addr + q * kSubs * kQSub;
         const uint32_t tmem_s = tmem + (uint32_t)(q * 128);
 #pragma unroll
@@ -361,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait_or_flag(&bars->p_full[q], (unsigned)(j & 1), a.err, &bars->abort);
       if (lane == 0) {
         tc::fence_after_sync();
-        const uint32_t v_addr = smem_addr(sV + (j % kStages) * kSubs * kKVSub);
+        const uint32_t v_addr = smem_addr(sV + (j % kVStages) * kSubs * kKVSub);
         const uint32_t tmem_p = tmem + (uint32_t)(q * 128);
         const uint32_t tmem_o = tmem + 256u + (uint32_t)(q * 128);
 #pragma unroll
@@ -376,8 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // Rows of V(j) that hold no valid key are zeroed before any P V reads them.
     auto v_ready = [&](int j) {
-      const int st = j % kStages;
-      wait_or_flag(&bars->v_full[st], (unsigned)((j / kStages) & 1), a.err, &bars->abort);
+      const int st = j % kVStages;
+      wait_or_flag(&bars->v_full[st], (unsigned)((j / kVStages) & 1), a.err, &bars->abort);
       const unsigned bits = bars->tile_bits[j % kBitsRing];
       unsigned char* v = sV + st * kSubs * kKVSub;
       bool zeroed = false;
@@ -415,10 +443,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (*reinterpret_cast<volatile uint32_t*>(&bars->abort) != 0u) break;
         v_ready(j);
         bool next = false;
+        const int last_q = j < n_q[1] ? 1 : 0;     // the last query tile that reads V(j)
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           if (j < n_q[q]) {
             pv(q, j);
+            if (q == last_q && lane == 0) tc::commit(&bars->v_empty[j % kVStages]);
             if (j + 1 < n_q[q]) {
               if (!next) {
                 k_ready(j + 1);
@@ -428,10 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (lane == 0) {
-          tc::commit(&bars->v_empty[j % kStages]);
-          if (next) tc::commit(&bars->k_empty[(j + 1) % kStages]);
-        }
+        if (lane == 0 && next) tc::commit(&bars->k_empty[(j + 1) % kKStages]);
         __syncwarp();
       }
     }
@@ -513,8 +540,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           const int cc = h * 32 + c;
-          const float p0 = exp2_mixed(fmaf(sv[cc], sl, -m_sub), cc);
-          const float p1 = exp2_mixed(fmaf(sv[cc + 1], sl, -m_sub), cc + 1);
+          const float p0 = exp2_mixed<POLY>(fmaf(sv[cc], sl, -m_sub), cc);
+          const float p1 = exp2_mixed<POLY>(fmaf(sv[cc + 1], sl, -m_sub), cc + 1);
           sum4[(c >> 1) & 3] += p0 + p1;
           pk[c / 2] = pack2<KV_DT>(p0, p1);
         }
@@ -592,9 +619,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Eighths of the exponentials evaluated by the polynomial: 2 by default,
+// LLMOPT_B200_FA_POLY=0|2|4 to measure the split.
+int fa_poly() {
+  static const int v = [] {
+    const char* e = getenv("LLMOPT_B200_FA_POLY");
+    if (e == nullptr) return 2;
+    const int x = atoi(e);
+    return x == 0 || x == 4 ? x : 2;
+  }();
+  return v;
+}
+
+// L2 prefetch distance in key tiles (LLMOPT_B200_FA_PF, 0..4; 0 = off).
+int fa_prefetch() {
+  static const int v = [] {
+    const char* e = getenv("LLMOPT_B200_FA_PF");
+    const int x = e != nullptr ? atoi(e) : 2;
+    return x < 0 ? 0 : (x > 4 ? 4 : x);
+  }();
+  return v;
+}
+
 template <int D, int KV_DT>
 const void* fa_ptr() {
-  return reinterpret_cast<const void*>(&prefill_fa_kernel<D, KV_DT>);
+  switch (fa_poly()) {
+    case 0: return reinterpret_cast<const void*>(&prefill_fa_kernel<D, KV_DT, 0>);
+    case 4: return reinterpret_cast<const void*>(&prefill_fa_kernel<D, KV_DT, 4>);
+    default: return reinterpret_cast<const void*>(&prefill_fa_kernel<D, KV_DT, 2>);
+  }
 }
 
 const void* select_fa(const AttnArgs& a) {
@@ -631,8 +684,9 @@ cudaError_t prefill_fa_launch(const AttnArgs& a, const CUtensorMap& tmq, const C
   const long long grid = a.batch * a.kv_heads * ctiles;
   if (grid <= 0) return cudaSuccess;
   if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  int pf = fa_prefetch();
   void* args[] = {const_cast<CUtensorMap*>(&tmq), const_cast<CUtensorMap*>(&tmk),
-                  const_cast<CUtensorMap*>(&tmv), const_cast<AttnArgs*>(&a)};
+                  const_cast<CUtensorMap*>(&tmv), const_cast<AttnArgs*>(&a), &pf};
   return launch_pdl(fn, dim3((unsigned)grid), dim3(kThreads), args, smem, stream);
 }
 
