@@ -20,9 +20,9 @@
 //   While softmax group 0 turns S0 into P0, the tensor core computes P1 V and
 //   the next S1, and the other way round: the exponentials of one tile hide
 //   behind the matrix products of the other.
-// * A quarter of the exponentials run as a polynomial on the FMA pipe
-//   (exp2_poly) instead of the special-function unit, whose 16 results per
-//   clock per SM would otherwise take as long as the tile's matrix products.
+// * Optionally a quarter or half of the exponentials run as a polynomial on the
+//   FMA pipe (exp2_poly) instead of the special-function unit (measured slower
+//   on B200 for this kernel, so off by default).
 // * Warps: 0-3 softmax of tile 0, 4-7 softmax of tile 1 (one thread per row =
 //   tensor-memory lane, a score row of 128 fp32 values in registers), 8 K
 //   loader (Q once, then K tiles through the block table: 5-D map over the
@@ -619,23 +619,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Eighths of the exponentials evaluated by the polynomial: 2 by default,
-// LLMOPT_B200_FA_POLY=0|2|4 to measure the split.
+// Eighths of the exponentials evaluated by the polynomial: none by default
+// (measured fastest on B200: the special-function unit is not the limit),
+// LLMOPT_B200_FA_POLY=2|4 for a quarter or a half.
 int fa_poly() {
   static const int v = [] {
     const char* e = getenv("LLMOPT_B200_FA_POLY");
-    if (e == nullptr) return 2;
+    if (e == nullptr) return 0;
     const int x = atoi(e);
-    return x == 0 || x == 4 ? x : 2;
+    return x == 2 || x == 4 ? x : 0;
   }();
   return v;
 }
 
-// L2 prefetch distance in key tiles (LLMOPT_B200_FA_PF, 0..4; 0 = off).
+// L2 prefetch distance in key tiles (LLMOPT_B200_FA_PF, 0..4; off by default:
+// on B200 a TMA L2 prefetch ahead of the loads did not shorten them).
 int fa_prefetch() {
   static const int v = [] {
     const char* e = getenv("LLMOPT_B200_FA_PF");
-    const int x = e != nullptr ? atoi(e) : 2;
+    const int x = e != nullptr ? atoi(e) : 0;
     return x < 0 ? 0 : (x > 4 ? 4 : x);
   }();
   return v;
@@ -644,9 +646,9 @@ int fa_prefetch() {
 template <int D, int KV_DT>
 const void* fa_ptr() {
   switch (fa_poly()) {
-    case 0: return reinterpret_cast<const void*>(&prefill_fa_kernel<D, KV_DT, 0>);
+    case 2: return reinterpret_cast<const void*>(&prefill_fa_kernel<D, KV_DT, 2>);
     case 4: return reinterpret_cast<const void*>(&prefill_fa_kernel<D, KV_DT, 4>);
-    default: return reinterpret_cast<const void*>(&prefill_fa_kernel<D, KV_DT, 2>);
+    default: return reinterpret_cast<const void*>(&prefill_fa_kernel<D, KV_DT, 0>);
   }
 }
 

@@ -176,3 +176,22 @@ def test_input_dtype_must_match_compute_dtype(cuda):
     with pytest.raises(RuntimeError, match="dtype"):
         layer(torch.zeros(2, 128, dtype=torch.float16, device=cuda))
     assert layer(torch.zeros(0, 128, dtype=torch.bfloat16, device=cuda)).shape == (0, 64)
+
+
+@pytest.mark.parametrize("kind", ["bf16", "f16"])
+@pytest.mark.parametrize("bits,symmetric", [(4, True), (4, False), (2, True), (2, False)])
+@pytest.mark.parametrize("group", [128, 256, 2048])
+def test_decode_batch_path(cuda, kind, bits, symmetric, group):
+    """Up to 16 tokens with groups of whole 128-column chunks run on the
+    register-streaming kernel (zero point applied per group through the token
+    sums), split over k; every token count from 1 to 16 crosses its one- and
+    two-tile forms."""
+    n, k = 1024, 2048
+    layer, (qw, s, z, b) = _random_layer(1000 + bits + group + 7 * symmetric, n, k, bits, group,
+                                         symmetric, kind, device=cuda)
+    rng = np.random.default_rng(group + bits)
+    for m in (1, 3, 8, 9, 16):
+        x = po.from_f32(rng.standard_normal((m, k)).astype(np.float32), kind)
+        y = layer(to_dev(x, kind, cuda)).float().cpu().numpy()
+        want = qo.quant_linear(x, kind, qw, s, z, bits, group, symmetric, (n, k), b)
+        _assert_close(y, want, kind, f"m={m}")
