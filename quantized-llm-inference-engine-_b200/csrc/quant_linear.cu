@@ -606,174 +606,6 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_acc_kernel(const QuantLinear
   }
 }
 
-// ---- decode batches: 2- and 4-bit codes, groups of whole 128-column chunks --------
-//
-// For up to 16 tokens the layer is a weight stream: every code is read once and
-// meets at most 16 token values.  wq_gemv_kernel keeps no shared memory and no
-// block-wide barrier: each warp owns 16 rows and a k range and streams them
-// with 16-byte loads straight into registers, kDepth chunks of 128 columns
-// ahead, so a resident set of ~24 warps per SM keeps enough bytes in flight to
-// cover the memory latency.  Per chunk, lane (g, t) holds 32 codes of rows g
-// and g + 8 (columns 32 t .. 32 t + 31 of the chunk) and the 32 matching values
-// of token g (and g + 8) of x, read through L1.  MMA k-step (w, h) pairs the
-// lane's codes (2h, 2h+4) and (2h+1, 2h+5) of word w with the token values of
-// the same columns (the k order inside an MMA is free as long as A and B agree).
-// The codes enter the MMA as 128 + q (bf16) or 1024 + q (f16) - one LOP3 of the
-// nibbles into the magic number's mantissa, no subtraction - and a second MMA
-// with an all-ones A operand sums the token values of the same columns, so per
-// group y += s * (sum (B + q) x - (B + z) sum x), with B the magic base: the
-// zero point (2^(bits-1) when symmetric) costs one MMA per k-step, not a
-// subtraction per code pair.  Both products are exact in fp32 (integers times
-// 16-bit values), the sums carry fp32 rounding only.
-constexpr int kGvRows = 16;          // rows per warp
-constexpr int kGvWarps = 4;          // independent warps per CTA
-constexpr int kGvDepth = 4;          // chunks of codes loaded ahead
-
-__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ uint32_t word_of4(const uint4& v, int i) {
-  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
-
-template <int DT, int NT>
-__global__ void __launch_bounds__(kGvWarps * 32) wq_gemv_kernel(const QuantLinearArgs a) {
-  griddep_wait();
-  griddep_launch_dependents();
-  using P = Pair<DT>;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int g = lane >> 2;
-  const int t = lane & 3;
-  const long long r0 = ((long long)blockIdx.x * kGvWarps + warp) * kGvRows;
-  if (r0 >= a.n) return;                              // n % 16 == 0: whole warps only
-  const long long kb = (long long)blockIdx.y * a.k_per_split;
-  const long long ke = kb + a.k_per_split < a.k ? kb + a.k_per_split : a.k;
-  const int nchunks = (int)((ke - kb) / kKT);
-  const long long row_bytes = a.k / 2;
-  const unsigned char* wa = a.qweight + (r0 + g) * row_bytes + kb / 2 + 16 * t;
-  const unsigned char* wb = wa + 8 * row_bytes;
-  const long long groups = a.k / a.group;
-  const int cpg = a.group / kKT;                      // chunks per group (group % 128 == 0)
-  const float base = P::kBase;
-  const float zsym = (float)(1 << (a.bits - 1));
-  // token rows of this lane's B fragments: g (n-tile 0) and g + 8 (n-tile 1)
-  const unsigned short* xs[NT];
-  bool xok[NT];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const long long tok = nt * 8 + g;
-    xok[nt] = tok < a.m;
-    xs[nt] = static_cast<const unsigned short*>(a.x) + (xok[nt] ? tok * a.ldx : 0) + kb + 32 * t;
-  }
-  const uint32_t ones2 = as_u32(P::splat(1.f));
-  const uint32_t ones[4] = {ones2, ones2, ones2, ones2};
-
-  float acc[NT][4];
-  float part[NT][4];
-  float xsum[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[nt][e] = part[nt][e] = xsum[nt][e] = 0.f;
-  }
-  uint4 ca[kGvDepth], cb[kGvDepth];
-#pragma unroll
-  for (int d = 0; d < kGvDepth; ++d) {
-    if (d < nchunks) {
-      ca[d] = ldg_nc_v4(wa + (long long)d * (kKT / 2));
-      cb[d] = ldg_nc_v4(wb + (long long)d * (kKT / 2));
-    }
-  }
-  long long grp = kb / a.group;
-  int in_grp = (int)((kb % a.group) / kKT);
-  for (int c0 = 0; c0 < nchunks; c0 += kGvDepth) {
-#pragma unroll
-    for (int d = 0; d < kGvDepth; ++d) {
-      const int c = c0 + d;
-      if (c < nchunks) {
-        const uint4 wra = ca[d], wrb = cb[d];
-        if (c + kGvDepth < nchunks) {                 // refill this slot kDepth chunks ahead
-          ca[d] = ldg_nc_v4(wa + (long long)(c + kGvDepth) * (kKT / 2));
-          cb[d] = ldg_nc_v4(wb + (long long)(c + kGvDepth) * (kKT / 2));
-        }
-        uint4 xv[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            xv[nt][w] = xok[nt] ? ldg_nc_v4(xs[nt] + (long long)c * kKT + 8 * w)
-                                : make_uint4(0u, 0u, 0u, 0u);
-          }
-        }
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const uint32_t qa = word_of4(wra, w), qb = word_of4(wrb, w);
-          uint32_t pa[4], pb[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            pa[j] = ((qa >> (4 * j)) & 0x000F000Fu) | P::kMagic;
-            pb[j] = ((qb >> (4 * j)) & 0x000F000Fu) | P::kMagic;
-          }
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            const uint4 x8 = xv[nt][w];
-            const uint32_t b[4] = {__byte_perm(x8.x, x8.z, 0x5410), __byte_perm(x8.x, x8.z, 0x7632),
-                                   __byte_perm(x8.y, x8.w, 0x5410), __byte_perm(x8.y, x8.w, 0x7632)};
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const uint32_t af[4] = {pa[2 * h], pb[2 * h], pa[2 * h + 1], pb[2 * h + 1]};
-              mma_16816<DT>(part[nt], af, b[2 * h], b[2 * h + 1]);
-              mma_16816<DT>(xsum[nt], ones, b[2 * h], b[2 * h + 1]);
-            }
-          }
-        }
-        if (++in_grp == cpg || c == nchunks - 1) {
-          // group epilogue: rows g (e = 0, 1) and g + 8 (e = 2, 3)
-          const long long gi0 = (r0 + g) * groups + grp;
-          const long long gi1 = gi0 + 8 * groups;
-          const float s0 = a.scales[gi0], s1 = a.scales[gi1];
-          const float z0 = base + (a.symmetric ? zsym : a.zeros[gi0]);
-          const float z1 = base + (a.symmetric ? zsym : a.zeros[gi1]);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            acc[nt][0] = fmaf(s0, fmaf(-z0, xsum[nt][0], part[nt][0]), acc[nt][0]);
-            acc[nt][1] = fmaf(s0, fmaf(-z0, xsum[nt][1], part[nt][1]), acc[nt][1]);
-            acc[nt][2] = fmaf(s1, fmaf(-z1, xsum[nt][2], part[nt][2]), acc[nt][2]);
-            acc[nt][3] = fmaf(s1, fmaf(-z1, xsum[nt][3], part[nt][3]), acc[nt][3]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) part[nt][e] = xsum[nt][e] = 0.f;
-          }
-          in_grp = 0;
-          ++grp;
-        }
-      }
-    }
-  }
-  // c-fragment e of n-tile nt: row r0 + g + 8 (e >> 1), token 8 nt + 2 t + (e & 1)
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const long long tok = nt * 8 + 2 * t + (e & 1);
-      const long long f = r0 + g + 8 * (e >> 1);
-      if (tok >= a.m) continue;
-      if (a.partial != nullptr) {
-        a.partial[((long long)blockIdx.y * a.m + tok) * a.n + f] = acc[nt][e];
-      } else {
-        float v = acc[nt][e];
-        if (a.bias != nullptr) v += load_f32<DT>(a.bias, f);
-        store_f32<DT>(a.out, tok * a.ldo + f, v);
-      }
-    }
-  }
-}
-
 // ---- 2- and 4-bit codes on the 5th-generation tensor cores (opt-in) ------------
 //
 // For token batches the weight is dequantized once per CTA into shared memory
@@ -1123,31 +955,10 @@ bool quant_linear_tc_supported(const QuantLinearArgs& a) {
          (reinterpret_cast<uintptr_t>(a.qweight) & 15) == 0;
 }
 
-// Decode batches (up to 16 tokens) of 2/4-bit codes whose groups are whole
-// 128-column chunks run on wq_gemv_kernel (LLMOPT_B200_QUANT_GEMV=0 turns it off).
-bool quant_linear_gemv_supported(const QuantLinearArgs& a) {
-  static const bool on = [] {
-    const char* v = std::getenv("LLMOPT_B200_QUANT_GEMV");
-    return !(v != nullptr && v[0] == '0');
-  }();
-  return on && quant_linear_tc_supported(a) && a.bits < 8 && a.m <= 16 && a.group % kKT == 0;
-}
-
 // Splits of the k range: about two full waves of CTAs at the kernel's
 // occupancy (one wave leaves a ragged tail when the tile count is not a
-// multiple of the slots; more splits cost partial traffic).  For the
-// decode-batch kernel: enough warps for ~24 per SM, each streaming at least
-// four chunks.
+// multiple of the slots; more splits cost partial traffic).
 int quant_linear_splits(const QuantLinearArgs& a, int sm_count) {
-  if (quant_linear_gemv_supported(a)) {
-    const long long warps = a.n / kGvRows;
-    const long long want = 24LL * sm_count;
-    long long splits = (want + warps - 1) / (warps > 0 ? warps : 1);
-    const long long max_splits = a.k / (kKT * kGvDepth);
-    if (splits > max_splits) splits = max_splits;
-    if (splits > 16) splits = 16;
-    return (int)(splits < 1 ? 1 : splits);
-  }
   const GemmShape g = gemm_shape(a);
   const long long ctas = (a.n / g.rows) * ((a.m + g.tokens - 1) / g.tokens);
   const long long tiles = a.k / kKT;
@@ -1178,26 +989,14 @@ cudaError_t quant_linear_launch(const QuantLinearArgs& a, cudaStream_t stream) {
     if (gx > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidConfiguration;
     return launch_pdl(fn, dim3((unsigned)gx, (unsigned)gy), dim3(256), args, 0, stream);
   }
-  cudaError_t e;
-  if (quant_linear_gemv_supported(a)) {
-    const void* fn =
-        a.m <= 8 ? (a.x_dtype == kBF16 ? reinterpret_cast<const void*>(&wq_gemv_kernel<kBF16, 1>)
-                                       : reinterpret_cast<const void*>(&wq_gemv_kernel<kF16, 1>))
-                 : (a.x_dtype == kBF16 ? reinterpret_cast<const void*>(&wq_gemv_kernel<kBF16, 2>)
-                                       : reinterpret_cast<const void*>(&wq_gemv_kernel<kF16, 2>));
-    const long long gx = a.n / (kGvRows * kGvWarps);
-    if (gx > 0x7fffffffLL || a.splits > 65535) return cudaErrorInvalidConfiguration;
-    e = launch_pdl(fn, dim3((unsigned)gx, (unsigned)a.splits, 1u), dim3(kGvWarps * 32), args, 0,
-                   stream);
-  } else {
-    const GemmShape g = gemm_shape(a);
-    const long long gx = a.n / g.rows, gz = (a.m + g.tokens - 1) / g.tokens;
-    if (gx > 0x7fffffffLL || gz > 65535 || a.splits > 65535) return cudaErrorInvalidConfiguration;
-    e = cudaFuncSetAttribute(g.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
-    if (e != cudaSuccess) return e;
-    e = launch_pdl(g.fn, dim3((unsigned)gx, (unsigned)a.splits, (unsigned)gz),
-                   dim3((unsigned)g.threads), args, g.smem, stream);
-  }
+  const GemmShape g = gemm_shape(a);
+  const long long gx = a.n / g.rows, gz = (a.m + g.tokens - 1) / g.tokens;
+  if (gx > 0x7fffffffLL || gz > 65535 || a.splits > 65535) return cudaErrorInvalidConfiguration;
+  cudaError_t e =
+      cudaFuncSetAttribute(g.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(g.fn, dim3((unsigned)gx, (unsigned)a.splits, (unsigned)gz),
+                 dim3((unsigned)g.threads), args, g.smem, stream);
   if (e != cudaSuccess || a.partial == nullptr) return e;
   const void* rfn = a.x_dtype == kBF16 ? reinterpret_cast<const void*>(&wq_reduce_kernel<kBF16>)
                                        : reinterpret_cast<const void*>(&wq_reduce_kernel<kF16>);

@@ -182,10 +182,9 @@ def test_input_dtype_must_match_compute_dtype(cuda):
 @pytest.mark.parametrize("bits,symmetric", [(4, True), (4, False), (2, True), (2, False)])
 @pytest.mark.parametrize("group", [128, 256, 2048])
 def test_decode_batch_path(cuda, kind, bits, symmetric, group):
-    """Up to 16 tokens with groups of whole 128-column chunks run on the
-    register-streaming kernel (zero point applied per group through the token
-    sums), split over k; every token count from 1 to 16 crosses its one- and
-    two-tile forms."""
+    """Decode batches (1 to 16 tokens) over groups of whole 128-column tiles
+    and one group per row, 2- and 4-bit codes, symmetric and asymmetric, both
+    16-bit dtypes, the k range split across CTAs."""
     n, k = 1024, 2048
     layer, (qw, s, z, b) = _random_layer(1000 + bits + group + 7 * symmetric, n, k, bits, group,
                                          symmetric, kind, device=cuda)
