@@ -91,6 +91,14 @@ bool prefill_fa_enabled();
 bool prefill_fa_usable(const AttnArgs& a);
 cudaError_t prefill_fa_launch(const AttnArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
                               const CUtensorMap& tmv, cudaStream_t stream);
+// head_dim 128 on 2-SM tensor-core pairs (prefill_pair.cu), which
+// prefill_tc_launch uses for those shapes unless LLMOPT_B200_PREFILL names
+// another kernel (tc or fa).
+bool prefill_pair_enabled();
+bool prefill_pair_usable(const AttnArgs& a);
+cudaError_t prefill_pair_launch(const AttnArgs& a, const CUtensorMap& tmq,
+                                const CUtensorMap& tmk, const CUtensorMap& tmv,
+                                cudaStream_t stream);
 
 // Generic path: any dtype / head_dim <= 256 / block size / q_len (CUDA cores).
 constexpr int kGenericRowTile = 16;

@@ -605,6 +605,9 @@ bool prefill_tc_supported(const AttnArgs& a) {
 
 cudaError_t prefill_tc_launch(const AttnArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
                               const CUtensorMap& tmv, cudaStream_t stream) {
+  if (prefill_pair_enabled() && prefill_pair_usable(a)) {
+    return prefill_pair_launch(a, tmq, tmk, tmv, stream);
+  }
   if (prefill_fa_enabled() && prefill_fa_usable(a)) {
     return prefill_fa_launch(a, tmq, tmk, tmv, stream);
   }
