@@ -372,6 +372,30 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed two-lane fp32 fused multiply-add (sm_100): per lane exactly the
+// IEEE operation of fmaf, at one issue for two.
+// (b, b) and (c, c) come pre-packed (pack2f), built once outside the loop.
+__device__ __forceinline__ uint64_t pack2f(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void ffma2(float& x0, float& x1, float a0, float a1, uint64_t bb,
+                                      uint64_t cc) {
+  asm("{\n\t.reg .b64 ra, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "fma.rn.f32x2 rd, ra, %4, %5;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "l"(bb), "l"(cc));
+}
+// max(a, b, c) in one instruction (NaN operands ignored, as fmaxf does).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ float warp_max_xor(float v, int mask) {
   return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, mask));
 }

@@ -398,40 +398,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool bf16 = KV_DT == kBF16;
       const uint32_t idesc_qk = tc::instr_desc_f16(bf16, 2 * kM, kN, false, false);
       const uint32_t idesc_pv = tc::instr_desc_f16(bf16, 2 * kM, kD, false, true);
-      const uint32_t q_addr = smem_addr(sQ);
-      // S(q, j) = Q(q) K(j)^T over the pair: 256 rows x 128 keys.
-      auto qk = [&](int q, int j) {
+      // The issuing warp shares its SM sub-partition with two softmax warps,
+      // so the loops below carry few instructions per MMA: descriptors are
+      // built once and stepped by constants (the start address is bits 0-13,
+      // address / 16, and no step carries out of it below 256 KB), and ring
+      // stages are counters, not remainders.
+      const uint64_t qdesc = tc::smem_desc_sw128(smem_addr(sQ), 16, 1024);
+      const uint64_t kdesc = tc::smem_desc_sw128(smem_addr(sK), 16, 1024);
+      const uint64_t vdesc = tc::smem_desc_sw128(smem_addr(sV), kVStage, 1024);
+      // S(q, j) = Q(q) K^T over the pair (256 rows x 128 keys), K in stage ks.
+      auto qk = [&](int q, int ks) {
         if (lane == 0) {
           tc::fence_after_sync();
-          const uint32_t k_addr = smem_addr(sK + (j % kKStages) * kKStage);
-          const uint32_t qa = q_addr + q * kSubs * kQSub;
+          const uint64_t a0 = qdesc + (uint64_t)((q * kSubs * kQSub) >> 4);
+          const uint64_t b0 = kdesc + (uint64_t)((ks * kKStage) >> 4);
           const uint32_t tmem_s = tmem + (uint32_t)(q * 128);
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk) {
             const uint32_t koff = (kk & 3) * 32;
-            tc::mma_f16_pair(tmem_s,
-                             tc::smem_desc_sw128(qa + (kk >> 2) * kQSub + koff, 16, 1024),
-                             tc::smem_desc_sw128(k_addr + (kk >> 2) * kKSub + koff, 16, 1024),
-                             idesc_qk, kk > 0 ? 1u : 0u);
+            tc::mma_f16_pair(tmem_s, a0 + (uint64_t)(((kk >> 2) * kQSub + koff) >> 4),
+                             b0 + (uint64_t)(((kk >> 2) * kKSub + koff) >> 4), idesc_qk,
+                             kk > 0 ? 1u : 0u);
           }
           tc::commit_pair(&bars->s_full[q], kPairMask);
         }
         __syncwarp();
       };
-      // O(q) += P(q, j) V(j) over the pair: 256 rows x 128 dims.
-      auto pv = [&](int q, int j) {
+      // O(q) += P(q, j) V over the pair (256 rows x 128 dims), V in stage vs.
+      auto pv = [&](int q, int vs, bool first, bool last) {
         if (lane == 0) {
           tc::fence_after_sync();
-          const uint32_t v_addr = smem_addr(sV + (j % kVStages) * kVStage);
+          const uint64_t b0 = vdesc + (uint64_t)((vs * kVStage) >> 4);
           const uint32_t tmem_p = tmem + (uint32_t)(q * 128);
           const uint32_t tmem_o = tmem + 256u + (uint32_t)(q * 128);
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
             tc::mma_f16_ts_pair(tmem_o, tmem_p + kk * 8,
-                                tc::smem_desc_sw128(v_addr + kk * 16 * 128, kVStage, 1024),
-                                idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                                b0 + (uint64_t)((kk * 16 * 128) >> 4), idesc_pv,
+                                (!first || kk > 0) ? 1u : 0u);
           }
-          if (j == n_q[q] - 1) tc::commit_pair(&bars->o_final[q], kPairMask);
+          if (last) tc::commit_pair(&bars->o_final[q], kPairMask);
         }
         __syncwarp();
       };
@@ -444,9 +450,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (ok && n_q[1] > 0) qk(1, 0);
         if (lane == 0) tc::commit_pair(&bars->k_empty[0], kPairMask);
         __syncwarp();
+        int ks = 1 % kKStages;      // stage of K(j + 1)
+        int vs = 0;                 // stage of V(j)
+        int rs = 0;                 // ready-ring slot of tile j
+        unsigned rph = 0;           // its phase parity
         for (int j = 0; j < n_tiles && ok; ++j) {
-          ok = pw.wait(&bars->ready[j % kReadyRing], (unsigned)((j / kReadyRing) & 1),
-                       kErrWaitPeer);
+          ok = pw.wait(&bars->ready[rs], rph, kErrWaitPeer);
           bool next = false;
           const int last_q = j < n_q[1] ? 1 : 0;     // the last query tile that reads V(j)
 #pragma unroll
@@ -454,18 +463,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (ok && j < n_q[q]) {
               // Both CTAs' softmax warps have written P(q, j).
               ok = pw.wait(&bars->p_full[q], (unsigned)(j & 1), kErrWaitData);
-              if (ok) pv(q, j);
-              if (q == last_q && lane == 0) {
-                tc::commit_pair(&bars->v_empty[j % kVStages], kPairMask);
-              }
+              if (ok) pv(q, vs, j == 0, j == n_q[q] - 1);
+              if (q == last_q && lane == 0) tc::commit_pair(&bars->v_empty[vs], kPairMask);
               if (ok && j + 1 < n_q[q]) {
                 next = true;
-                qk(q, j + 1);
+                qk(q, ks);
               }
             }
           }
-          if (lane == 0 && next) tc::commit_pair(&bars->k_empty[(j + 1) % kKStages], kPairMask);
+          if (lane == 0 && next) tc::commit_pair(&bars->k_empty[ks], kPairMask);
           __syncwarp();
+          ks = ks + 1 == kKStages ? 0 : ks + 1;
+          vs = vs + 1 == kVStages ? 0 : vs + 1;
+          rs = rs + 1 == kReadyRing ? 0 : rs + 1;
+          rph ^= rs == 0 ? 1u : 0u;
         }
       }
       if (lane == 0) tc::commit_pair(&bars->mma_done, kPairMask);
@@ -529,13 +540,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           sv[c] = ok ? sv[c] : -INFINITY;
         }
       }
+      // Row maximum: 8 strided chains of three-input maxima.
       float mx8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+      for (int k = 0; k < 8; ++k) {
+        float acc = max3f(sv[k], sv[k + 8], sv[k + 16]);
 #pragma unroll
-      for (int c = 8; c < kN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], sv[c]);
-      const float m01 = fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3]));
-      const float m23 = fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+        for (int i = 3; i + 1 < 16; i += 2) acc = max3f(acc, sv[k + 8 * i], sv[k + 8 * i + 8]);
+        mx8[k] = fmaxf(acc, sv[k + 120]);
+      }
+      const float m01 = max3f(mx8[0], mx8[1], max3f(mx8[2], mx8[3], mx8[4]));
+      const float m23 = max3f(mx8[5], mx8[6], mx8[7]);
       const float sl = (capped || !(scale_log2 > 0.f)) ? 1.f : scale_log2;
       const float rowmax = fmaxf(m01, m23) * sl;
       const float m_new = rowmax > m_used + kRescaleLog2 ? rowmax : m_used;
@@ -543,22 +558,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool rescale = j > 0 && m_new != m_used && m_used != -INFINITY;
       const float alpha = rescale ? fast_exp2(m_used - m_new) : 1.f;
       m_used = m_new;
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-      // P over the first 64 columns of S(j), 32 keys (16 columns) at a time.
+      // P over the first 64 columns of S(j), 32 keys (16 columns) at a time;
+      // the exponent arguments in packed two-float arithmetic (per lane the
+      // same IEEE fused multiply-add as fmaf).  Packed row sums would spill.
+      float sa0 = 0.f, sa1 = 0.f, sb0 = 0.f, sb1 = 0.f;
+      const uint64_t sl2 = pack2f(sl, sl);
+      const uint64_t nm2 = pack2f(-m_sub, -m_sub);
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         uint32_t pk[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
           const int cc = h * 32 + c;
-          const float p0 = fast_exp2(fmaf(sv[cc], sl, -m_sub));
-          const float p1 = fast_exp2(fmaf(sv[cc + 1], sl, -m_sub));
-          sum4[(c >> 1) & 3] += p0 + p1;
+          float x0, x1;
+          ffma2(x0, x1, sv[cc], sv[cc + 1], sl2, nm2);
+          const float p0 = fast_exp2(x0);
+          const float p1 = fast_exp2(x1);
+          if ((c >> 1) & 1) {
+            sb0 += p0;
+            sb1 += p1;
+          } else {
+            sa0 += p0;
+            sa1 += p1;
+          }
           pk[c / 2] = pack2<KV_DT>(p0, p1);
         }
         tc::tmem_st16u(tmem_s + h * 16, pk);
       }
-      l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+      l = l * alpha + ((sa0 + sb0) + (sa1 + sb1));
       // O rescaled once the scores are dead.  S(j) was committed after
       // P(j-1) V(j-1), so O is stable; P(j) V(j) is issued only after the
       // arrivals below.
