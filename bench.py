@@ -769,19 +769,25 @@ def run_extra(args) -> None:
         if wl["kind"] == "prefill":
             flops = prefill_flops(wl["ctx"] - q_len, q_len, H, HEAD_DIM)
             app = B * q_len * KVH * HEAD_DIM * 2 * 4
-            peak = 1705.1
+            peak, peak_kind = 1590.0, "fallback"
             try:
                 with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
-                    peak = float(json.load(f)["bf16_tflops"])
+                    peak, peak_kind = float(json.load(f)["bf16_tflops"]), "measured"
             except Exception:
                 pass
+            # The kernel the library picks for head_dim 128 (LLMOPT_B200_PREFILL).
+            choice = os.environ.get("LLMOPT_B200_PREFILL", "") or "pair"
+            kernel = {"tc": "prefill_tc_kernel (one SM, one query tile)",
+                      "fa": "prefill_fa_kernel (one SM, two query tiles)"}.get(
+                          choice, "prefill_pair_kernel (2-SM pairs, cta_group::2)")
             tf = flops / (attn_ms * 1e-3) / 1e12
             line.update({"metric": "chunked-prefill causal attention TFLOP/s", "unit": "TFLOP/s",
                          "value": round(tf, 1), "algorithmic_flops": int(flops),
                          "append_GBps": round(app / (append_ms * 1e-3) / 1e9, 1),
                          "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak,
                                       "unit": "TFLOP/s", "frac": round(tf / peak, 4),
-                                      "kernel": "prefill_tc_kernel"}})
+                                      "kernel": kernel,
+                                      "peak_kind": f"{peak_kind} bf16_tflops (burst)"}})
         else:
             dec = decode_bytes(wl["ctx"], KVH, HEAD_DIM, 2, B, H, 2, 2, BLOCK)
             value = dec / (ms_step * 1e-3) / 1e9
