@@ -330,6 +330,7 @@ int choose(AttnArgs& a, long long split_tokens, int device, bool encode_maps, Ch
         if (occ > kMaxBalancedCtasPerSm) occ = kMaxBalancedCtasPerSm;
         long long ctas = (long long)sms * occ / head_groups;
         if (ctas < 1) ctas = 1;
+        if (!e4m3 && c->launch.streams == 2) ctas *= 2;  // plan ranges, two per CTA
         c->plan.ctas = (int)ctas;
         c->plan.split_blocks = 0;
         c->plan.splits = 0;

@@ -661,6 +661,7 @@ bool decode_fp8_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch)
     return false;
   }
   launch->heads_per_cta = hpc;
+  launch->streams = 1;
   launch->self_issue = sp ? 1 : 0;
   launch->stages = stages;
   launch->ctas_per_sm = occ;

@@ -18,10 +18,17 @@
 // is -1 (or out of range) are not loaded at all.  A ring of `stages` buffers
 // with full/empty mbarriers keeps several blocks in flight per SM.
 //
-// Self-issuing mode (SP, used when a CTA holds one KV head): the CTA is one
-// warp that issues its own K/V copies a ring's depth ahead of the block it is
-// consuming, into stages it has already consumed - no producer warp, so about
-// twice as many CTAs (and copy issuers, what limits this kernel) fit per SM.
+// Two-stream mode (streams == 2, used when a rank holds one KV head): the CTA
+// keeps the two-head layout and producer warp, but its two consumer warps take
+// the same head over two consecutive ranges of the balanced plan (two
+// "virtual CTAs"): the producer stages block i of each range into the two head
+// slots of ring stage i, so each copy issuer keeps two streams in flight, as
+// it does for two heads.
+//
+// Self-issuing mode (SP, the one-head alternative): the CTA is one warp that
+// issues its own K/V copies a ring's depth ahead of the block it is consuming,
+// into stages it has already consumed - no producer warp, so about twice as
+// many CTAs fit per SM.
 //
 // Math.  Consumer warp w handles KV head (first + w).  Its query rows (the
 // group's heads x q_len, padded to 16) are the A operand of m16n8k16 MMAs:
@@ -92,11 +99,13 @@ __device__ __forceinline__ void load_q_frags(const AttnArgs& a, long long s, int
 }
 
 // SP: 12 one-warp CTAs per SM by registers (168 a thread at head_dim 128).
-template <int D, int Q_DT, int KV_DT, bool SP>
+// ST: two-stream mode (never together with SP).
+template <int D, int Q_DT, int KV_DT, bool SP, bool ST>
 __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1)
     decode_tma_kernel(const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const AttnArgs a, const int hpc,
                       const int nstages) {
+  constexpr int streams = ST ? 2 : 1;
   // When the dependent kernel (the combine, or the next decode) may start
   // launching, measured on B200: with a producer warp, right away - the next
   // grid's CTAs then fill SMs as this grid's tail CTAs exit; with self-issuing
@@ -122,12 +131,12 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
     unsigned char* tail = sm.stages + (size_t)nstages * stage_bytes;
     sm.full = reinterpret_cast<uint64_t*>(tail);
     sm.empty = sm.full + nstages;
-    sm.meta = reinterpret_cast<int*>(sm.empty + nstages);
-    sm.prefix = sm.meta + nstages;
+    sm.meta = reinterpret_cast<int*>(sm.empty + nstages);   // [stage][stream]
+    sm.prefix = sm.meta + 2 * nstages;
   }
 
   // ---- this CTA's block range ------------------------------------------------
-  long long lo = 0, hi = 0, fixed_seq = -1;
+  long long lo = 0, hi = 0, mid = 0, fixed_seq = -1;
   if (balanced) {
     // Exclusive prefix sum of per-sequence block counts over the whole batch.
     const int nthreads = blockDim.x;
@@ -165,8 +174,12 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
     if (blockIdx.x == 0 && blockIdx.y == 0) {
       for (long long s = threadIdx.x; s <= batch; s += blockDim.x) a.prefix[s] = sm.prefix[s];
     }
-    lo = range_start(blockIdx.x, total, a.plan.ctas);
-    hi = range_start(blockIdx.x + 1, total, a.plan.ctas);
+    // Ranges of this CTA's virtual CTAs: [lo, mid) and [mid, hi) with two
+    // streams, [lo, hi) with one.
+    const long long v0 = (long long)blockIdx.x * streams;
+    lo = range_start(v0, total, a.plan.ctas);
+    hi = range_start(v0 + streams, total, a.plan.ctas);
+    mid = streams == 2 ? range_start(v0 + 1, total, a.plan.ctas) : hi;
   } else {
     fixed_seq = blockIdx.x / a.plan.splits;
     const int j = blockIdx.x - (int)fixed_seq * a.plan.splits;
@@ -177,6 +190,7 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
     }
     lo = (long long)j * a.plan.split_blocks;
     hi = lo + a.plan.split_blocks < nb ? lo + a.plan.split_blocks : nb;
+    mid = hi;
   }
   if (lo >= hi) return;  // uniform over the CTA
 
@@ -189,16 +203,19 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
   }
   __syncthreads();
 
-  const int kh0 = blockIdx.y * hpc;
-  const long long total = hi - lo;
+  const int kh0 = blockIdx.y * (streams == 2 ? 1 : hpc);
+  // Stream k covers [s_lo[k], s_lo[k] + s_len[k]); `total` ring steps in all.
+  const long long s_lo[2] = {lo, mid};
+  const long long s_len[2] = {mid - lo, hi - mid};
+  const long long total = streams == 2 ? (s_len[0] > s_len[1] ? s_len[0] : s_len[1]) : hi - lo;
 
-  // Block `idx` of this CTA's range (0-based): its table entry and valid-token
-  // count (0: not loaded).  Called by each lane for its own block.
-  auto resolve = [&](long long idx, int* id, int* ntok) {
+  // Block `idx` of stream k (0-based): its table entry and valid-token count
+  // (0: not loaded).  Called by each lane for its own block.
+  auto resolve = [&](int k, long long idx, int* id, int* ntok) {
     *id = 0;
     *ntok = 0;
-    if (idx >= total) return;
-    const long long f = lo + idx;
+    if (idx >= (streams == 2 ? s_len[k] : total)) return;
+    const long long f = s_lo[k] + idx;
     long long s, j;
     if (balanced) {
       s = find_seq(sm.prefix, batch, f);
@@ -220,9 +237,34 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
     *id = (int)raw;
     *ntok = nt;
   };
-  // Fill stage st with block id (ntok > 0) or mark it empty; one thread.
-  auto fill_stage = [&](int st, int id_i, int nt_i) {
-    sm.meta[st] = nt_i;
+  // Fill stage st with block id (ntok > 0) or mark it empty; one thread.  With
+  // two streams, block id1 of stream 1 goes to the second head slot.
+  auto fill_stage = [&](int st, int id_i, int nt_i, int id1, int nt1) {
+    sm.meta[2 * st] = nt_i;
+    sm.meta[2 * st + 1] = nt1;
+    if (streams == 2) {
+      const int one = kBS * kSubRowBytes;  // one 64-dim slice of one head slot
+      const unsigned bytes = (unsigned)(((nt_i > 0) + (nt1 > 0)) * 2 * kSubs * one);
+      if (bytes == 0) {
+        mbar_arrive(&sm.full[st]);
+        return;
+      }
+      unsigned char* kdst = sm.stages + (size_t)st * stage_bytes;
+      unsigned char* vdst = kdst + half_bytes;
+      mbar_arrive_expect_tx(&sm.full[st], bytes);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int idk = k ? id1 : id_i;
+        if ((k ? nt1 : nt_i) <= 0) continue;
+#pragma unroll
+        for (int sub = 0; sub < kSubs; ++sub) {
+          const int off = sub * sub_bytes + k * one;
+          tma_load_5d(kdst + off, &tmk, &sm.full[st], sub * kSub, kh0, 0, idk, a.layer);
+          tma_load_5d(vdst + off, &tmv, &sm.full[st], sub * kSub, kh0, 0, idk, a.layer);
+        }
+      }
+      return;
+    }
     if (nt_i > 0) {
       unsigned char* kdst = sm.stages + (size_t)st * stage_bytes;
       unsigned char* vdst = kdst + half_bytes;
@@ -247,13 +289,16 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
       prefetch_tensormap(&tmv);
     }
     for (long long base = 0; base < total; base += 32) {
-      // Each lane resolves one block: its table entry and valid-token count.
-      int id, ntok;
-      resolve(base + lane, &id, &ntok);
+      // Each lane resolves one block per stream: table entry and valid tokens.
+      int id, ntok, id1 = 0, ntok1 = 0;
+      resolve(0, base + lane, &id, &ntok);
+      if (streams == 2) resolve(1, base + lane, &id1, &ntok1);
       const int cnt = total - base < 32 ? (int)(total - base) : 32;
       for (int i = 0; i < cnt; ++i) {
         const int id_i = __shfl_sync(0xffffffffu, id, i);
         const int nt_i = __shfl_sync(0xffffffffu, ntok, i);
+        const int id1_i = __shfl_sync(0xffffffffu, id1, i);
+        const int nt1_i = __shfl_sync(0xffffffffu, ntok1, i);
         if (lane == 0) {
           const long long it = base + i;
           const int st = (int)(it % nstages);
@@ -261,7 +306,7 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
           if (round > 0 && !mbar_wait(&sm.empty[st], (unsigned)((round - 1) & 1))) {
             record_error(a.err, kErrWaitTimeout | kErrWaitSlot);
           }
-          fill_stage(st, id_i, nt_i);
+          fill_stage(st, id_i, nt_i, id1_i, nt1_i);
         }
         __syncwarp();
       }
@@ -278,8 +323,9 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
     return;
   }
 
-  // ---- consumer warps: one KV head each ----------------------------------------
-  const int kh = kh0 + warp;
+  // ---- consumer warps: one KV head each, or one stream each ----------------------
+  const int kh = streams == 2 ? kh0 : kh0 + warp;
+  const int my = streams == 2 ? warp : 0;     // this warp's stream (meta column)
   const int gid = lane >> 2;
   const int tid4 = lane & 3;
   const int mi = lane >> 3;  // which 8x8 matrix this lane addresses in ldmatrix.x4
@@ -298,7 +344,7 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
     while (issued < limit) {
       if (issued >= cache_base + 32) {
         cache_base = issued;
-        resolve(cache_base + lane, &c_id, &c_nt);
+        resolve(0, cache_base + lane, &c_id, &c_nt);
       }
       const int k = (int)(issued - cache_base);
       const int id_i = __shfl_sync(0xffffffffu, c_id, k);
@@ -306,7 +352,7 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
       // This stage's previous block was consumed by this warp: order its reads
       // (and any zeroing) before the copy that overwrites it.
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      if (lane == 0) fill_stage((int)(issued % nstages), id_i, nt_i);
+      if (lane == 0) fill_stage((int)(issued % nstages), id_i, nt_i, 0, 0);
       __syncwarp();
       ++issued;
     }
@@ -320,13 +366,14 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
   }
 
   long long it = 0;
-  long long cur = lo;
-  while (cur < hi) {
+  long long cur = s_lo[my];
+  const long long my_hi = streams == 2 ? s_lo[my] + s_len[my] : hi;
+  while (cur < my_hi) {
     long long s, seg_begin, seg_end;
     if (balanced) {
       s = find_seq(sm.prefix, batch, cur);
       seg_begin = sm.prefix[s];
-      seg_end = sm.prefix[s + 1] < hi ? sm.prefix[s + 1] : hi;
+      seg_end = sm.prefix[s + 1] < my_hi ? sm.prefix[s + 1] : my_hi;
     } else {
       s = fixed_seq;
       seg_begin = 0;
@@ -351,7 +398,7 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
       if (!mbar_wait(&sm.full[st], (unsigned)((it / nstages) & 1))) {
         record_error(a.err, kErrWaitTimeout | kErrWaitData);
       }
-      const int ntok = sm.meta[st];
+      const int ntok = sm.meta[2 * st + my];
       if (ntok > 0) {
         unsigned char* kst = sm.stages + (size_t)st * stage_bytes;
         unsigned char* vst = kst + half_bytes;
@@ -459,7 +506,8 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
     const long long slot =
-        balanced ? s + blockIdx.x : s * a.plan.splits + (blockIdx.x - s * a.plan.splits);
+        balanced ? s + (long long)blockIdx.x * streams + my
+                 : s * a.plan.splits + (blockIdx.x - s * a.plan.splits);
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int r = gid + 8 * half;
@@ -481,6 +529,15 @@ __global__ void __launch_bounds__(SP ? 32 : (kMaxBoxHeads + 1) * 32, SP ? 12 : 1
     }
     cur = seg_end;
   }
+  // The shorter stream releases the ring steps it has no block for.
+  for (; streams == 2 && it < total; ++it) {
+    const int st = (int)(it % nstages);
+    if (!mbar_wait(&sm.full[st], (unsigned)((it / nstages) & 1))) {
+      record_error(a.err, kErrWaitTimeout | kErrWaitData);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[st]);
+  }
   if (SP) griddep_launch_dependents();
 }
 
@@ -499,14 +556,15 @@ int choose_heads_per_cta(int kv_heads, int head_dim) {
 }
 
 template <int D, int Q_DT, int KV_DT>
-const void* kernel_ptr(bool sp) {
-  return sp ? reinterpret_cast<const void*>(&decode_tma_kernel<D, Q_DT, KV_DT, true>)
-            : reinterpret_cast<const void*>(&decode_tma_kernel<D, Q_DT, KV_DT, false>);
+const void* kernel_ptr(bool sp, bool st) {
+  if (sp) return reinterpret_cast<const void*>(&decode_tma_kernel<D, Q_DT, KV_DT, true, false>);
+  if (st) return reinterpret_cast<const void*>(&decode_tma_kernel<D, Q_DT, KV_DT, false, true>);
+  return reinterpret_cast<const void*>(&decode_tma_kernel<D, Q_DT, KV_DT, false, false>);
 }
 
-const void* select_kernel(const AttnArgs& a, bool sp = false) {
+const void* select_kernel(const AttnArgs& a, bool sp = false, bool st = false) {
 #define LLMOPT_DECODE_CASE(DV, QT, KT) \
-  if (a.head_dim == DV && a.q_dtype == QT && a.kv_dtype == KT) return kernel_ptr<DV, QT, KT>(sp);
+  if (a.head_dim == DV && a.q_dtype == QT && a.kv_dtype == KT) return kernel_ptr<DV, QT, KT>(sp, st);
 #define LLMOPT_DECODE_Q(DV, KT)     \
   LLMOPT_DECODE_CASE(DV, kF32, KT)  \
   LLMOPT_DECODE_CASE(DV, kF16, KT)  \
@@ -524,7 +582,7 @@ const void* select_kernel(const AttnArgs& a, bool sp = false) {
 
 size_t smem_bytes_for(int hpc, int head_dim, int stages, long long prefix_entries) {
   const size_t stage = 2ull * hpc * kBS * head_dim * 2;
-  return 1024 + stage * stages + stages * (8 + 8 + 4) + (size_t)prefix_entries * 4 + 16;
+  return 1024 + stage * stages + stages * (8 + 8 + 2 * 4) + (size_t)prefix_entries * 4 + 16;
 }
 
 }  // namespace
@@ -556,22 +614,31 @@ bool decode_tma_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch)
       2ull * hpc_env * kBS * a.head_dim * 2 <= 64 * 1024) {
     hpc = hpc_env;
   }
-  // A single-head CTA issues its own copies (one warp, no producer warp).
+  // One KV head (a rank's shard of 8 heads over 8 GPUs): two streams of the
+  // balanced plan per CTA in the two-head layout, or (LLMOPT_B200_DECODE_SP=1,
+  // and for fixed plans) self-issuing one-warp CTAs.
   bool sp = hpc == 1;
   const int sp_env = env_int("LLMOPT_B200_DECODE_SP", -1);
   if (sp_env == 0 || sp_env == 1) sp = sp_env == 1;
   if (hpc != 1 || a.head_dim > 128) sp = false;   // head_dim 256 would spill at its bound
-  const void* fn = select_kernel(a, sp);
+  int streams = 1;
+  if (hpc == 1 && a.plan.mode == kModeBalanced && sp_env != 1 &&
+      2ull * 2 * kBS * a.head_dim * 2 <= 64 * 1024) {
+    streams = 2;
+    sp = false;
+  }
+  const int box_heads = hpc * streams;          // head slots of the ring layout
+  const void* fn = select_kernel(a, sp, streams == 2);
   if (fn == nullptr) return false;
   const long long prefix_entries = a.plan.mode == kModeBalanced ? a.batch + 1 : 0;
   // Double buffering per CTA; parallelism comes from several CTAs per SM.
   int stages = env_int("LLMOPT_B200_DECODE_STAGES", 2);
   if (stages < 2) stages = 2;
   if (stages > 16) stages = 16;
-  size_t smem = smem_bytes_for(hpc, a.head_dim, stages, prefix_entries);
+  size_t smem = smem_bytes_for(box_heads, a.head_dim, stages, prefix_entries);
   while (smem > 227 * 1024 && stages > 2) {
     --stages;
-    smem = smem_bytes_for(hpc, a.head_dim, stages, prefix_entries);
+    smem = smem_bytes_for(box_heads, a.head_dim, stages, prefix_entries);
   }
   if (smem > 227 * 1024) return false;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
@@ -580,12 +647,13 @@ bool decode_tma_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch)
     return false;
   }
   int occ = 0;
-  const int threads = sp ? 32 : (hpc + 1) * 32;
+  const int threads = sp ? 32 : (box_heads + 1) * 32;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, threads, smem) != cudaSuccess ||
       occ < 1) {
     return false;
   }
   launch->heads_per_cta = hpc;
+  launch->streams = streams;
   launch->self_issue = sp ? 1 : 0;
   launch->stages = stages;
   launch->ctas_per_sm = occ;
@@ -597,16 +665,18 @@ bool decode_tma_configure(const AttnArgs& a, int sm_count, DecodeLaunch* launch)
 cudaError_t decode_tma_launch(const AttnArgs& a, const DecodeLaunch& launch,
                               const CUtensorMap& tmk, const CUtensorMap& tmv,
                               cudaStream_t stream) {
-  const void* fn = select_kernel(a, launch.self_issue != 0);
+  const void* fn = select_kernel(a, launch.self_issue != 0, launch.streams == 2);
   if (fn == nullptr) return cudaErrorInvalidValue;
   const int head_groups = a.kv_heads / launch.heads_per_cta;
-  const long long gx =
-      a.plan.mode == kModeBalanced ? a.plan.ctas : a.batch * (long long)a.plan.splits;
+  const int streams = launch.streams == 2 ? 2 : 1;
+  if (a.plan.mode == kModeBalanced && a.plan.ctas % streams != 0) return cudaErrorInvalidValue;
+  const long long gx = a.plan.mode == kModeBalanced ? a.plan.ctas / streams
+                                                    : a.batch * (long long)a.plan.splits;
   if (gx <= 0) return cudaSuccess;
   if (gx > 0x7fffffffLL || head_groups > 65535) return cudaErrorInvalidConfiguration;
   dim3 grid((unsigned)gx, (unsigned)head_groups);
-  dim3 block(launch.self_issue ? 32 : (launch.heads_per_cta + 1) * 32);
-  int hpc = launch.heads_per_cta;
+  int hpc = launch.heads_per_cta * streams;    // head slots of the ring layout
+  dim3 block(launch.self_issue ? 32 : (hpc + 1) * 32);
   int stages = launch.stages;
   void* args[] = {const_cast<CUtensorMap*>(&tmk), const_cast<CUtensorMap*>(&tmv),
                   const_cast<AttnArgs*>(&a), &hpc, &stages};

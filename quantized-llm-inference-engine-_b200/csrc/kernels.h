@@ -58,6 +58,7 @@ struct AttnArgs {
 struct DecodeLaunch {
   int heads_per_cta;  // KV heads one CTA stages per block (box height)
   int self_issue;     // 1: one-warp CTAs that issue their own copies (heads_per_cta == 1)
+  int streams;        // 2: two balanced ranges of one head per CTA (plan.ctas counts ranges)
   int stages;         // shared-memory ring depth
   int ctas_per_sm;
   size_t smem_bytes;
