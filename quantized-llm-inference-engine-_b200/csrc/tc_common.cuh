@@ -172,6 +172,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// One lane of the (converged) warp; the same lane every time it is called with
+// all 32 lanes active.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // ---- 2-SM pairs (cta_group::2): a cluster of two CTAs shares each MMA ----------
 // Every tcgen05 instruction of a kernel uses one cta_group, so a pair kernel
 // allocates, issues and commits with these.  Allocation and release are
