@@ -61,6 +61,17 @@ def test_prefill_chunk_lengths(cuda, q_len):
     check(cuda, case)
 
 
+def test_prefill_large_batch_index_order(cuda):
+    """More than 256 sequences: the kernels keep the index order instead of ranking
+    sequences longest first; ragged short contexts, some shorter than the chunk."""
+    rng = np.random.default_rng(64)
+    q_len = 20
+    ctx = rng.integers(1, 140, size=300)
+    case = build_paged_case(64, batch=300, heads=8, kv_heads=2, head_dim=128, block_size=16,
+                            ctx=ctx, kv_kind="bf16", q_kind="bf16", q_len=q_len)
+    check(cuda, case)
+
+
 def test_prefill_fp16_softcap_holes_and_short_context(cuda):
     case = build_paged_case(60, batch=4, heads=16, kv_heads=4, head_dim=128, block_size=16,
                             ctx=[3, 90, 260, 513], kv_kind="f16", q_kind="f16", q_len=48,
