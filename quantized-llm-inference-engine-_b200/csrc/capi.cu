@@ -189,6 +189,26 @@ bool kv_tensor_map(const void* base, int dtype, int layers, int num_blocks, int 
   return true;
 }
 
+}  // namespace
+
+bool llmopt::tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base,
+                           uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                           uint32_t box_inner, uint32_t box_outer) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  std::memset(out, 0, sizeof(*out));
+  return encode(out, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace {
+
 // Per-call descriptor of the query for the prefill kernel: (head_dim, q_len,
 // num_heads, batch), box (64, 128 / group tokens, group heads, 1).
 bool query_tensor_map(const AttnArgs& a, CUtensorMap* out, std::string* why) {
@@ -789,6 +809,11 @@ void plan_quant_splits(QuantLinearArgs* a, int sms) {
   a->splits = (int)((tiles + per - 1) / per);
 }
 
+// fp32 workspace bytes of a planned call.
+size_t quant_workspace_bytes(const QuantLinearArgs& a) {
+  return a.splits > 1 ? (size_t)a.splits * (size_t)a.m * (size_t)a.n * sizeof(float) : 0;
+}
+
 }  // namespace
 
 int llmopt_quant_linear_workspace_size(int device, int64_t m, int64_t n, int64_t k,
@@ -811,7 +836,7 @@ int llmopt_quant_linear_workspace_size(int device, int64_t m, int64_t n, int64_t
   a.m = m;
   a.ldx = k;
   plan_quant_splits(&a, sm_count_of(device));
-  if (a.splits > 1) *bytes = (size_t)a.splits * (size_t)m * (size_t)n * sizeof(float);
+  *bytes = quant_workspace_bytes(a);
   return ok();
 }
 
@@ -839,8 +864,8 @@ int llmopt_quant_linear(const void* x, int32_t x_dtype, int64_t m, int64_t ldx,
   a.out = out;
   a.ldo = ldo;
   plan_quant_splits(&a, sm_count_of(current_device()));
-  if (a.splits > 1) {
-    const size_t need = (size_t)a.splits * (size_t)m * (size_t)n * sizeof(float);
+  const size_t need = quant_workspace_bytes(a);
+  if (need > 0) {
     if (workspace == nullptr || workspace_bytes < need) {
       return fail(LLMOPT_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed", workspace_bytes,
                   need);

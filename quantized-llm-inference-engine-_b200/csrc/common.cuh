@@ -237,6 +237,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   return ok != 0;
 }
 
+// The same, suspending the thread until the phase completes or about `ns`
+// nanoseconds pass (a suspended warp issues nothing).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, unsigned parity, unsigned ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity; false after the limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
   if (mbar_try_wait(bar, parity)) return true;

@@ -234,6 +234,13 @@ cudaError_t quant_linear_launch(const QuantLinearArgs& a, cudaStream_t stream);
 // LLMOPT_DEVERR_* bits recorded by the quantized-linear kernels' bounded waits
 // on the current device (read, and cleared when `clear`).
 cudaError_t quant_linear_device_errors(unsigned* bits, bool clear);
+// 2-D tensor map for TMA tile loads: `inner` elements per row (contiguous),
+// `outer` rows `row_bytes` apart, boxes of box_inner x box_outer, 128-byte
+// swizzle, zero fill outside the tensor.  False when the driver's encoder is
+// unavailable or rejects the arguments.
+bool tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base,
+                   uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+                   uint32_t box_outer);
 cudaError_t dequantize_launch(const QuantLinearArgs& a, void* out, int out_dtype,
                               cudaStream_t stream);
 

@@ -606,236 +606,452 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_acc_kernel(const QuantLinear
   }
 }
 
-// ---- 2- and 4-bit codes on the 5th-generation tensor cores (opt-in) ------------
+// ---- 2- and 4-bit codes on the 5th-generation tensor cores ---------------------
 //
-// For token batches the weight is dequantized once per CTA into shared memory
-// and multiplied by tcgen05.mma.  A CTA owns 128 output features (TMEM lanes,
-// MMA M) and 64 tokens (MMA N) and walks its k range in 64-column slices:
-// * all 128 threads copy a slice's codes (128 rows x 32 bytes), token rows
-//   (64 x 128 bytes, in the 128-byte-swizzled K-major layout the MMA reads)
-//   and group constants with cp.async into a 4-stage ring;
-// * thread r dequantizes row r of the slice as the reference does, (q - z) * s
-//   in float32 rounded once to the compute dtype, into a swizzled K-major A
-//   tile (two A buffers), so the weights are the reference's bit for bit;
-// * one thread issues the slice's four MMAs (K = 16 each) into the fp32
-//   accumulator in tensor memory and commits them to an mbarrier.
-// Slice t waits only for the MMAs of slice t - 2, which free its A buffer and
-// the copy stage it refills, so one slice's dequantization overlaps the MMAs
-// of the one before.  The epilogue reads the accumulator with tcgen05.ld
-// (thread r = feature r, 32 tokens per load).  Every wait is bounded; a wait
-// that gives up sets g_wq_err and the CTA skips the rest of its MMAs.
+// A CTA owns 128 output features (the 128 lanes of tensor memory, MMA M) and bn
+// tokens (MMA N: the batch rounded up to 16, at most 64; larger batches take
+// several token blocks) over a k range of whole 64-column slices.  Each weight
+// is dequantized once per CTA and token block, straight into tensor memory as
+// the MMA's A operand; the token rows are the B operand in shared memory.
+// Warp roles:
+// * warps 0-11 dequantize in three sets of four: set h = w / 4 takes the
+//   slices s with s % 3 == h, warp w the 32 rows of lane quarter w % 4.
+//   Thread r turns its row's 64 codes of a slice into the reference's weights
+//   - (q - z) * s in float32, rounded once to the compute dtype - and stores
+//   the 32 pairs into a 32-column A slot in tensor memory (tcgen05.st).  Each
+//   set owns two slots, so a slot's barriers are only ever waited on by the
+//   warps that saw all of its earlier phases;
+// * warp 12 loads the codes: one TMA box of 128 rows x 128 bytes (256 columns,
+//   128-byte swizzle) per stage of a 4-stage ring, plus the stage's group
+//   scales (and zero points) by cp.async completing on the same mbarrier;
+// * warp 13 loads the token rows: one TMA box of bn rows x 64 columns per
+//   slice (K-major, 128-byte swizzle: the layout the MMA reads);
+// * warp 14 issues, from one elected thread, the four tcgen05.mma (K = 16, A
+//   from tensor memory) of each slice into the fp32 accumulator and commits
+//   them to the slot barriers that free the A slot and the token slot.
+// The dequantize warps then read the accumulator (tcgen05.ld, thread r =
+// feature r) and write the output, or the split's fp32 partial.
+// (Token tiles of 128 and 256 ran 2.2x and 4x faster at those batches but
+// returned wrong sums for the first lane quarter of some CTAs, 1 to 10 of
+// 112 row blocks per call, when the MMAs outran the dequantization; the tile
+// stays at 64 tokens, where long stress runs never showed it.)
+//
+// Dequantization without conversions: OR-ing nibble j of a code word (bits
+// 4j..4j+3) into the float 2^23 gives 2^23 + q * 16^j exactly; one packed FMA
+// by (16^-j, -(2^(23-4j) + c)) leaves q - c exactly (c = 2^(bits-1) for
+// symmetric codes, 0 before an asymmetric zero point is subtracted), and one
+// packed multiply by the scale rounds the product once, as the reference does.
+//
+// Every wait is bounded.  A wait that gives up sets g_wq_err and the CTA's
+// abort flag; the other roles then stop at their next wait, the loaders wait
+// (bounded) for the copies they issued, the MMA issuer's final commit drains
+// the MMAs before tensor memory is read or freed, and the CTA writes NaN.
 namespace tc05 {
-constexpr int kBM = 128;                    // features per CTA
-constexpr int kBN = 64;                     // tokens per CTA
-constexpr int kBK = 64;                     // k per slice (one 128-byte row of 16-bit values)
-constexpr int kThreads = 128;
-constexpr int kStages = 4;
-constexpr int kGroups = 2;                  // groups per slice at most (group 32)
-constexpr int kATile = kBM * 128;
-constexpr int kXTile = kBN * 128;
-constexpr int kCodes = kBM * 32;
-constexpr int kConsts = kBM * kGroups * 4;
-constexpr int kOffA = 0;                    // offsets from the 1024-byte aligned base
-constexpr int kOffX = kOffA + 2 * kATile;
-constexpr int kOffC = kOffX + kStages * kXTile;
-constexpr int kOffS = kOffC + kStages * kCodes;
-constexpr int kOffZ = kOffS + kStages * kConsts;
-constexpr int kOffBar = kOffZ + kStages * kConsts;
-constexpr int kSmem = kOffBar + 64 + 1024;  // barriers, TMEM address, alignment slack
-static_assert(kBN % 32 == 0 && kBN >= 32 && kBN <= 256, "TMEM columns / MMA N");
-static_assert(kBN * 8 % kThreads == 0, "token-row copy slots");
+constexpr int kBM = 128;                          // features per CTA
+constexpr int kSliceK = 64;                       // k per slice: one A slot, one commit
+constexpr int kSliceCols = kSliceK / 2;           // tensor-memory columns of an A slot
+constexpr int kXBoxes = kSliceK / 64;             // 64-column token boxes per slice
+constexpr int kWords = kSliceK / 8;               // 32-bit code words of a row per slice
+constexpr int kQuarters = kSliceK / 32;           // group constants per row per slice
+constexpr int kStageK = 256;                      // k per codes stage (128 bytes of a row)
+constexpr int kSlicesPerStage = kStageK / kSliceK;
+constexpr int kCodeStages = 4;
+constexpr int kSlotsPerSet = 2;                   // A slots of a set, reused only by it
+constexpr int kMaxXSlots = 8;
+constexpr int kDqWarps = 12;
+constexpr int kSets = kDqWarps / 4;               // slices in flight in the dequantize warps
+constexpr int kCodesWarp = kDqWarps;
+constexpr int kTokensWarp = kDqWarps + 1;
+constexpr int kMmaWarp = kDqWarps + 2;
+constexpr int kThreads = (kDqWarps + 3) * 32;
+constexpr int kMaxBN = 64;
+constexpr int kCodeBytes = kBM * kStageK / 2;     // 16 KB per stage
+constexpr int kConstBytes = kSlicesPerStage * kQuarters * kBM * 4;   // [slice][32 cols][row]
+constexpr int kXBytes = 128 * 1024;               // token-slice ring
+constexpr int kOffCodes = 0;                      // offsets from the 1024-byte aligned base
+constexpr int kOffX = kOffCodes + kCodeStages * kCodeBytes;
+constexpr int kOffS = kOffX + kXBytes;
+constexpr int kOffZ = kOffS + kCodeStages * kConstBytes;
+constexpr int kOffBar = kOffZ + kCodeStages * kConstBytes;
+constexpr int kBarBytes = 512;
+constexpr int kSmem = kOffBar + kBarBytes + 1024; // + alignment slack
+constexpr uint32_t kTmemCols = 512;               // A ring [0, 256), accumulator [256, 256 + bn)
+constexpr int kASlots = kSets * kSlotsPerSet;     // A ring in tensor-memory columns [0, 256)
+constexpr int kAccCol = 256;
+static_assert(kAccCol + kMaxBN <= (int)kTmemCols, "tensor-memory columns");
+static_assert(kSmem <= 227 * 1024, "shared memory");
+static_assert(kOffX % 1024 == 0 && kOffS % 1024 == 0, "TMA destinations");
+static_assert(kDqWarps % 4 == 0 && kSets <= kSlicesPerStage, "dequantize warp sets");
+static_assert(kASlots * kSliceCols <= kAccCol, "A ring");
+
+struct Bars {
+  uint64_t codes_full[kCodeStages];   // TMA bytes + the 32 cp.async lanes + 1
+  uint64_t codes_empty[kCodeStages];  // the dequantize warps
+  uint64_t x_full[kMaxXSlots];        // TMA bytes + 1
+  uint64_t x_empty[kMaxXSlots];       // MMA commit
+  uint64_t a_full[kASlots];           // the 4 dequantize warps of the slice's set
+  uint64_t a_empty[kASlots];          // MMA commit
+  uint64_t acc_full;                  // MMA commit after the last slice
+  uint32_t tmem;
+  uint32_t abort;
+};
+static_assert(sizeof(Bars) <= kBarBytes, "barrier block");
+
+// Tokens per CTA and token-slice ring depth (host and device agree on both).
+// A slot of slice s and how many times that slot was used before it: a set
+// owns its slots, so the warps that wait on a slot's barriers are the ones that
+// saw every one of its earlier phases.
+__host__ __device__ constexpr int a_slot(long long s) {
+  return (int)(s % kSets) * kSlotsPerSet + (int)((s / kSets) % kSlotsPerSet);
+}
+__host__ __device__ constexpr long long a_use(long long s) { return s / kSets / kSlotsPerSet; }
+__host__ __device__ constexpr int bn_of(long long m) {
+  return m >= kMaxBN ? kMaxBN : (int)((m + 15) & ~15LL);
+}
+__host__ __device__ constexpr int x_slots(int bn) {
+  return kXBytes / (bn * 128 * kXBoxes) < kMaxXSlots ? kXBytes / (bn * 128 * kXBoxes)
+                                                      : kMaxXSlots;
+}
 }  // namespace tc05
 
 __device__ unsigned g_wq_err;               // LLMOPT_DEVERR_* bits of the tcgen05 path
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+__device__ __forceinline__ void fmul2(float& x0, float& x1, float a0, float a1, uint64_t bb) {
+  asm("{\n\t.reg .b64 ra, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mul.rn.f32x2 rd, ra, %4;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "l"(bb));
+}
+__device__ __forceinline__ void fadd2(float& x0, float& x1, uint64_t bb) {
+  asm("{\n\t.reg .b64 ra;\n\t"
+      "mov.b64 ra, {%0, %1};\n\t"
+      "add.rn.f32x2 ra, ra, %2;\n\t"
+      "mov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(x0), "+f"(x1)
+      : "l"(bb));
 }
 
-template <int DT>
-__global__ void __launch_bounds__(tc05::kThreads) wq_gemm_tc05_kernel(const QuantLinearArgs a) {
+// Constants of one row and group: (16^-j, -(2^(23-4j) + c)) for nibbles j = 0, 1
+// and j = 2, 3 of a half-word, the scale pair and the negated zero-point pair.
+struct DqConst {
+  uint64_t m01, c01, m23, c23;
+};
+__device__ __forceinline__ DqConst dq_const(float c) {
+  return {pack2f(1.f, 0.0625f), pack2f(-(8388608.f + c), -(524288.f + c)),
+          pack2f(0.00390625f, 0.000244140625f), pack2f(-(32768.f + c), -(2048.f + c))};
+}
+
+// Eight codes (code j in bits 4j..4j+3 of w) -> four 16-bit pairs of weights,
+// the lower half holding the even code.
+template <int DT, bool SYM>
+__device__ __forceinline__ void dequant8(uint32_t w, const DqConst& k, uint64_t ss, uint64_t nz,
+                                         uint32_t* out) {
+  constexpr uint32_t e = 0x4B000000u;
+  const uint32_t u = w >> 16;
+  float d[8];
+  ffma2(d[0], d[1], __uint_as_float(e | (w & 0xFu)), __uint_as_float(e | (w & 0xF0u)), k.m01,
+        k.c01);
+  ffma2(d[2], d[3], __uint_as_float(e | (w & 0xF00u)), __uint_as_float(e | (w & 0xF000u)),
+        k.m23, k.c23);
+  ffma2(d[4], d[5], __uint_as_float(e | (u & 0xFu)), __uint_as_float(e | (u & 0xF0u)), k.m01,
+        k.c01);
+  ffma2(d[6], d[7], __uint_as_float(e | (u & 0xF00u)), __uint_as_float(e | (u & 0xF000u)),
+        k.m23, k.c23);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (!SYM) fadd2(d[2 * i], d[2 * i + 1], nz);
+    fmul2(d[2 * i], d[2 * i + 1], d[2 * i], d[2 * i + 1], ss);
+    out[i] = pack2<DT>(d[2 * i], d[2 * i + 1]);
+  }
+}
+
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+template <int DT, bool SYM>
+__global__ void __launch_bounds__(tc05::kThreads, 1)
+    wq_gemm_tc05_kernel(const QuantLinearArgs a, const __grid_constant__ CUtensorMap tm_codes,
+                        const __grid_constant__ CUtensorMap tm_x) {
+  using namespace tc05;
   griddep_wait();
   griddep_launch_dependents();
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* mma_done = reinterpret_cast<uint64_t*>(base + tc05::kOffBar);   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + tc05::kOffBar + 16);
-  uint32_t* abort_flag = reinterpret_cast<uint32_t*>(base + tc05::kOffBar + 20);
+  Bars* bars = reinterpret_cast<Bars*>(base + kOffBar);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
 
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const long long rbase = (long long)blockIdx.x * tc05::kBM;
-  const long long m0 = (long long)blockIdx.z * tc05::kBN;
+  const int bn = bn_of(a.m);
+  const int xs = x_slots(bn);
+  const long long rbase = (long long)blockIdx.x * kBM;
+  const long long m0 = (long long)blockIdx.z * bn;
   const long long kb = (long long)blockIdx.y * a.k_per_split;
   const long long ke = kb + a.k_per_split < a.k ? kb + a.k_per_split : a.k;
-  const int nslices = (int)((ke - kb) / tc05::kBK);
-  const long long mrem = a.m - m0;
+  const int nslices = (int)((ke - kb) / kSliceK);
+  const int nstages = (nslices + kSlicesPerStage - 1) / kSlicesPerStage;
   const long long groups = a.k / a.group;
-  const long long row_bytes = a.k / 2;
-  const int gps = a.group >= tc05::kBK ? 1 : tc05::kBK / a.group;   // groups per slice: 1 or 2
-  const int sps = a.group >= tc05::kBK ? a.group / tc05::kBK : 1;   // slices per group
-  const int slice0 = (int)(kb / tc05::kBK);
+  const uint32_t ug = (uint32_t)a.group;                         // k < 2^31 (host check)
 
-  if (tid == 0) {
-    mbar_init(&mma_done[0], 1);
-    mbar_init(&mma_done[1], 1);
-    *abort_flag = 0u;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kCodeStages; ++i) {
+      mbar_init(&bars->codes_full[i], 1 + 32);
+      mbar_init(&bars->codes_empty[i], kDqWarps);
+    }
+    for (int i = 0; i < kMaxXSlots; ++i) {
+      mbar_init(&bars->x_full[i], 1);
+      mbar_init(&bars->x_empty[i], 1);
+    }
+    for (int i = 0; i < kASlots; ++i) {
+      mbar_init(&bars->a_full[i], 4);
+      mbar_init(&bars->a_empty[i], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    bars->abort = 0u;
     mbar_init_fence();
   }
   if (warp == 0) {
-    tc::tmem_alloc(tmem_slot, tc05::kBN);
+    tc::tmem_alloc(&bars->tmem, kTmemCols);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = bars->tmem;
 
-  auto wait_mma = [&](int slice) {           // bounded; the first give-up aborts the CTA
-    if (*reinterpret_cast<volatile uint32_t*>(abort_flag) != 0u) return;
-    if (!mbar_wait(&mma_done[slice & 1], (unsigned)((slice >> 1) & 1))) {
-      atomicOr(&g_wq_err, kErrWaitTimeout | kErrWaitData);
-      *reinterpret_cast<volatile uint32_t*>(abort_flag) = 1u;
-    }
-  };
-
-  // Copy slots, fixed per thread.  Codes: row tid, its two 16-byte pieces,
-  // piece p stored at p ^ ((row >> 2) & 1) so a quarter warp's reads hit eight
-  // bank groups.  Token rows: rows tid/8 + 16 q, chunk tid % 8, stored at
-  // chunk position chunk ^ (row & 7) (the 128-byte swizzle).
-  const unsigned char* csrc = a.qweight + (rbase + tid) * row_bytes + kb / 2;
-  const int cdst0 = tid * 32 + 16 * ((tid >> 2) & 1);
-  const int cdst1 = tid * 32 + 16 * (1 ^ ((tid >> 2) & 1));
-  const int xr0 = tid >> 3;
-  const int xc = tid & 7;
-  const unsigned short* xsrc =
-      static_cast<const unsigned short*>(a.x) + (m0 + xr0) * a.ldx + kb + 8 * xc;
-  const int xdst = xr0 * 128 + 16 * (xc ^ (xr0 & 7));
-  const float* ssrc = a.scales + (rbase + tid) * groups;
-  const float* zsrc = a.zeros != nullptr ? a.zeros + (rbase + tid) * groups : nullptr;
-  // first group of slice t: (slice0 + t) * gps, or (slice0 + t) / sps; issue()
-  // runs for t = 0, 1, 2, ... in order and keeps a cursor
-  long long g_cur = gps > 1 ? (long long)slice0 * gps : slice0 / sps;
-  int g_in = gps > 1 ? 0 : slice0 % sps;
-
-  auto issue = [&](int t) {
-    const int st = t % tc05::kStages;
-    unsigned char* cst = base + tc05::kOffC + st * tc05::kCodes;
-    const unsigned char* src = csrc + (long long)t * (tc05::kBK / 2);
-    cp_async16(cst + cdst0, src, 16);
-    cp_async16(cst + cdst1, src + 16, 16);
-    unsigned char* xst = base + tc05::kOffX + st * tc05::kXTile;
-#pragma unroll
-    for (int q = 0; q < tc05::kBN * 8 / tc05::kThreads; ++q) {
-      const bool ok = xr0 + 16 * q < mrem;
-      // a row past the last token copies nothing (source size 0) from a valid address
-      cp_async16(xst + xdst + q * 16 * 128,
-                 ok ? xsrc + 16 * q * a.ldx + (long long)t * tc05::kBK
-                    : static_cast<const unsigned short*>(a.x),
-                 ok ? 16 : 0);
-    }
-    float* sst = reinterpret_cast<float*>(base + tc05::kOffS + st * tc05::kConsts) + tid * tc05::kGroups;
-    float* zst = reinterpret_cast<float*>(base + tc05::kOffZ + st * tc05::kConsts) + tid * tc05::kGroups;
-    for (int g = 0; g < gps; ++g) {
-      cp_async4(sst + g, ssrc + g_cur + g);
-      if (!a.symmetric) cp_async4(zst + g, zsrc + g_cur + g);
-    }
-    if (gps > 1) {
-      g_cur += gps;
-    } else if (++g_in == sps) {
-      g_in = 0;
-      ++g_cur;
-    }
-  };
-
-#pragma unroll
-  for (int t = 0; t < tc05::kStages - 2; ++t) {
-    if (t < nslices) issue(t);
-    cp_async_commit();
-  }
-  const float zsym = (float)(1 << (a.bits - 1));
-  const uint32_t idesc = tc::instr_desc_f16(DT == kBF16, tc05::kBM, tc05::kBN, false, false);
-  int last_committed = -1;                   // thread 0: the last slice whose MMAs it issued
-
-  for (int t = 0; t < nslices; ++t) {
-    cp_async_wait<tc05::kStages - 3>();
-    fence_proxy_async_smem();                // the copies, for the tensor core's reads
-    __syncthreads();                         // slice t landed for every thread
-    if (t >= 2) wait_mma(t - 2);             // frees A[t & 1] and stage (t - 2) % tc05::kStages
-    if (t + tc05::kStages - 2 < nslices) issue(t + tc05::kStages - 2);
-    cp_async_commit();
-    const int st = t % tc05::kStages;
-    const unsigned char* cst = base + tc05::kOffC + st * tc05::kCodes;
-    const uint4 c0 = *reinterpret_cast<const uint4*>(cst + cdst0);
-    const uint4 c1 = *reinterpret_cast<const uint4*>(cst + cdst1);
-    const float* sst = reinterpret_cast<const float*>(base + tc05::kOffS + st * tc05::kConsts) + tid * tc05::kGroups;
-    const float* zst = reinterpret_cast<const float*>(base + tc05::kOffZ + st * tc05::kConsts) + tid * tc05::kGroups;
-    unsigned char* arow = base + tc05::kOffA + (t & 1) * tc05::kATile + tid * 128;
-    const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {            // 16-byte chunk c of the row: codes 8c .. 8c + 7
-      const int g = gps > 1 ? (c >> 2) : 0;  // group 32: chunks 0-3 and 4-7
-      const float sc = sst[g];
-      const float zoff = 8388608.f + (a.symmetric ? zsym : zst[g]);
-      uint32_t pk[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {          // codes 2j (low nibble) and 2j + 1
-        const float f0 = __int_as_float(0x4B000000u | ((words[c] >> (8 * j)) & 0xFu)) - zoff;
-        const float f1 = __int_as_float(0x4B000000u | ((words[c] >> (8 * j + 4)) & 0xFu)) - zoff;
-        pk[j] = as_u32(Pair<DT>::pack(__fmul_rn(f0, sc), __fmul_rn(f1, sc)));
+  volatile uint32_t* abort_flag = &bars->abort;
+  // Warp-uniform bounded wait: false once any wait of the CTA has given up.
+  auto wait = [&](uint64_t* bar, unsigned parity, unsigned what) -> bool {
+    bool ok = mbar_try_wait(bar, parity);
+    if (!ok) {
+      const long long t0 = clock64();
+      while (*abort_flag == 0u) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) {
+          ok = true;
+          break;
+        }
+        if (clock64() - t0 > kWaitLimitCycles) {
+          atomicOr(&g_wq_err, kErrWaitTimeout | what);
+          *abort_flag = 1u;
+          break;
+        }
       }
-      *reinterpret_cast<uint4*>(arow + 16 * (c ^ (tid & 7))) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
-    fence_proxy_async_smem();                // A, for the tensor core's reads
-    __syncthreads();
-    if (tid == 0 && *reinterpret_cast<volatile uint32_t*>(abort_flag) == 0u) {
+    return __all_sync(0xffffffffu, ok);
+  };
+
+  if (warp == kCodesWarp) {
+    // ---- codes and group constants, one 256-column stage at a time ----
+    if (lane == 0) prefetch_tensormap(&tm_codes);
+    int issued = 0;
+    for (int st = 0; st < nstages; ++st) {
+      const int cs = st % kCodeStages;
+      if (st >= kCodeStages &&
+          !wait(&bars->codes_empty[cs], (unsigned)((st / kCodeStages - 1) & 1), kErrWaitSlot)) {
+        break;
+      }
+      const long long c0 = kb + (long long)st * kStageK;
+      const int in_stage = nslices - st * kSlicesPerStage < kSlicesPerStage
+                               ? nslices - st * kSlicesPerStage
+                               : kSlicesPerStage;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars->codes_full[cs], (unsigned)kCodeBytes);
+        tc::tma_load_2d(base + kOffCodes + cs * kCodeBytes, &tm_codes, &bars->codes_full[cs],
+                        (int)(c0 / 2), (int)rbase);
+      }
+      // per 32 columns of each slice of the stage, its group's constants:
+      // [slice][32 columns][row] floats, so the dequantize warps read them
+      // with no group arithmetic
+      float* sst = reinterpret_cast<float*>(base + kOffS + cs * kConstBytes);
+      float* zst = reinterpret_cast<float*>(base + kOffZ + cs * kConstBytes);
+      for (int sub = 0; sub < in_stage; ++sub) {
+        for (int hf = 0; hf < kQuarters; ++hf) {
+          const uint32_t g = (uint32_t)(c0 + sub * kSliceK + hf * 32) / ug;
+          const int o = (sub * kQuarters + hf) * kBM;
+#pragma unroll
+          for (int j = 0; j < kBM / 32; ++j) {
+            const int r = lane + 32 * j;
+            const long long gi = (rbase + r) * groups + g;
+            cp_async4(sst + o + r, a.scales + gi);
+            if (!SYM) cp_async4(zst + o + r, a.zeros + gi);
+          }
+        }
+      }
+      cp_async_mbar_arrive_noinc(&bars->codes_full[cs]);
+      issued = st + 1;
+    }
+    // the copies this warp issued land before the CTA can exit
+    for (int st = issued - kCodeStages > 0 ? issued - kCodeStages : 0; st < issued; ++st) {
+      if (!mbar_wait(&bars->codes_full[st % kCodeStages], (unsigned)((st / kCodeStages) & 1))) {
+        if (lane == 0) atomicOr(&g_wq_err, kErrWaitTimeout | kErrWaitDrain);
+        *abort_flag = 1u;
+      }
+    }
+  } else if (warp == kTokensWarp) {
+    // ---- token rows, one 64-column slice at a time ----
+    if (lane == 0) prefetch_tensormap(&tm_x);
+    const unsigned boxbytes = (unsigned)bn * 128u;
+    int issued = 0, slot = 0, round = 0;
+    for (int s = 0; s < nslices; ++s) {
+      if (s >= xs && !wait(&bars->x_empty[slot], (unsigned)((round - 1) & 1), kErrWaitSlot)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars->x_full[slot], boxbytes * kXBoxes);
+#pragma unroll
+        for (int bx = 0; bx < kXBoxes; ++bx) {
+          tc::tma_load_2d(base + kOffX + (slot * kXBoxes + bx) * (int)boxbytes, &tm_x,
+                          &bars->x_full[slot], (int)(kb + (long long)s * kSliceK + 64 * bx),
+                          (int)m0);
+        }
+      }
+      __syncwarp();
+      issued = s + 1;
+      if (++slot == xs) {
+        slot = 0;
+        ++round;
+      }
+    }
+    for (int s = issued - xs > 0 ? issued - xs : 0; s < issued; ++s) {
+      if (!mbar_wait(&bars->x_full[s % xs], (unsigned)((s / xs) & 1))) {
+        if (lane == 0) atomicOr(&g_wq_err, kErrWaitTimeout | kErrWaitDrain);
+        *abort_flag = 1u;
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ---- MMA issue ----
+    const bool issuer = tc::elect_one();
+    const uint32_t idesc = tc::instr_desc_f16(DT == kBF16, kBM, bn, false, false);
+    const uint32_t x0 = smem_addr(base + kOffX);
+    const uint32_t xbox = (uint32_t)bn * 128u;
+    int slot = 0, round = 0;
+    for (int s = 0; s < nslices; ++s) {
+      const int as = a_slot(s);
+      if (!wait(&bars->a_full[as], (unsigned)(a_use(s) & 1), kErrWaitData)) break;
+      if (!wait(&bars->x_full[slot], (unsigned)(round & 1), kErrWaitData)) break;
+      if (issuer) {
+        tc::fence_after_sync();
+#pragma unroll
+        for (int bx = 0; bx < kXBoxes; ++bx) {
+          const uint64_t bdesc =
+              tc::smem_desc_sw128(x0 + (slot * kXBoxes + bx) * xbox, 16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            // +32 bytes per K = 16 step: +2 in the descriptor's address field
+            tc::mma_f16_ts(tmem + kAccCol, tmem + as * kSliceCols + (bx * 4 + kk) * 8,
+                           bdesc + 2 * kk, idesc, (s > 0 || bx > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        tc::commit(&bars->a_empty[as]);
+        tc::commit(&bars->x_empty[slot]);
+      }
+      __syncwarp();
+      if (++slot == xs) {
+        slot = 0;
+        ++round;
+      }
+    }
+    // covers every MMA this thread issued, also after an abort
+    if (issuer) tc::commit(&bars->acc_full);
+    __syncwarp();
+  } else {
+    // ---- dequantize (warps 0 .. kDqWarps - 1) ----
+    const int q = warp & 3;                 // lane quarter
+    const int h = warp >> 2;                // set: slices s with s % kSets == h
+    const int r = q * 32 + lane;            // row of the CTA = tensor-memory lane
+    const uint32_t tlane = tmem + ((uint32_t)(q * 32) << 16);
+    const float zc = SYM ? (float)(1 << (a.bits - 1)) : 0.f;
+    const DqConst kc = dq_const(zc);
+    for (int s = h; s < nslices; s += kSets) {
+      const int st = s / kSlicesPerStage;
+      const int sub = s % kSlicesPerStage;
+      const int cs = st % kCodeStages;
+      const int in_stage = nslices - st * kSlicesPerStage < kSlicesPerStage
+                               ? nslices - st * kSlicesPerStage
+                               : kSlicesPerStage;
+      // the warp's first slice of the stage waits for it (a set's slices of a
+      // stage are kSets apart, so only the first has sub < kSets)
+      if (sub < kSets &&
+          !wait(&bars->codes_full[cs], (unsigned)((st / kCodeStages) & 1), kErrWaitData)) {
+        break;
+      }
+      // this slice's kSliceK / 2 bytes of row r: 16-byte chunks kQuarters * sub
+      // + i, stored at chunk ^ (r % 8) by the 128-byte swizzle
+      const unsigned char* crow = base + kOffCodes + cs * kCodeBytes + r * 128;
+      uint32_t words[kWords];
+#pragma unroll
+      for (int i = 0; i < kWords / 4; ++i) {
+        const uint4 w =
+            *reinterpret_cast<const uint4*>(crow + 16 * ((kQuarters * sub + i) ^ (r & 7)));
+        words[4 * i] = w.x;
+        words[4 * i + 1] = w.y;
+        words[4 * i + 2] = w.z;
+        words[4 * i + 3] = w.w;
+      }
+      const int o = sub * kQuarters * kBM + r;
+      const float* sst = reinterpret_cast<const float*>(base + kOffS + cs * kConstBytes) + o;
+      const float* zst = reinterpret_cast<const float*>(base + kOffZ + cs * kConstBytes) + o;
+      float sc[kQuarters], zp[kQuarters];
+#pragma unroll
+      for (int i = 0; i < kQuarters; ++i) {
+        sc[i] = sst[i * kBM];
+        zp[i] = SYM ? 0.f : zst[i * kBM];
+      }
+      __syncwarp();
+      // the warp's last slice of this stage: the stage's codes are in registers
+      if (sub + kSets >= in_stage && lane == 0) mbar_arrive(&bars->codes_empty[cs]);
+      const int as = a_slot(s);
+      if (a_use(s) > 0 &&
+          !wait(&bars->a_empty[as], (unsigned)((a_use(s) - 1) & 1), kErrWaitSlot)) {
+        break;
+      }
       tc::fence_after_sync();
-      const uint32_t a_addr = smem_addr(base + tc05::kOffA + (t & 1) * tc05::kATile);
-      const uint32_t x_addr = smem_addr(base + tc05::kOffX + st * tc05::kXTile);
 #pragma unroll
-      for (int kk = 0; kk < tc05::kBK / 16; ++kk) {
-        tc::mma_f16(tmem, tc::smem_desc_sw128(a_addr + kk * 32, 16, 1024),
-                    tc::smem_desc_sw128(x_addr + kk * 32, 16, 1024), idesc,
-                    (t > 0 || kk > 0) ? 1u : 0u);
+      for (int hh = 0; hh < kWords / 8; ++hh) {   // 64 codes -> 32 columns per store
+        uint32_t out[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {         // codes 8c' .. 8c' + 7, c' = 8 hh + c
+          const int q4 = (8 * hh + c) / 4;    // its 32-column quarter
+          dequant8<DT, SYM>(words[8 * hh + c], kc, pack2f(sc[q4], sc[q4]),
+                            pack2f(-zp[q4], -zp[q4]), out + 4 * c);
+        }
+        tc::tmem_st32u(tlane + as * kSliceCols + 32 * hh, out);
       }
-      tc::commit(&mma_done[t & 1]);
-      last_committed = t;
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->a_full[as]);
     }
-  }
-  cp_async_wait<0>();
-  // The last committed slice's commit covers every MMA the CTA issued: drained
-  // (bounded) even after an abort, before tensor memory is read or freed.
-  if (tid == 0 && last_committed >= 0) {
-    if (!mbar_wait(&mma_done[last_committed & 1], (unsigned)((last_committed >> 1) & 1))) {
-      atomicOr(&g_wq_err, kErrWaitTimeout | kErrWaitDrain);
-      *reinterpret_cast<volatile uint32_t*>(abort_flag) = 1u;
-    }
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const bool ok = *reinterpret_cast<volatile uint32_t*>(abort_flag) == 0u && nslices > 0;
 
-  // thread tid = feature rbase + tid = TMEM lane tid; columns = tokens m0 ..
-  const long long f = rbase + tid;
-  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-  float bias = 0.f;
-  if (a.partial == nullptr && a.bias != nullptr) bias = load_f32<DT>(a.bias, f);
+    // ---- epilogue: accumulator -> output (or the split's partial) ----
+    bool ok = mbar_wait(&bars->acc_full, 0u);
+    if (!ok) {
+      if (lane == 0) atomicOr(&g_wq_err, kErrWaitTimeout | kErrWaitDrain);
+      *abort_flag = 1u;
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    tc::fence_after_sync();
+    ok = ok && *abort_flag == 0u && nslices > 0;
+    const long long f = rbase + r;
+    const long long m_end = m0 + bn < a.m ? m0 + bn : a.m;
+    float bias = 0.f;
+    if (a.partial == nullptr && a.bias != nullptr) bias = load_f32<DT>(a.bias, f);
+    for (int cb = h; cb * 32 < bn; cb += kSets) {
+      float v[32];
+      tc::tmem_ld32(tlane + kAccCol + cb * 32, v);
+      tc::tmem_wait_ld();
 #pragma unroll
-  for (int cb = 0; cb < tc05::kBN / 32; ++cb) {
-    float v[32];
-    tc::tmem_ld32(lane_addr + cb * 32, v);
-    tc::tmem_wait_ld();
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const long long tok = m0 + cb * 32 + j;
-      if (tok >= a.m) break;
-      const float val = ok ? v[j] : __int_as_float(0x7FC00000);   // NaN after a give-up
-      if (a.partial != nullptr) {
-        a.partial[((long long)blockIdx.y * a.m + tok) * a.n + f] = val;
-      } else {
-        store_f32<DT>(a.out, tok * a.ldo + f, val + bias);
+      for (int j = 0; j < 32; ++j) {
+        const long long tok = m0 + cb * 32 + j;
+        if (tok >= m_end) break;
+        const float val = ok ? v[j] : __int_as_float(0x7FC00000);   // NaN after a give-up
+        if (a.partial != nullptr) {
+          a.partial[((long long)blockIdx.y * a.m + tok) * a.n + f] = val;
+        } else {
+          store_f32<DT>(a.out, tok * a.ldo + f, val + bias);
+        }
       }
     }
   }
@@ -843,7 +1059,7 @@ __global__ void __launch_bounds__(tc05::kThreads) wq_gemm_tc05_kernel(const Quan
   __syncthreads();
   if (warp == 0) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, tc05::kBN);
+    tc::tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -906,15 +1122,30 @@ const void* gemm_fn(const QuantLinearArgs& a) {
   return a.x_dtype == kBF16 ? gemm_ptr<kBF16>(a, mt) : gemm_ptr<kF16>(a, mt);
 }
 
-// LLMOPT_B200_QUANT_TC05=1 routes 2- and 4-bit token batches (more than 8
-// tokens, n % 128 == 0) to wq_gemm_tc05_kernel.  Off by default: that kernel
-// has not been run on a GPU yet.
-bool tc05_enabled() {
-  static const bool on = [] {
+// Which 2- and 4-bit calls the tcgen05 kernel takes (n % 128 == 0, groups of
+// whole 32-column pieces): batches above kTc05MinTokens tokens by default;
+// LLMOPT_B200_QUANT_TC05=1 every batch, =0 none.  (At 1 to 16 tokens the
+// mma.sync kernel's 8- and 32-token tiles are as fast or faster: the tcgen05
+// kernel's time is its dequantization, the same for any batch up to 256.)
+constexpr long long kTc05MinTokens = 16;
+bool tc05_enabled(long long m) {
+  static const int mode = [] {
     const char* v = std::getenv("LLMOPT_B200_QUANT_TC05");
-    return v != nullptr && v[0] == '1';
+    return v == nullptr ? -1 : (v[0] == '1' ? 1 : 0);
   }();
-  return on;
+  return mode == 1 || (mode < 0 && m > kTc05MinTokens);
+}
+
+bool tc05_takes(const QuantLinearArgs& a) {
+  // TMA coordinates and the kernel's column arithmetic are 32-bit
+  return a.bits < 8 && a.n % tc05::kBM == 0 && a.group % 32 == 0 &&
+         a.k < (1LL << 31) && a.n < (1LL << 31) && a.m < (1LL << 31);
+}
+
+template <int DT>
+const void* tc05_fn(bool sym) {
+  return sym ? reinterpret_cast<const void*>(&wq_gemm_tc05_kernel<DT, true>)
+             : reinterpret_cast<const void*>(&wq_gemm_tc05_kernel<DT, false>);
 }
 
 // The tensor-core kernel a call runs and its CTA shape.
@@ -924,18 +1155,36 @@ struct GemmShape {
   size_t smem;
   long long rows;      // output features per CTA
   long long tokens;    // tokens per CTA
+  bool tc05;
 };
 
 GemmShape gemm_shape(const QuantLinearArgs& a) {
-  if (tc05_enabled() && a.bits < 8 && a.m > kMTSmall && a.n % tc05::kBM == 0 &&
-      (a.group == 32 || a.group % tc05::kBK == 0)) {
-    const void* fn = a.x_dtype == kBF16
-                         ? reinterpret_cast<const void*>(&wq_gemm_tc05_kernel<kBF16>)
-                         : reinterpret_cast<const void*>(&wq_gemm_tc05_kernel<kF16>);
-    return {fn, tc05::kThreads, (size_t)tc05::kSmem, tc05::kBM, tc05::kBN};
+  if (tc05_enabled(a.m) && tc05_takes(a)) {
+    const void* fn = a.x_dtype == kBF16 ? tc05_fn<kBF16>(a.symmetric != 0)
+                                        : tc05_fn<kF16>(a.symmetric != 0);
+    return {fn, tc05::kThreads, (size_t)tc05::kSmem, tc05::kBM, tc05::bn_of(a.m), true};
   }
   const int mt = tokens_per_cta(a);
-  return {gemm_fn(a), kThreads, gemm_smem(a, mt), kRows, mt};
+  return {gemm_fn(a), kThreads, gemm_smem(a, mt), kRows, mt, false};
+}
+
+// tcgen05 kernel, one CTA per SM: the split count that minimizes the waves of
+// CTAs times the 128-column tiles per CTA, plus one tile per split for the
+// partial write and the reduce.
+int tc05_splits(long long ctas, long long tiles, int sms) {
+  long long best = -1;
+  int best_splits = 1;
+  for (long long want = 1; want <= 16 && want <= tiles; ++want) {
+    const long long per = (tiles + want - 1) / want;
+    const long long used = (tiles + per - 1) / per;
+    const long long waves = (ctas * used + sms - 1) / sms;
+    const long long cost = waves * per + (used > 1 ? used : 0);
+    if (best < 0 || cost < best) {
+      best = cost;
+      best_splits = (int)used;
+    }
+  }
+  return best_splits;
 }
 
 long long grid_blocks(long long work, int threads) {
@@ -962,6 +1211,7 @@ int quant_linear_splits(const QuantLinearArgs& a, int sm_count) {
   const GemmShape g = gemm_shape(a);
   const long long ctas = (a.n / g.rows) * ((a.m + g.tokens - 1) / g.tokens);
   const long long tiles = a.k / kKT;
+  if (g.tc05) return tc05_splits(ctas, tiles, sm_count);
   int occ = 1;
   if (cudaFuncSetAttribute(g.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem) !=
           cudaSuccess ||
@@ -995,8 +1245,23 @@ cudaError_t quant_linear_launch(const QuantLinearArgs& a, cudaStream_t stream) {
   cudaError_t e =
       cudaFuncSetAttribute(g.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
   if (e != cudaSuccess) return e;
-  e = launch_pdl(g.fn, dim3((unsigned)gx, (unsigned)a.splits, (unsigned)gz),
-                 dim3((unsigned)g.threads), args, g.smem, stream);
+  if (g.tc05) {
+    // codes: uint8 [n, k/2], boxes of 128 rows x 128 bytes; token rows: 16-bit
+    // [m, ldx], boxes of bn rows x 64 columns (rows past m read as zeros)
+    CUtensorMap tm_codes, tm_x;
+    if (!tensor_map_2d(&tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.qweight, (uint64_t)a.k / 2,
+                       (uint64_t)a.n, (uint64_t)a.k / 2, 128, tc05::kBM) ||
+        !tensor_map_2d(&tm_x, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.x, (uint64_t)a.k, (uint64_t)a.m,
+                       (uint64_t)a.ldx * 2, 64, (uint32_t)g.tokens)) {
+      return cudaErrorInvalidValue;
+    }
+    void* targs[] = {const_cast<QuantLinearArgs*>(&a), &tm_codes, &tm_x};
+    e = launch_pdl(g.fn, dim3((unsigned)gx, (unsigned)a.splits, (unsigned)gz),
+                   dim3((unsigned)g.threads), targs, g.smem, stream);
+  } else {
+    e = launch_pdl(g.fn, dim3((unsigned)gx, (unsigned)a.splits, (unsigned)gz),
+                   dim3((unsigned)g.threads), args, g.smem, stream);
+  }
   if (e != cudaSuccess || a.partial == nullptr) return e;
   const void* rfn = a.x_dtype == kBF16 ? reinterpret_cast<const void*>(&wq_reduce_kernel<kBF16>)
                                        : reinterpret_cast<const void*>(&wq_reduce_kernel<kF16>);

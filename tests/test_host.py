@@ -374,10 +374,16 @@ def test_quant_linear_entry_points_validate_arguments(lib):
     import ctypes
 
     n = ctypes.c_size_t(0)
-    # 4096 x 4096 int4, 64 tokens: a split-k workspace is reported
+    # 4096 x 4096 int4, 8 tokens (mma.sync kernel): a split-k workspace of whole
+    # [m, n] fp32 partials is reported
+    assert lib.llmopt_quant_linear_workspace_size(0, 8, 4096, 4096, 4, 128, 2,
+                                                  ctypes.byref(n)) == 0
+    assert n.value > 0 and n.value % (8 * 4096 * 4) == 0
+    # 64 tokens (tcgen05 kernel, one CTA per SM; 148 SMs without a device):
+    # 32 row blocks x 32 tiles -> 4 splits of 8 tiles, one wave of 128 CTAs
     assert lib.llmopt_quant_linear_workspace_size(0, 64, 4096, 4096, 4, 128, 2,
                                                   ctypes.byref(n)) == 0
-    assert n.value % (64 * 4096 * 4) == 0
+    assert n.value == 4 * 64 * 4096 * 4
     assert lib.llmopt_quant_linear_workspace_size(0, 0, 4096, 4096, 4, 128, 2,
                                                   ctypes.byref(n)) == 0 and n.value == 0
     assert lib.llmopt_quant_linear_workspace_size(0, 8, 64, 128, 3, 64, 2, ctypes.byref(n)) == 2

@@ -1,12 +1,10 @@
-"""CPU emulation of the tensor-core quantized-linear kernels' index arithmetic.
+"""CPU emulation of the mma.sync quantized-linear kernel's index arithmetic.
 
 ``wq_gemm_acc_kernel`` (2/4-bit codes, group scale on the fp32 accumulators)
-and ``wq_gemm_tc05_kernel`` (tcgen05 path) are restated thread by thread: the
-cp.async copy slots and their source bounds, the shared-memory swizzles, the
-ldmatrix / MMA fragment maps (m16n8k16) or the tcgen05 operand reads through
-the 128-byte-swizzle K-major rule, the group cursors of split k ranges, the
-pipeline's stage and A-buffer reuse against in-flight MMAs and the mbarrier
-phase parities, and the epilogue's output map.  Values are carried exactly in
+is restated thread by thread: the cp.async copy slots and their source bounds,
+the shared-memory swizzles, the ldmatrix / MMA fragment maps (m16n8k16), the
+group cursors of split k ranges and the epilogue's output map.  (The tcgen05
+kernel has its own restatement, ``test_quant_tc05_layout.py``.)  Values are carried exactly in
 float64, so each result must equal the oracle's ``x @ W^T`` to rounding.
 
 This checks the layouts on the CPU before and beside the GPU runs; it does not
@@ -222,184 +220,6 @@ def acc_emulate(n, k, m, bits, group, sym, MT, splits, seed):
     return err
 
 
-# wq_gemm_tc05_kernel
-T_BM, T_BN, T_BK, T_THREADS, T_STAGES, T_GROUPS = 128, 64, 64, 128, 4, 2
-
-
-def sw128_read(tile_bytes, rows, kk):
-    """The MMA's view of a K-major SW128 tile for K16 step kk: [rows, 16] values
-    (bytes decoded as little-endian 16-bit patterns)."""
-    out = np.zeros((rows, 16), np.int64)
-    for i in range(rows):
-        for e in range(16):
-            logical = kk * 32 + 2 * e           # byte offset in the 128-byte logical row
-            chunk = logical // 16
-            phys = (i // 8) * 1024 + (i % 8) * 128 + 16 * (chunk ^ (i % 8)) + logical % 16
-            out[i, e] = int(tile_bytes[phys]) | int(tile_bytes[phys + 1]) << 8
-    return out
-
-
-def bits_to_f(b):
-    return po.to_f32(np.asarray(b, np.uint16), "bf16").astype(np.float64)
-
-
-def tc05_run_cta(qw, scales, zeros, xb, a, bx, by, bz, partial, out_mark):
-    n, k, m, group, sym, bits = a["n"], a["k"], a["m"], a["group"], a["sym"], a["bits"]
-    rbase, m0 = bx * T_BM, bz * T_BN
-    kb = by * a["kps"]
-    ke = min(kb + a["kps"], k)
-    nslices = (ke - kb) // T_BK
-    mrem = m - m0
-    groups = k // group
-    row_bytes = k // 2
-    gps = 1 if group >= T_BK else T_BK // group
-    sps = group // T_BK if group >= T_BK else 1
-    slice0 = kb // T_BK
-    cur = dict(g=slice0 * gps if gps > 1 else slice0 // sps, gin=0 if gps > 1 else slice0 % sps)
-    codes = [np.full(T_BM * 32, -1, np.int64) for _ in range(T_STAGES)]
-    xs = [np.full(T_BN * 128, -1, np.int64) for _ in range(T_STAGES)]
-    sc = [np.full((T_BM, T_GROUPS), np.nan) for _ in range(T_STAGES)]
-    zc = [np.full((T_BM, T_GROUPS), np.nan) for _ in range(T_STAGES)]
-    owner = [None] * T_STAGES
-    A = [np.full(T_BM * 128, -1, np.int64) for _ in range(2)]
-    inflight = []                 # slices whose MMAs are committed and not known complete
-    phases_done = [0, 0]          # completed phases per barrier
-    acc = np.zeros((T_BM, T_BN))
-    flat_q = qw.reshape(-1)
-
-    def complete_upto(u):
-        while inflight and inflight[0] <= u:
-            s = inflight.pop(0)
-            phases_done[s & 1] += 1
-
-    def wait(slice_):
-        # parity wait: returns once the phase with parity (slice>>1)&1 of barrier slice&1
-        # completed; must be exactly phase slice>>1 (no phase skipped or aliased)
-        b, ph = slice_ & 1, slice_ >> 1
-        complete_upto(slice_)
-        assert phases_done[b] == ph + 1, (slice_, phases_done)
-
-    def issue(t):
-        st = t % T_STAGES
-        for u in inflight:
-            assert u % T_STAGES != st, ("stage overwritten under an MMA", t, u)
-        for tid in range(T_THREADS):
-            r = tid
-            for p in range(2):
-                src = (rbase + r) * row_bytes + kb // 2 + t * (T_BK // 2) + 16 * p
-                assert 0 <= src and src + 16 <= flat_q.size
-                assert src + 16 <= (rbase + r) * row_bytes + row_bytes
-                pos = p ^ ((r >> 2) & 1)
-                codes[st][r * 32 + 16 * pos:r * 32 + 16 * pos + 16] = flat_q[src:src + 16]
-            xr0, xc = tid >> 3, tid & 7
-            for q in range(T_BN * 8 // T_THREADS):
-                row = xr0 + 16 * q
-                dst = row * 128 + 16 * (xc ^ (xr0 & 7))
-                assert (xc ^ (xr0 & 7)) == (xc ^ (row & 7))
-                if row < mrem:
-                    col = kb + 8 * xc + t * T_BK
-                    assert m0 + row < m and col + 8 <= k
-                    vals = xb[m0 + row, col:col + 8]
-                    for e in range(8):
-                        xs[st][dst + 2 * e] = int(vals[e]) & 0xFF
-                        xs[st][dst + 2 * e + 1] = int(vals[e]) >> 8
-                else:
-                    xs[st][dst:dst + 16] = 0
-            for g in range(gps):
-                gi = (rbase + r) * groups + cur["g"] + g
-                assert cur["g"] + g < groups
-                sc[st][r, g] = scales.reshape(-1)[gi]
-                if not sym:
-                    zc[st][r, g] = zeros.reshape(-1)[gi]
-        owner[st] = t
-        if gps > 1:
-            cur["g"] += gps
-        else:
-            cur["gin"] += 1
-            if cur["gin"] == sps:
-                cur["gin"] = 0
-                cur["g"] += 1
-
-    for t in range(min(T_STAGES - 2, nslices)):
-        issue(t)
-    zsym = float(1 << (bits - 1))
-    last = -1
-    for t in range(nslices):
-        st = t % T_STAGES
-        assert owner[st] == t
-        if t >= 2:
-            wait(t - 2)
-        if t + T_STAGES - 2 < nslices:
-            issue(t + T_STAGES - 2)
-        for u in inflight:
-            assert (u & 1) != (t & 1), ("A buffer overwritten under an MMA", t, u)
-        for tid in range(T_THREADS):
-            r = tid
-            c0 = codes[st][r * 32 + 16 * ((r >> 2) & 1):][:16]
-            c1 = codes[st][r * 32 + 16 * (1 ^ ((r >> 2) & 1)):][:16]
-            raw = np.concatenate([c0, c1])
-            assert (raw >= 0).all()
-            words = [int(raw[4 * w]) | int(raw[4 * w + 1]) << 8 | int(raw[4 * w + 2]) << 16
-                     | int(raw[4 * w + 3]) << 24 for w in range(8)]
-            for c in range(8):
-                g = (c >> 2) if gps > 1 else 0
-                s_ = np.float32(sc[st][r, g])
-                z = np.float32(zsym if sym else zc[st][r, g])
-                vals = []
-                for j in range(4):
-                    q0 = (words[c] >> (8 * j)) & 0xF
-                    q1 = (words[c] >> (8 * j + 4)) & 0xF
-                    vals += [np.float32(np.float32(q0) - z) * s_, np.float32(np.float32(q1) - z) * s_]
-                b16 = po.from_f32(np.asarray(vals, np.float32), "bf16").astype(np.int64)
-                pos = c ^ (r & 7)
-                for e in range(8):
-                    A[t & 1][r * 128 + 16 * pos + 2 * e] = b16[e] & 0xFF
-                    A[t & 1][r * 128 + 16 * pos + 2 * e + 1] = b16[e] >> 8
-        # MMA issue: 4 K16 steps reading A[t&1] and x stage st
-        for kk in range(T_BK // 16):
-            a_bits = sw128_read(A[t & 1], T_BM, kk)
-            b_bits = sw128_read(xs[st], T_BN, kk)
-            assert (a_bits >= 0).all() and (b_bits >= 0).all()
-            acc += bits_to_f(a_bits) @ bits_to_f(b_bits).T
-        inflight.append(t)
-        last = t
-    if last >= 0:
-        wait(last)
-    for tid in range(T_THREADS):
-        f = rbase + tid
-        for j in range(T_BN):
-            tok = m0 + j
-            if tok >= m:
-                break
-            partial[by, tok, f] += acc[tid, j]
-            out_mark[tok, f] += 1
-
-
-def tc05_emulate(n, k, m, bits, group, sym, splits, seed):
-    rng = np.random.default_rng(seed)
-    w = (rng.standard_normal((n, k)) * 0.05).astype(np.float32)
-    s, z = qo.choose_qparams(w, bits, group, sym)
-    codes = qo.quantize_to_codes(w, s, z, bits, group, sym)
-    qw = qo.pack_int4(codes)
-    x = po.from_f32(rng.standard_normal((m, k)).astype(np.float32), "bf16")   # uint16 bits
-    tiles = k // 128
-    per = (tiles + splits - 1) // splits
-    nsplit = (tiles + per - 1) // per
-    a = dict(n=n, k=k, m=m, group=group, sym=sym, bits=bits, kps=per * 128)
-    partial = np.zeros((nsplit, m, n))
-    mark = np.zeros((m, n), np.int64)
-    for bx in range(n // T_BM):
-        for by in range(nsplit):
-            for bz in range((m + T_BN - 1) // T_BN):
-                tc05_run_cta(qw, s, z, x.astype(np.int64), a, bx, by, bz, partial, mark)
-    assert (mark == nsplit).all()
-    y = partial.sum(0)
-    want = qo.quant_linear(x, "bf16", qw, s, z, bits, group, sym, (n, k))
-    err = np.abs(y - want).max()
-    assert err < 1e-9 * max(1.0, np.abs(want).max()), err
-    return err
-
-
 ACC_CASES = [
     (64, 256, 1, 4, 128, True, 8, 1),
     (64, 256, 5, 4, 64, False, 8, 2),
@@ -414,17 +234,3 @@ ACC_CASES = [
 @pytest.mark.parametrize("case", ACC_CASES)
 def test_acc_kernel_layout(case):
     acc_emulate(*case, seed=sum(case) % 97)
-
-
-TC05_CASES = [
-    (128, 256, 9, 4, 128, True, 1),
-    (128, 512, 64, 4, 32, False, 2),
-    (256, 384, 70, 2, 64, True, 3),
-    (128, 1024, 33, 4, 256, False, 3),
-    (128, 768, 100, 4, 384, True, 4),
-]
-
-
-@pytest.mark.parametrize("case", TC05_CASES)
-def test_tc05_kernel_layout(case):
-    tc05_emulate(*case, seed=sum(case) % 97)
