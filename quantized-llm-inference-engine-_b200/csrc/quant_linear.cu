@@ -608,33 +608,34 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_acc_kernel(const QuantLinear
 
 // ---- 2- and 4-bit codes on the 5th-generation tensor cores ---------------------
 //
-// A CTA owns 128 output features (the 128 lanes of tensor memory, MMA M) and bn
-// tokens (MMA N: the batch rounded up to 16, at most 64; larger batches take
-// several token blocks) over a k range of whole 64-column slices.  Each weight
-// is dequantized once per CTA and token block, straight into tensor memory as
-// the MMA's A operand; the token rows are the B operand in shared memory.
-// Warp roles:
+// A CTA owns 128 output features (MMA M; the accumulator's 128 tensor-memory
+// lanes) and bn tokens (MMA N: the batch rounded up to 16, at most 64; larger
+// batches take several token blocks) over a k range of whole 64-column
+// slices.  Each weight is dequantized once per CTA and token block into a
+// K-major, 128-byte-swizzled A tile in shared memory; the token rows are the
+// B operand beside it.  Warp roles:
 // * warps 0-11 dequantize in three sets of four: set h = w / 4 takes the
 //   slices s with s % 3 == h, warp w the 32 rows of lane quarter w % 4.
 //   Thread r turns its row's 64 codes of a slice into the reference's weights
-//   - (q - z) * s in float32, rounded once to the compute dtype - and stores
-//   the 32 pairs into a 32-column A slot in tensor memory (tcgen05.st).  Each
-//   set owns two slots, so a slot's barriers are only ever waited on by the
-//   warps that saw all of its earlier phases;
+//   - (q - z) * s in float32, rounded once to the compute dtype - and writes
+//   the 128-byte row of the set's A tile (eight 16-byte stores at chunk
+//   c ^ (r % 8)), then fence.proxy.async for the MMA's reads.  Each set owns
+//   its A tile, so a tile's barriers are only ever waited on by the warps
+//   that saw all of its earlier phases;
 // * warp 12 loads the codes: one TMA box of 128 rows x 128 bytes (256 columns,
 //   128-byte swizzle) per stage of a 4-stage ring, plus the stage's group
 //   scales (and zero points) by cp.async completing on the same mbarrier;
 // * warp 13 loads the token rows: one TMA box of bn rows x 64 columns per
 //   slice (K-major, 128-byte swizzle: the layout the MMA reads);
-// * warp 14 issues, from one elected thread, the four tcgen05.mma (K = 16, A
-//   from tensor memory) of each slice into the fp32 accumulator and commits
-//   them to the slot barriers that free the A slot and the token slot.
+// * warp 14 issues, from one elected thread, the four tcgen05.mma (K = 16)
+//   of each slice into the fp32 accumulator and commits them to the barriers
+//   that free the A tile and the token slot.
 // The dequantize warps then read the accumulator (tcgen05.ld, thread r =
 // feature r) and write the output, or the split's fp32 partial.
-// (Token tiles of 128 and 256 ran 2.2x and 4x faster at those batches but
-// returned wrong sums for the first lane quarter of some CTAs, 1 to 10 of
-// 112 row blocks per call, when the MMAs outran the dequantization; the tile
-// stays at 64 tokens, where long stress runs never showed it.)
+// (kAInSmem = false keeps A in tensor memory instead - tcgen05.st by the
+// dequantize warps, MMAs with A from tensor memory - which ran 10 % faster at
+// 64 tokens but returned wrong sums for the first lane quarter (features 0-31
+// of a row block) of a few CTAs per call under load; it is not used.)
 //
 // Dequantization without conversions: OR-ing nibble j of a code word (bits
 // 4j..4j+3) into the float 2^23 gives 2^23 + q * 16^j exactly; one packed FMA
@@ -656,7 +657,8 @@ constexpr int kQuarters = kSliceK / 32;           // group constants per row per
 constexpr int kStageK = 256;                      // k per codes stage (128 bytes of a row)
 constexpr int kSlicesPerStage = kStageK / kSliceK;
 constexpr int kCodeStages = 4;
-constexpr int kSlotsPerSet = 2;                   // A slots of a set, reused only by it
+constexpr int kSlotsPerSet = 1;                   // A slots of a set, reused only by it
+constexpr bool kAInSmem = true;                   // A tiles in shared memory (else tensor memory)
 constexpr int kMaxXSlots = 8;
 constexpr int kDqWarps = 12;
 constexpr int kSets = kDqWarps / 4;               // slices in flight in the dequantize warps
@@ -665,24 +667,29 @@ constexpr int kTokensWarp = kDqWarps + 1;
 constexpr int kMmaWarp = kDqWarps + 2;
 constexpr int kThreads = (kDqWarps + 3) * 32;
 constexpr int kMaxBN = 64;
+constexpr int kATile = kBM * 128;                 // one A slot in shared memory: 16 KB
 constexpr int kCodeBytes = kBM * kStageK / 2;     // 16 KB per stage
 constexpr int kConstBytes = kSlicesPerStage * kQuarters * kBM * 4;   // [slice][32 cols][row]
-constexpr int kXBytes = 128 * 1024;               // token-slice ring
+constexpr int kASlots = kSets * kSlotsPerSet;
+constexpr int kXBytes = kAInSmem ? 64 * 1024 : 128 * 1024;   // token-slice ring
 constexpr int kOffCodes = 0;                      // offsets from the 1024-byte aligned base
-constexpr int kOffX = kOffCodes + kCodeStages * kCodeBytes;
+constexpr int kOffA = kOffCodes + kCodeStages * kCodeBytes;
+constexpr int kOffX = kOffA + (kAInSmem ? kASlots * kATile : 0);
 constexpr int kOffS = kOffX + kXBytes;
 constexpr int kOffZ = kOffS + kCodeStages * kConstBytes;
 constexpr int kOffBar = kOffZ + kCodeStages * kConstBytes;
 constexpr int kBarBytes = 512;
 constexpr int kSmem = kOffBar + kBarBytes + 1024; // + alignment slack
-constexpr uint32_t kTmemCols = 512;               // A ring [0, 256), accumulator [256, 256 + bn)
-constexpr int kASlots = kSets * kSlotsPerSet;     // A ring in tensor-memory columns [0, 256)
-constexpr int kAccCol = 256;
+// tensor memory: the accumulator [kAccCol, kAccCol + bn), and the A ring in
+// columns [0, 256) when it is not in shared memory
+constexpr uint32_t kTmemCols = kAInSmem ? 64 : 512;
+constexpr int kAccCol = kAInSmem ? 0 : 256;
 static_assert(kAccCol + kMaxBN <= (int)kTmemCols, "tensor-memory columns");
 static_assert(kSmem <= 227 * 1024, "shared memory");
-static_assert(kOffX % 1024 == 0 && kOffS % 1024 == 0, "TMA destinations");
+static_assert(kOffX % 1024 == 0 && kOffS % 1024 == 0 && kOffA % 1024 == 0, "TMA / MMA tiles");
 static_assert(kDqWarps % 4 == 0 && kSets <= kSlicesPerStage, "dequantize warp sets");
-static_assert(kASlots * kSliceCols <= kAccCol, "A ring");
+static_assert(kAInSmem || kASlots * kSliceCols <= kAccCol, "A ring");
+static_assert(!kAInSmem || kSliceK == 64, "a shared-memory A slot is one 128-byte swizzle span");
 
 struct Bars {
   uint64_t codes_full[kCodeStages];   // TMA bytes + the 32 cp.async lanes + 1
@@ -940,8 +947,15 @@ __global__ void __launch_bounds__(tc05::kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             // +32 bytes per K = 16 step: +2 in the descriptor's address field
-            tc::mma_f16_ts(tmem + kAccCol, tmem + as * kSliceCols + (bx * 4 + kk) * 8,
-                           bdesc + 2 * kk, idesc, (s > 0 || bx > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (kAInSmem) {
+              const uint64_t adesc =
+                  tc::smem_desc_sw128(smem_addr(base + kOffA + as * kATile), 16, 1024);
+              tc::mma_f16(tmem + kAccCol, adesc + 2 * (bx * 4 + kk), bdesc + 2 * kk, idesc,
+                          (s > 0 || bx > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              tc::mma_f16_ts(tmem + kAccCol, tmem + as * kSliceCols + (bx * 4 + kk) * 8,
+                             bdesc + 2 * kk, idesc, (s > 0 || bx > 0 || kk > 0) ? 1u : 0u);
+            }
           }
         }
         tc::commit(&bars->a_empty[as]);
@@ -1017,10 +1031,25 @@ __global__ void __launch_bounds__(tc05::kThreads, 1)
           dequant8<DT, SYM>(words[8 * hh + c], kc, pack2f(sc[q4], sc[q4]),
                             pack2f(-zp[q4], -zp[q4]), out + 4 * c);
         }
-        tc::tmem_st32u(tlane + as * kSliceCols + 32 * hh, out);
+        if constexpr (kAInSmem) {
+          // row r of the K-major A tile, 16-byte chunk c at c ^ (r % 8) (the
+          // 128-byte swizzle the MMA's descriptor names)
+          unsigned char* arow = base + kOffA + as * kATile + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            *reinterpret_cast<uint4*>(arow + 16 * ((4 * hh + c) ^ (r & 7))) =
+                make_uint4(out[4 * c], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]);
+          }
+        } else {
+          tc::tmem_st32u(tlane + as * kSliceCols + 32 * hh, out);
+        }
       }
-      tc::tmem_wait_st();
-      tc::fence_before_sync();
+      if constexpr (kAInSmem) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // for the MMA's reads
+      } else {
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->a_full[as]);
     }

@@ -11,7 +11,8 @@ its constants read from the kernel source:
   magnitude and fractional zero points;
 * the data path of whole CTAs: the codes box as the TMA writes it with the
   128-byte swizzle, each thread's chunk reads, the per-slice group constants
-  the codes warp stages, the A operand's tensor-memory columns, the token
+  the codes warp stages, the A operand (its swizzled shared-memory tile, or
+  its tensor-memory columns), the token
   boxes as the MMA reads them through the K-major 128-byte-swizzle rule, the
   split of the k range, the accumulation and the output / split partials
   (summed in split order with the bias) - against the oracle's
@@ -48,6 +49,11 @@ def _constants():
     for name, expr in re.findall(r"constexpr (?:int|uint32_t|bool) (\w+) = ([^;]+);", body):
         expr = re.sub(r"\(int\)", "", expr).replace("/", "//")
         expr = expr.replace("false", "False").replace("true", "True")
+        # C conditionals: (a ? b : c) and a ? b : c
+        expr = re.sub(r"\(([^()?]+)\?([^():]+):([^()]+)\)", r"((\2) if (\1) else (\3))", expr)
+        m = re.fullmatch(r"([^?]+)\?([^:]+):(.+)", expr)
+        if m:
+            expr = "((%s) if (%s) else (%s))" % (m.group(2), m.group(1), m.group(3))
         env[name] = eval(expr, {}, dict(env))
     return env
 
@@ -58,6 +64,7 @@ SLICE_COLS, XBOXES, WORDS, QUARTERS = C["kSliceCols"], C["kXBoxes"], C["kWords"]
 SPS, CODE_STAGES, ASLOTS, MAX_XSLOTS = C["kSlicesPerStage"], C["kCodeStages"], C["kASlots"], C["kMaxXSlots"]
 DQ_WARPS, SETS, MAX_BN, XBYTES = C["kDqWarps"], C["kSets"], C["kMaxBN"], C["kXBytes"]
 ACC_COL, TMEM_COLS, SLOTS_PER_SET = C["kAccCol"], C["kTmemCols"], C["kSlotsPerSet"]
+A_IN_SMEM = C["kAInSmem"]
 
 
 def a_slot(s):
@@ -81,17 +88,18 @@ def x_slots(bn):
 def test_constants_fit():
     assert STAGE % SLICE == 0 and SLICE % 64 == 0
     assert ACC_COL + MAX_BN <= TMEM_COLS and TMEM_COLS in (32, 64, 128, 256, 512)
-    assert ASLOTS == SETS * SLOTS_PER_SET and ASLOTS * SLICE_COLS <= ACC_COL
+    assert ASLOTS == SETS * SLOTS_PER_SET
+    assert A_IN_SMEM or ASLOTS * SLICE_COLS <= ACC_COL
     # every set has a slice in each full stage (one codes_empty arrival per
     # warp per stage: at the set's last slice there)
-    assert DQ_WARPS % 4 == 0 and SETS <= SPS and 2 * SETS <= ASLOTS
+    assert DQ_WARPS % 4 == 0 and SETS <= SPS and SLOTS_PER_SET >= 1
     for bn in range(16, MAX_BN + 1, 16):
         assert 2 <= x_slots(bn) <= MAX_XSLOTS
         assert x_slots(bn) * bn * 128 * XBOXES <= XBYTES
         assert (bn * 128) % 1024 == 0        # every token box starts on a swizzle atom
     smem = C["kSmem"]
     assert smem <= 227 * 1024
-    for off in ("kOffCodes", "kOffX", "kOffS", "kOffZ", "kOffBar"):
+    for off in ("kOffCodes", "kOffA", "kOffX", "kOffS", "kOffZ", "kOffBar"):
         assert C[off] % 1024 == 0
     assert C["kOffBar"] + C["kBarBytes"] + 1024 == smem
 
@@ -226,8 +234,10 @@ def run_segment(qw, scales, zeros, x_bytes, a, rbase, m0, kb, length):
                         zst[(sub * QUARTERS + hf) * BM + r] = zeros[rbase + r, g]
         for sub in range(in_stage):
             j = st * SPS + sub                      # slice of the segment
-            # dequantize warps: thread r builds its row's A slot
+            # dequantize warps: thread r builds its row's A slot (tensor-memory
+            # columns, or a K-major 128-byte-swizzled shared-memory tile)
             a_cols = np.full((BM, SLICE_COLS, 2), -1, np.int64)
+            a_tile = np.full(BM * 128, -1, np.int64)
             for r in range(BM):
                 raw = []
                 for i in range(WORDS // 4):
@@ -247,13 +257,22 @@ def run_segment(qw, scales, zeros, x_bytes, a, rbase, m0, kb, length):
                         for t in range(4):
                             col = 32 * hh + 4 * c + t
                             a_cols[r, col] = pairs[8 * hh + c, 2 * t:2 * t + 2]
+                        pos = r * 128 + 16 * ((4 * hh + c) ^ (r & 7))
+                        for e in range(8):
+                            a_tile[pos + 2 * e] = int(pairs[8 * hh + c, e]) & 0xFF
+                            a_tile[pos + 2 * e + 1] = int(pairs[8 * hh + c, e]) >> 8
             assert (a_cols >= 0).all()
+            if A_IN_SMEM:
+                assert (a_tile >= 0).all()
             # MMA: per token box, 4 K = 16 steps; the segment's first resets
             for b in range(XBOXES):
                 tile = tma_box_sw128(x_bytes, 2 * (kb + j * SLICE + 64 * b), m0, 2 * k, bn)
                 for kk in range(4):
-                    first = (4 * b + kk) * 8            # A columns of this K step
-                    a_bits = a_cols[:, first:first + 8, :].reshape(BM, 16)
+                    if A_IN_SMEM:                       # descriptor start + 32 (4b + kk)
+                        a_bits = sw128_read(a_tile, BM, 4 * b + kk)
+                    else:
+                        first = (4 * b + kk) * 8        # A columns of this K step
+                        a_bits = a_cols[:, first:first + 8, :].reshape(BM, 16)
                     b_bits = sw128_read(tile, bn, kk)
                     acc += bf16_value(a_bits) @ bf16_value(b_bits).T
     return acc
