@@ -50,16 +50,18 @@ def stream_handle(device: torch.device) -> int:
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """A uint8 device buffer of at least ``nbytes`` (cached per device).
+    """A uint8 device buffer of at least ``nbytes`` for calls on the current
+    stream (cached per device and stream).
 
-    One buffer serves every call on the device.  Calls issued on one stream
-    are ordered by it, which is how the engine runs (one stream, one lock);
-    calls overlapping on two streams would share the buffer.  A buffer that
-    is outgrown stays allocated, so graphs captured with it stay valid.
+    Calls on one stream are ordered by it, so they share one buffer; a call
+    on another stream gets that stream's own buffer, so calls overlapping on
+    two streams never share scratch.  A buffer that is outgrown stays
+    allocated, so graphs captured with it stay valid.
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, torch.cuda.current_stream(torch.device("cuda", idx)).cuda_stream)
     with _lock:
-        buf = _workspaces.get(idx)
+        buf = _workspaces.get(key)
         if buf is None or buf.numel() < nbytes:
             # Round up so slowly growing shapes do not reallocate every call.
             size = max(nbytes, 1 << 20)
@@ -67,7 +69,7 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
             if buf is not None:
                 _retired.append(buf)
             buf = torch.empty(size, dtype=torch.uint8, device=torch.device("cuda", idx))
-            _workspaces[idx] = buf
+            _workspaces[key] = buf
         return buf
 
 
