@@ -635,7 +635,9 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_acc_kernel(const QuantLinear
 // (kAInSmem = false keeps A in tensor memory instead - tcgen05.st by the
 // dequantize warps, MMAs with A from tensor memory - which ran 10 % faster at
 // 64 tokens but returned wrong sums for the first lane quarter (features 0-31
-// of a row block) of a few CTAs per call under load; it is not used.)
+// of a row block) of a few CTAs per call under load; it is not used.  The
+// tile is capped at 64 tokens: a 256-token tile with A in shared memory also
+// returned one wrong call in 13, cause not found.)
 //
 // Dequantization without conversions: OR-ing nibble j of a code word (bits
 // 4j..4j+3) into the float 2^23 gives 2^23 + q * 16^j exactly; one packed FMA
