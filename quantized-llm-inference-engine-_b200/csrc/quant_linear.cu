@@ -608,36 +608,32 @@ __global__ void __launch_bounds__(kThreads) wq_gemm_acc_kernel(const QuantLinear
 
 // ---- 2- and 4-bit codes on the 5th-generation tensor cores ---------------------
 //
-// A CTA owns 128 output features (MMA M; the accumulator's 128 tensor-memory
-// lanes) and bn tokens (MMA N: the batch rounded up to 16, at most 64; larger
-// batches take several token blocks) over a k range of whole 64-column
-// slices.  Each weight is dequantized once per CTA and token block into a
-// K-major, 128-byte-swizzled A tile in shared memory; the token rows are the
-// B operand beside it.  Warp roles:
+// A CTA owns 128 output features (the 128 lanes of tensor memory, MMA M) and bn
+// tokens (MMA N: the batch rounded up to 16, at most 256; larger batches take
+// several token blocks) over a k range of whole 64-column slices.  Each weight
+// is dequantized once per CTA and token block, straight into tensor memory as
+// the MMA's A operand; the token rows are the B operand in shared memory.
+// Warp roles:
 // * warps 0-11 dequantize in three sets of four: set h = w / 4 takes the
 //   slices s with s % 3 == h, warp w the 32 rows of lane quarter w % 4.
 //   Thread r turns its row's 64 codes of a slice into the reference's weights
-//   - (q - z) * s in float32, rounded once to the compute dtype - and writes
-//   the 128-byte row of the set's A tile (eight 16-byte stores at chunk
-//   c ^ (r % 8)), then fence.proxy.async for the MMA's reads.  Each set owns
-//   its A tile, so a tile's barriers are only ever waited on by the warps
-//   that saw all of its earlier phases;
+//   - (q - z) * s in float32, rounded once to the compute dtype - and stores
+//   the 32 pairs into a 32-column A slot in tensor memory (tcgen05.st).  Each
+//   set owns two slots, so a slot's barriers are only ever waited on by the
+//   warps that saw all of its earlier phases;
 // * warp 12 loads the codes: one TMA box of 128 rows x 128 bytes (256 columns,
 //   128-byte swizzle) per stage of a 4-stage ring, plus the stage's group
 //   scales (and zero points) by cp.async completing on the same mbarrier;
 // * warp 13 loads the token rows: one TMA box of bn rows x 64 columns per
 //   slice (K-major, 128-byte swizzle: the layout the MMA reads);
-// * warp 14 issues, from one elected thread, the four tcgen05.mma (K = 16)
-//   of each slice into the fp32 accumulator and commits them to the barriers
-//   that free the A tile and the token slot.
+// * warp 14 issues, from one elected thread, the four tcgen05.mma (K = 16, A
+//   from tensor memory) of each slice into the fp32 accumulator and commits
+//   them to the barriers that free the A slot and the token slot.
 // The dequantize warps then read the accumulator (tcgen05.ld, thread r =
 // feature r) and write the output, or the split's fp32 partial.
-// (kAInSmem = false keeps A in tensor memory instead - tcgen05.st by the
-// dequantize warps, MMAs with A from tensor memory - which ran 10 % faster at
-// 64 tokens but returned wrong sums for the first lane quarter (features 0-31
-// of a row block) of a few CTAs per call under load; it is not used.  The
-// tile is capped at 64 tokens: a 256-token tile with A in shared memory also
-// returned one wrong call in 13, cause not found.)
+// (kAInSmem = true instead writes A as K-major, 128-byte-swizzled tiles in
+// shared memory for MMAs with both operands there: the same results, 10-30 %
+// slower from the extra shared-memory traffic.)
 //
 // Dequantization without conversions: OR-ing nibble j of a code word (bits
 // 4j..4j+3) into the float 2^23 gives 2^23 + q * 16^j exactly; one packed FMA
@@ -659,8 +655,8 @@ constexpr int kQuarters = kSliceK / 32;           // group constants per row per
 constexpr int kStageK = 256;                      // k per codes stage (128 bytes of a row)
 constexpr int kSlicesPerStage = kStageK / kSliceK;
 constexpr int kCodeStages = 4;
-constexpr int kSlotsPerSet = 1;                   // A slots of a set, reused only by it
-constexpr bool kAInSmem = true;                   // A tiles in shared memory (else tensor memory)
+constexpr bool kAInSmem = false;                  // A tiles in shared memory (else tensor memory)
+constexpr int kSlotsPerSet = kAInSmem ? 1 : 2;    // A slots of a set, reused only by it
 constexpr int kMaxXSlots = 8;
 constexpr int kDqWarps = 12;
 constexpr int kSets = kDqWarps / 4;               // slices in flight in the dequantize warps
@@ -668,7 +664,7 @@ constexpr int kCodesWarp = kDqWarps;
 constexpr int kTokensWarp = kDqWarps + 1;
 constexpr int kMmaWarp = kDqWarps + 2;
 constexpr int kThreads = (kDqWarps + 3) * 32;
-constexpr int kMaxBN = 64;
+constexpr int kMaxBN = 256;
 constexpr int kATile = kBM * 128;                 // one A slot in shared memory: 16 KB
 constexpr int kCodeBytes = kBM * kStageK / 2;     // 16 KB per stage
 constexpr int kConstBytes = kSlicesPerStage * kQuarters * kBM * 4;   // [slice][32 cols][row]
@@ -684,7 +680,7 @@ constexpr int kBarBytes = 512;
 constexpr int kSmem = kOffBar + kBarBytes + 1024; // + alignment slack
 // tensor memory: the accumulator [kAccCol, kAccCol + bn), and the A ring in
 // columns [0, 256) when it is not in shared memory
-constexpr uint32_t kTmemCols = kAInSmem ? 64 : 512;
+constexpr uint32_t kTmemCols = kAInSmem ? 256 : 512;
 constexpr int kAccCol = kAInSmem ? 0 : 256;
 static_assert(kAccCol + kMaxBN <= (int)kTmemCols, "tensor-memory columns");
 static_assert(kSmem <= 227 * 1024, "shared memory");
@@ -1015,9 +1011,11 @@ __global__ void __launch_bounds__(tc05::kThreads, 1)
         sc[i] = sst[i * kBM];
         zp[i] = SYM ? 0.f : zst[i * kBM];
       }
-      __syncwarp();
-      // the warp's last slice of this stage: the stage's codes are in registers
-      if (sub + kSets >= in_stage && lane == 0) mbar_arrive(&bars->codes_empty[cs]);
+      // The warp's last slice of the stage releases it, but only once the math
+      // below has consumed the loaded words and constants: an arrival right
+      // after the loads let the codes warp refill the stage while shared-memory
+      // loads were still in flight, and those returned the next stage's bytes.
+      const bool last_in_stage = sub + kSets >= in_stage;
       const int as = a_slot(s);
       if (a_use(s) > 0 &&
           !wait(&bars->a_empty[as], (unsigned)((a_use(s) - 1) & 1), kErrWaitSlot)) {
@@ -1032,6 +1030,10 @@ __global__ void __launch_bounds__(tc05::kThreads, 1)
           const int q4 = (8 * hh + c) / 4;    // its 32-column quarter
           dequant8<DT, SYM>(words[8 * hh + c], kc, pack2f(sc[q4], sc[q4]),
                             pack2f(-zp[q4], -zp[q4]), out + 4 * c);
+        }
+        if (hh == kWords / 8 - 1 && last_in_stage) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->codes_empty[cs]);
         }
         if constexpr (kAInSmem) {
           // row r of the K-major A tile, 16-byte chunk c at c ^ (r % 8) (the

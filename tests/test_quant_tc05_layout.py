@@ -23,6 +23,12 @@ its constants read from the kernel source:
   it expects in its slot, no slot may be rewritten while an MMA still reads
   it, and no waiter may fall two phases behind a barrier.
 
+The model takes a warp's shared-memory reads as done when it reads; the
+kernel therefore releases a codes stage only after its math has consumed
+them (an arrival right after the loads let the codes warp refill the stage
+under loads still in flight).  ``test_release_follows_the_math`` checks that
+order in the source.
+
 This does not run the kernel.
 """
 
@@ -116,6 +122,18 @@ def test_host_boxes_match_the_kernel():
     x_box = [t.strip() for t in x_args.split(",")][-2:]
     assert codes_box == ["128", "tc05::kBM"], codes_box
     assert x_box[0] == "64" and "tokens" in x_box[1], x_box
+
+
+def test_release_follows_the_math():
+    """The dequantize warps arrive on codes_empty inside the store loop, after
+    the dequant8 calls that consume the stage's words and constants."""
+    text = open(SRC).read()
+    body = text[text.index("// ---- dequantize (warps 0 .. kDqWarps - 1) ----"):]
+    body = body[:body.index("// ---- epilogue")]
+    first_math = body.index("dequant8<DT, SYM>(")
+    release = body.index("mbar_arrive(&bars->codes_empty[cs])")
+    assert body.count("mbar_arrive(&bars->codes_empty[cs])") == 1
+    assert first_math < release
 
 
 # ---- dequantization arithmetic --------------------------------------------------
