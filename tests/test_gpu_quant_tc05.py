@@ -1,12 +1,12 @@
 """The tcgen05 quantized-linear kernel under the whole quantized-linear parity suite.
 
-``wq_gemm_tc05_kernel`` (token batches of 2/4-bit codes on the 5th-generation
-tensor cores: bit-exact fp32 dequantization into swizzled shared-memory tiles,
-TMEM accumulator) is selected by ``LLMOPT_B200_QUANT_TC05=1``, which the library
-reads once per process.  This test therefore reruns ``test_gpu_quant.py`` in a
-child process with the switch on, so every batch above the decode-batch size
-with a feature count divisible by 128 runs on that kernel against the
-reference's golden data and the oracle.
+``wq_gemm_tc05_kernel`` (2/4-bit codes on the 5th-generation tensor cores:
+bit-exact fp32 dequantization into tensor memory, TMEM accumulator) runs
+batches above 16 tokens by default, so ``test_gpu_quant.py`` already covers
+it there.  ``LLMOPT_B200_QUANT_TC05=1`` routes every batch to it, decode
+batches of 1-16 tokens included; the library reads the switch once per
+process, so this test reruns ``test_gpu_quant.py`` in a child process with the
+switch on, against the reference's golden data and the oracle.
 """
 
 from __future__ import annotations
