@@ -194,3 +194,29 @@ def test_decode_batch_path(cuda, kind, bits, symmetric, group):
         y = layer(to_dev(x, kind, cuda)).float().cpu().numpy()
         want = qo.quant_linear(x, kind, qw, s, z, bits, group, symmetric, (n, k), b)
         _assert_close(y, want, kind, f"m={m}")
+
+
+def test_tcgen05_repeated_calls_at_llama_down_projection(cuda):
+    """14336 -> 4096 at 256 tokens, the tcgen05 kernel's heaviest case (one
+    256-token tile, four k splits with fp32 partials), eight calls in a row.
+    A dequantize warp that released its codes stage before consuming the loaded
+    values let the stage be refilled under its loads and returned wrong sums
+    for a few row blocks in about half such calls; every call must match the
+    dense product over the layer's own dequantized weight (fp32 matmul)."""
+    pkg = load_package()
+    n, k, m = 4096, 14336, 256
+    g = torch.Generator(device=cuda)
+    g.manual_seed(3)
+    qweight = torch.randint(0, 256, (n, k // 2), generator=g, device=cuda,
+                            dtype=torch.int32).to(torch.uint8)
+    scales = torch.rand((n, k // 128), generator=g, device=cuda) * 0.01 + 1e-3
+    qt = SimpleNamespace(qweight=qweight, scales=scales, zeros=torch.zeros_like(scales), bits=4,
+                         group_size=128, symmetric=True)
+    lin = torch.nn.Linear(k, n, bias=False, device=cuda, dtype=torch.bfloat16)
+    layer = pkg.QuantLinear.from_float(lin, qt, compute_dtype=torch.bfloat16)
+    w = layer.dequantized_weight(cuda).float()
+    x = torch.randn((m, k), generator=g, device=cuda).to(torch.bfloat16)
+    want = (x.float() @ w.T).cpu().numpy()
+    for call in range(8):
+        got = layer(x).float().cpu().numpy()
+        _assert_close(got, want, "bf16", f"call {call}")
